@@ -1,0 +1,474 @@
+"""Benchmark: ChronoQuant compressed-cache decode step on B200.
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3] [--impl ours|reference]
+
+Workload (BASELINE config 2 by default): one attention layer, B=8 sequences,
+32 query / 8 KV heads, head_dim 128, a compressed context of T=16384 tokens
+per sequence in the Standard preset (stride_k 32, stride_v 8, INT4 residuals,
+dead zone 0).  One step = append one new token per sequence (the streaming
+encode kernel) + decode attention of a bf16 query against everything cached
+(split-KV kernel + combine).  Synthetic AR(1) K/V (fp16), seeded.
+
+value: compressed bytes the step must move (the cache's active bytes, the
+reference accounting, plus query/output and the encode's own bytes) divided
+by the device time per step (CUDA events, max over ranks).  The cache (~170 MB
+per GPU) exceeds the 126 MB L2, so no flush is needed between steps.
+e2e: the same metric through the public API with pinned host buffers: the new
+token's K/V and the query copied host->device and the output device->host
+inside every timed step.
+
+--gpus N (under torchrun): weak scaling, each rank owns a full config-2 shard
+(its own 8 sequences x 8 KV heads); no collective on the data path.
+--impl reference: the reference's CPU path (restated in oracle/, the
+reference itself needs MLX/Metal) timed on the host cores.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import sys
+import threading
+import time
+
+import numpy as np
+
+HERE = os.path.dirname(os.path.abspath(__file__))
+METRIC = "fused dequant-SDPA decode GB/s vs 8 TB/s HBM; decode tokens/s at 32k ctx"
+
+CONFIGS = {
+    2: dict(name="cfg2-standard-decode", B=8, Hq=32, Hkv=8, D=128, T=16384, stride_k=32, stride_v=8,
+            bits_k=4, bits_v=4, dz_k=0.0, dz_v=0.0, rho_k=0.95, rho_v=0.8),
+    3: dict(name="cfg3-ftv3-decode", B=16, Hq=32, Hkv=8, D=128, T=32768, stride_k=64, stride_v=32,
+            bits_k=4, bits_v=3, dz_k=0.0, dz_v=0.05, rho_k=0.97, rho_v=0.85),
+}
+
+
+def active_bytes(B, H, T, D, sk, sv):
+    """cache.py:274-287 active bytes for K and V at T tokens."""
+    W = (D + 7) // 8
+    tot = 0
+    for s in (sk, sv):
+        nkf = (T - 1) // s + 1 if T > 0 else 0
+        npf = T - nkf
+        tot += B * H * (nkf * D * 2 + npf * W * 4 + npf * 2)
+    return tot
+
+
+def step_bytes(cfg, T):
+    """Algorithmic bytes of one decode step at T cached tokens (after append):
+    attention reads the active cache + q, writes out; the encode reads the new
+    K/V token and its anchor, writes codes+scale (or the anchor)."""
+    B, H, Hq, D = cfg["B"], cfg["Hkv"], cfg["Hq"], cfg["D"]
+    attn = active_bytes(B, H, T, D, cfg["stride_k"], cfg["stride_v"]) + 2 * B * Hq * D * 2
+    t = T - 1
+    enc = 0
+    for s in (cfg["stride_k"], cfg["stride_v"]):
+        if t % s == 0:
+            enc += B * H * (D * 2 + D * 2)
+        else:
+            enc += B * H * (D * 2 + D * 2 + (D // 8) * 4 + 2)
+    return attn, enc
+
+
+def ar1_host(B, H, T, D, rho_k, rho_v, seed):
+    """Seeded AR(1) K (innovation 0.31, lognormal(0,0.5) channel scale, 4
+    outlier channels x8) and unit-variance AR(1) V, fp16 [B, H, T, D]."""
+    g = np.random.default_rng(seed)
+    chan = g.lognormal(0.0, 0.5, size=(B, H, D)).astype(np.float32)
+    for b in range(B):
+        for h in range(H):
+            chan[b, h, g.choice(D, 4, replace=False)] *= 8.0
+    K = np.empty((B, H, T, D), np.float16)
+    V = np.empty((B, H, T, D), np.float16)
+    k = (g.standard_normal((B, H, D)) * 0.31 / math.sqrt(1 - rho_k ** 2)).astype(np.float32)
+    v = g.standard_normal((B, H, D)).astype(np.float32)
+    sdv = math.sqrt(1 - rho_v ** 2)
+    for t0 in range(0, T, 512):
+        n = min(512, T - t0)
+        ek = (g.standard_normal((n, B, H, D)) * 0.31).astype(np.float32)
+        ev = (g.standard_normal((n, B, H, D)) * sdv).astype(np.float32)
+        for i in range(n):
+            if t0 + i:
+                k = rho_k * k + ek[i]
+                v = rho_v * v + ev[i]
+            K[:, :, t0 + i] = k * chan
+            V[:, :, t0 + i] = v
+    return K, V
+
+
+class ClockSampler:
+    """Samples SM clock and clock-event reasons through NVML during the timed region."""
+
+    REASONS = {0x1: "gpu_idle", 0x2: "applications_clocks_setting", 0x4: "sw_power_cap", 0x8: "hw_slowdown",
+               0x10: "sync_boost", 0x20: "sw_thermal_slowdown", 0x40: "hw_thermal_slowdown",
+               0x80: "hw_power_brake_slowdown", 0x100: "display_clock_setting"}
+
+    def __init__(self, index):
+        self.samples, self.reasons, self.max_mhz = [], set(), None
+        self._stop = threading.Event()
+        self.ok = False
+        try:
+            import pynvml
+            pynvml.nvmlInit()
+            self.nv = pynvml
+            self.h = pynvml.nvmlDeviceGetHandleByIndex(index)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(self.h, pynvml.NVML_CLOCK_SM)
+            self.ok = True
+        except Exception as e:  # NVML missing: report without clocks
+            self.err = str(e)
+
+    def _run(self):
+        while not self._stop.is_set():
+            try:
+                self.samples.append(self.nv.nvmlDeviceGetClockInfo(self.h, self.nv.NVML_CLOCK_SM))
+                r = self.nv.nvmlDeviceGetCurrentClocksEventReasons(self.h)
+                for bit, name in self.REASONS.items():
+                    if r & bit and name != "gpu_idle":
+                        self.reasons.add(name)
+            except Exception:
+                pass
+            time.sleep(0.05)
+
+    def __enter__(self):
+        if self.ok:
+            self.t = threading.Thread(target=self._run, daemon=True)
+            self.t.start()
+        return self
+
+    def __exit__(self, *a):
+        if self.ok:
+            self._stop.set()
+            self.t.join()
+
+    def summary(self):
+        if not self.ok:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "note": "NVML unavailable"}
+        return {"sm_mhz": statistics.median(self.samples) if self.samples else None, "sm_max_mhz": self.max_mhz,
+                "reasons": sorted(self.reasons), "samples": len(self.samples)}
+
+
+def load_peak():
+    p = os.path.join(HERE, "MEASURED_PEAKS.json")
+    try:
+        with open(p) as f:
+            return float(json.load(f)["hbm_gbs"]), "measured"
+    except Exception:
+        return 6650.0, "fallback"
+
+
+def load_traffic(cfg_name):
+    """dram bytes per decode launch from the committed ncu summary, scaled to
+    this workload's active bytes (traffic grows with the cache)."""
+    p = os.path.join(HERE, "profiles", "decode_traffic.json")
+    try:
+        with open(p) as f:
+            d = json.load(f)
+        e = d[cfg_name]
+        return e
+    except Exception:
+        return None
+
+
+# ----------------------------------------------------------------------------- GPU arm
+
+
+def run_ours(args, cfg):
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+
+    sys.path.insert(0, HERE)
+    from chronoquant_mlx_b200 import ChronoQuantCache, chronoquant_sdpa
+
+    B, H, Hq, D, T0 = cfg["B"], cfg["Hkv"], cfg["Hq"], cfg["D"], cfg["T"]
+    n_new = args.warmup + args.steps + 2  # tokens appended by warm-up, timed and e2e steps
+    K, V = ar1_host(B, H, T0 + 2 * n_new, D, cfg["rho_k"], cfg["rho_v"], seed=1000 + rank)
+    cache = ChronoQuantCache(stride_k=cfg["stride_k"], stride_v=cfg["stride_v"], delta_bits_k=cfg["bits_k"],
+                             delta_bits_v=cfg["bits_v"], dead_zone_k=cfg["dz_k"], dead_zone_v=cfg["dz_v"],
+                             max_tokens=T0 + 2 * n_new + 8)
+    # prefill (untimed) in chunks
+    for t in range(0, T0, 4096):
+        n = min(4096, T0 - t)
+        cache.update_and_fetch(torch.from_numpy(K[:, :, t:t + n]).to(device),
+                               torch.from_numpy(V[:, :, t:t + n]).to(device))
+    newK = torch.from_numpy(np.ascontiguousarray(K[:, :, T0:])).to(device)
+    newV = torch.from_numpy(np.ascontiguousarray(V[:, :, T0:])).to(device)
+    g = torch.Generator(device="cpu").manual_seed(7 + rank)
+    qs = (torch.randn((2 * n_new, B, Hq, 1, D), generator=g) / math.sqrt(D)).to(torch.bfloat16).to(device)
+    scale = 1.0 / math.sqrt(D)
+    torch.cuda.synchronize()
+
+    stream = torch.cuda.current_stream()
+    i_tok = [0]
+
+    def step():
+        j = i_tok[0]
+        cache.update_and_fetch(newK[:, :, j:j + 1], newV[:, :, j:j + 1])
+        out = chronoquant_sdpa(qs[j], None, None, cache, scale, mask=None)
+        i_tok[0] += 1
+        return out
+
+    for _ in range(args.warmup):
+        step()
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    T_start = cache.offset
+    ev = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(args.steps)]
+    with ClockSampler(local) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for k in range(args.steps):
+            j = i_tok[0]
+            cache.update_and_fetch(newK[:, :, j:j + 1], newV[:, :, j:j + 1])
+            ev[k][0].record(stream)
+            chronoquant_sdpa(qs[j], None, None, cache, scale, mask=None)
+            ev[k][1].record(stream)
+            i_tok[0] += 1
+        t1.record(stream)
+        torch.cuda.synchronize()
+    elapsed_ms = t0.elapsed_time(t1)
+    attn_ms = [a.elapsed_time(b) for a, b in ev]
+    if world > 1:
+        tt = torch.tensor([elapsed_ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(tt.item())
+        dist.barrier()
+    T_end = cache.offset
+    tot_bytes = 0
+    attn_bytes = []
+    for T in range(T_start + 1, T_end + 1):
+        a, e = step_bytes(cfg, T)
+        tot_bytes += a + e
+        attn_bytes.append(a)
+    ms_per_step = elapsed_ms / args.steps
+    value = world * tot_bytes / (elapsed_ms * 1e-3) / 1e9
+
+    # e2e through the public API with pinned host buffers
+    hk = torch.from_numpy(np.ascontiguousarray(K[:, :, T0 + n_new:])).pin_memory()
+    hv = torch.from_numpy(np.ascontiguousarray(V[:, :, T0 + n_new:])).pin_memory()
+    hq = qs[n_new:].cpu().pin_memory()
+    hout = torch.empty((B, Hq, 1, D), dtype=torch.bfloat16).pin_memory()
+    e_steps = min(args.steps, n_new - 2)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    Te0 = cache.offset
+    e0.record(stream)
+    for k in range(e_steps):
+        kd = hk[:, :, k:k + 1].to(device, non_blocking=True)
+        vd = hv[:, :, k:k + 1].to(device, non_blocking=True)
+        qd = hq[k].to(device, non_blocking=True)
+        cache.update_and_fetch(kd, vd)
+        out = chronoquant_sdpa(qd, None, None, cache, scale, mask=None)
+        hout.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([e_ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_ms = float(tt.item())
+    e_bytes = sum(sum(step_bytes(cfg, T)) for T in range(Te0 + 1, cache.offset + 1))
+    e2e_value = world * e_bytes / (e_ms * 1e-3) / 1e9
+    h2d = (hk[:, :, :1].numel() * 2 + hv[:, :, :1].numel() * 2 + hq[0].numel() * 2)
+    d2h = hout.numel() * 2
+
+    peak, peak_kind = load_peak()
+    mean_attn_ms = sum(attn_ms) / len(attn_ms)
+    mean_attn_bytes = sum(attn_bytes) / len(attn_bytes)
+    achieved = mean_attn_bytes / (mean_attn_ms * 1e-3) / 1e9
+    traffic = None
+    tr = load_traffic(cfg["name"])
+    if tr:
+        traffic = tr["dram_bytes_per_launch"] * (mean_attn_bytes / tr["algorithmic_bytes_per_launch"])
+
+    if rank == 0:
+        res = {
+            "metric": METRIC,
+            "value": round(value, 2),
+            "unit": "GB/s",
+            "n_gpus": world,
+            "steps": args.steps,
+            "warmup": args.warmup,
+            "ms_per_step": round(ms_per_step, 5),
+            "higher_is_better": True,
+            "scaling": "weak",
+            "vs_baseline": None,
+            "dtype": "int4-residual/f16-anchor, bf16 q, f32 accumulate",
+            "data": "synthetic AR(1) K/V (seeded), random bf16 queries",
+            "config": {"workload": cfg["name"], "batch": B, "q_heads": Hq, "kv_heads": H, "head_dim": D,
+                       "context_tokens_start": T_start, "stride_k": cfg["stride_k"], "stride_v": cfg["stride_v"],
+                       "bits_k": cfg["bits_k"], "bits_v": cfg["bits_v"], "dead_zone_v": cfg["dz_v"],
+                       "step": "append 1 token (encode) + decode attention",
+                       "l2": "cache active bytes %.0f MB per GPU > 126 MB L2; no flush" %
+                             (active_bytes(B, H, T_start, D, cfg["stride_k"], cfg["stride_v"]) / 1e6),
+                       "parallelism": f"dp{world} (batch/head shards, no collective)"},
+            "tokens_per_s": round(world * B * args.steps / (elapsed_ms * 1e-3), 1),
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
+                    "d2h_bytes_per_step": d2h, "steps": e_steps},
+            "roofline": {"bound": "hbm", "kernel": "decode attention (split-KV + combine)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "traffic": None if traffic is None else round(traffic),
+                         "algorithmic_bytes_per_launch": round(mean_attn_bytes),
+                         "launch_ms": round(mean_attn_ms, 5)},
+            "clocks": clk.summary(),
+            "gpu_launches": args.steps * 3,
+        }
+        if not args.no_cpu_baseline and world == 1:
+            res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
+        print(json.dumps(res))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+# ----------------------------------------------------------------------------- CPU reference arm
+
+
+def _ref_unit_setup(cfg, seed):
+    from oracle import cq_oracle as O
+    K, V = ar1_host(1, 1, cfg["T"] + 64, cfg["D"], cfg["rho_k"], cfg["rho_v"], seed)
+    c = O.OracleCache(stride_k=cfg["stride_k"], stride_v=cfg["stride_v"], delta_bits_k=cfg["bits_k"],
+                      delta_bits_v=cfg["bits_v"], dead_zone_k=cfg["dz_k"], dead_zone_v=cfg["dz_v"])
+    c.update_and_fetch(K[:, :, :cfg["T"]], V[:, :, :cfg["T"]])
+    return c, K, V
+
+
+def _ref_unit_step(c, K, V, q, scale):
+    """One decode step of one (sequence, kv-head) unit on the reference's CPU
+    path: encode the new token (cache.py:87-129), reconstruct the fp16 history
+    (cache.py:131-160) and the fallback GQA SDPA (attention.py:61-74)."""
+    from oracle import cq_oracle as O
+    t = c.offset
+    c.update_and_fetch(K[:, :, t:t + 1], V[:, :, t:t + 1])
+    fk, fv = c.reconstruct_history()
+    return O.fallback_sdpa(q, "f16", fk, fv, scale, None)
+
+
+def _ref_worker(args):
+    cfg, seed, n_steps = args
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    c, K, V = _ref_unit_setup(cfg, seed)
+    rep = cfg["Hq"] // cfg["Hkv"]
+    q = (np.random.default_rng(seed).standard_normal((1, rep, 1, cfg["D"])) / math.sqrt(cfg["D"])).astype(np.float16)
+    times = []
+    for _ in range(n_steps):
+        t0 = time.perf_counter()
+        _ref_unit_step(c, K, V, q, 1.0 / math.sqrt(cfg["D"]))
+        times.append(time.perf_counter() - t0)
+    return times, c.offset
+
+
+def cpu_baseline(cfg, budget_s=20.0):
+    """The oracle's reference-structured decode step on one (sequence,
+    kv-head) unit, single thread, GB/s of that unit's compressed bytes."""
+    sys.path.insert(0, HERE)
+    c, K, V = _ref_unit_setup(cfg, 0)
+    rep = cfg["Hq"] // cfg["Hkv"]
+    q = (np.random.default_rng(0).standard_normal((1, rep, 1, cfg["D"])) / math.sqrt(cfg["D"])).astype(np.float16)
+    scale = 1.0 / math.sqrt(cfg["D"])
+    _ref_unit_step(c, K, V, q, scale)
+    n, t_tot, byts = 0, 0.0, 0
+    while t_tot < budget_s and n < 60:
+        t0 = time.perf_counter()
+        _ref_unit_step(c, K, V, q, scale)
+        t_tot += time.perf_counter() - t0
+        unit_cfg = dict(cfg, B=1, Hkv=1, Hq=rep)
+        a, e = step_bytes(unit_cfg, c.offset)
+        byts += a + e
+        n += 1
+    return {"value": round(byts / t_tot / 1e9, 4), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"{n} decode steps of 1 of {cfg['B'] * cfg['Hkv']} (sequence, kv-head) units at "
+                      f"T={cfg['T']}: oracle encode + fp16 reconstruct + fallback SDPA (numpy, 1 thread)",
+            "seconds": round(t_tot, 2), "host_cpus": os.cpu_count()}
+
+
+def run_reference(args, cfg):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import multiprocessing as mp
+    cores = os.cpu_count() or 1
+    # time one unit-step to size each step's sample (whole run within ~2 minutes)
+    sys.path.insert(0, HERE)
+    c, K, V = _ref_unit_setup(cfg, 0)
+    rep = cfg["Hq"] // cfg["Hkv"]
+    q = (np.random.default_rng(0).standard_normal((1, rep, 1, cfg["D"])) / math.sqrt(cfg["D"])).astype(np.float16)
+    t0 = time.perf_counter()
+    _ref_unit_step(c, K, V, q, 1.0 / math.sqrt(cfg["D"]))
+    t_unit = time.perf_counter() - t0
+    total_steps = args.steps + args.warmup
+    units = cfg["B"] * cfg["Hkv"]
+    workers = min(cores, units)
+    # steps per worker so that the whole timed run stays near 90 s of wall time
+    per_worker_steps = max(1, min(total_steps, int(90.0 / max(t_unit, 1e-3))))
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(workers) as pool:
+        res = pool.map(_ref_worker, [(cfg, 100 + i, per_worker_steps) for i in range(workers)])
+    w = min(args.warmup, per_worker_steps - 1)
+    step_times = []
+    for times, _ in res:
+        step_times.extend(times[w:])
+    # each worker processes one unit per step in parallel; throughput = bytes of all units / wall per step
+    mean_t = sum(step_times) / len(step_times)
+    unit_cfg = dict(cfg, B=1, Hkv=1, Hq=rep)
+    a, e = step_bytes(unit_cfg, cfg["T"] + 1)
+    value = workers * (a + e) / mean_t / 1e9
+    ms_per_step_full = mean_t * 1e3 * units / workers
+    out = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step_full, 3),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "int4-residual/f16-anchor, fp16 fallback SDPA", "data": "synthetic AR(1) K/V (seeded)",
+        "config": {"workload": cfg["name"], "batch": cfg["B"], "q_heads": cfg["Hq"], "kv_heads": cfg["Hkv"],
+                   "head_dim": cfg["D"], "context_tokens_start": cfg["T"], "parallelism": f"{workers} host processes"},
+        "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": workers, "kind": "port",
+                         "sample": f"{per_worker_steps} decode steps on each of {workers} of {units} (sequence, "
+                                   f"kv-head) units at T={cfg['T']} (oracle restatement of the reference's "
+                                   "encode + fp16 reconstruct + fallback SDPA; MLX/Metal is unavailable here)"},
+        "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out))
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=200)
+    ap.add_argument("--warmup", type=int, default=10)
+    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--cpu-budget", type=float, default=15.0)
+    args = ap.parse_args()
+    if args.warmup < 3:
+        args.warmup = 3
+    cfg = CONFIGS[args.config]
+    if args.impl == "reference":
+        run_reference(args, cfg)
+    else:
+        run_ours(args, cfg)
+
+
+if __name__ == "__main__":
+    main()

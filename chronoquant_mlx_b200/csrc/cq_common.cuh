@@ -1,0 +1,166 @@
+// cq_common.cuh -- shared device/host helpers for libchronoquant_b200.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_fp16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include <string>
+
+#include "../../include/chronoquant_b200.h"
+
+namespace cq {
+
+// ---------------------------------------------------------------------------
+// error reporting (thread-local message behind cq_last_error)
+// ---------------------------------------------------------------------------
+int set_error(int code, const std::string &msg);
+int check_launch(const char *what);
+
+#define CQ_REQUIRE(cond, code, msg)                  \
+  do {                                               \
+    if (!(cond)) return ::cq::set_error((code), (msg)); \
+  } while (0)
+
+// ---------------------------------------------------------------------------
+// device view of a paged cache (copied by value into kernel parameters)
+// ---------------------------------------------------------------------------
+struct CompView {
+  const __half *kf;
+  const uint32_t *codes;
+  const __half *scales;
+  int stride;
+  int apg;    // anchors per page
+  int ppg;    // P-frames per page
+  int srow;   // scale row length
+  int order;  // CQ_ORDER_*
+  int bits;
+  float dead_zone;
+};
+
+struct CacheView {
+  int B, H, D, P, max_pages, n_pages;
+  const int32_t *block_table;  // nullptr -> page b*max_pages + logical page (reference layout)
+  CompView c[2];
+};
+
+inline CacheView make_view(const cq_paged_cache &c) {
+  CacheView v;
+  v.B = c.batch;
+  v.H = c.kv_heads;
+  v.D = c.head_dim;
+  v.P = c.page_tokens;
+  v.max_pages = c.max_pages;
+  v.n_pages = c.n_pages;
+  v.block_table = c.block_table;
+  const cq_component *src[2] = {&c.k, &c.v};
+  for (int i = 0; i < 2; ++i) {
+    v.c[i].kf = (const __half *)src[i]->keyframes;
+    v.c[i].codes = src[i]->codes;
+    v.c[i].scales = (const __half *)src[i]->scales;
+    v.c[i].stride = src[i]->stride;
+    v.c[i].apg = src[i]->anchors_per_page;
+    v.c[i].ppg = src[i]->pframes_per_page;
+    v.c[i].srow = src[i]->scale_row;
+    v.c[i].order = src[i]->code_order;
+    v.c[i].bits = src[i]->bits;
+    v.c[i].dead_zone = src[i]->dead_zone;
+  }
+  return v;
+}
+
+int validate_cache(const cq_paged_cache *c);
+
+__host__ __device__ inline int words_of(int D) { return (D + 7) >> 3; }
+
+// Position of dim d's nibble in a code row: word index and bit shift.
+// NATURAL: word d/8, nibble d%8 (kernels.py:15-19).  MMA (head_dim multiple of
+// 64): with g = d%8, k = d/8 (0..D/8-1), M4 = D/64: word g*M4 + k/8, nibble k%8.
+__host__ __device__ inline void nibble_pos(int d, int D, int order, int &word, int &shift) {
+  if (order == CQ_ORDER_MMA) {
+    int g = d & 7, k = d >> 3, m4 = D >> 6;
+    word = g * m4 + (k >> 3);
+    shift = (k & 7) << 2;
+  } else {
+    word = d >> 3;
+    shift = (d & 7) << 2;
+  }
+}
+
+// Physical page of logical page lp of sequence b.
+__device__ __forceinline__ int64_t page_of(const CacheView &cv, int b, int64_t lp) {
+  return cv.block_table ? (int64_t)cv.block_table[(int64_t)b * cv.max_pages + lp] : (int64_t)b * cv.max_pages + lp;
+}
+
+// Locations of token t (absolute) of (b, h) in component comp.
+struct TokLoc {
+  const __half *anchor;   // fp16 [D]
+  const uint32_t *codes;  // nullptr for an I-frame
+  float scale;
+};
+
+__device__ __forceinline__ TokLoc locate(const CacheView &cv, int comp, int b, int h, int64_t t) {
+  const CompView &c = cv.c[comp];
+  int64_t lp = t / cv.P;
+  int tl = (int)(t - lp * cv.P);
+  int64_t pg = page_of(cv, b, lp);
+  int a = tl / c.stride;
+  TokLoc L;
+  L.anchor = c.kf + ((pg * cv.H + h) * c.apg + a) * (int64_t)cv.D;
+  if (tl - a * c.stride == 0) {
+    L.codes = nullptr;
+    L.scale = 0.f;
+  } else {
+    int pf = tl - a - 1;
+    L.codes = c.codes + ((pg * cv.H + h) * c.ppg + pf) * (int64_t)words_of(cv.D);
+    L.scale = __half2float(c.scales[(pg * cv.H + h) * c.srow + pf]);
+  }
+  return L;
+}
+
+__device__ __forceinline__ int nibble_at(const uint32_t *row, int d, int D, int order) {
+  int w, s;
+  nibble_pos(d, D, order, w, s);
+  return (int)((row[w] >> s) & 0xFu);
+}
+
+// ---------------------------------------------------------------------------
+// scalar type helpers
+// ---------------------------------------------------------------------------
+__device__ __forceinline__ float load_as_float(const void *p, int64_t i, int dtype) {
+  if (dtype == CQ_F16) return __half2float(((const __half *)p)[i]);
+  if (dtype == CQ_BF16) return __bfloat162float(((const __nv_bfloat16 *)p)[i]);
+  return ((const float *)p)[i];
+}
+
+__device__ __forceinline__ void store_from_float(void *p, int64_t i, float v, int dtype) {
+  if (dtype == CQ_F16)
+    ((__half *)p)[i] = __float2half_rn(v);
+  else if (dtype == CQ_BF16)
+    ((__nv_bfloat16 *)p)[i] = __float2bfloat16_rn(v);
+  else
+    ((float *)p)[i] = v;
+}
+
+// Round a float to the arithmetic type of the token dtype (fp16 or bf16).
+__device__ __forceinline__ float round_dt(float x, int dtype) {
+  if (dtype == CQ_BF16) return __bfloat162float(__float2bfloat16_rn(x));
+  return __half2float(__float2half_rn(x));
+}
+
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  return v;
+}
+
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  return v;
+}
+
+inline int ceil_div(int64_t a, int64_t b) { return (int)((a + b - 1) / b); }
+
+}  // namespace cq

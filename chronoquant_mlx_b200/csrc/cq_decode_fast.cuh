@@ -1,0 +1,15 @@
+// cq_decode_fast.cuh -- the sm_100a split-KV decode kernel's host interface.
+#pragma once
+#include "cq_common.cuh"
+
+namespace cq {
+
+// True when the fast decode kernel handles this shape (q_len == 1,
+// head_dim 128, GQA group <= 8, pages of <= 256 tokens laid out for it).
+bool fast_decode_supported(const cq_paged_cache &c, int n_q_heads, int q_len);
+size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len, int splits_req);
+int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, const void *q, int q_dtype,
+                    int n_q_heads, int64_t q_sb, int64_t q_sh, float scale, void *out, int out_dtype,
+                    float *lse_out, void *ws, size_t ws_bytes, int splits_req, cudaStream_t st);
+
+}  // namespace cq

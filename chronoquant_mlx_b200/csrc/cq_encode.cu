@@ -1,0 +1,185 @@
+// cq_encode.cu -- streaming encode of new K/V tokens into the paged cache.
+//
+// One warp per (component, sequence, kv-head, token).  A token at position t
+// is an I-frame iff t % stride == 0 (cache.py:100-105): it is stored as fp16.
+// Otherwise it is a P-frame anchored on the I-frame at (t/stride)*stride
+// (cache.py:107-111); its residual against that anchor is quantised per token
+// (codec.py:23-65) and packed into INT4 lanes (kernels.py:34-54).  Every step
+// rounds to the token dtype exactly as the reference's fp16 (or bf16) MLX
+// arithmetic does: fp32 arithmetic on dtype values followed by one rounding is
+// the correctly rounded dtype result for + - * /.
+#include "cq_common.cuh"
+
+namespace cq {
+
+constexpr int kEncodeWarps = 8;
+constexpr int kMaxDimsPerLane = 8;  // head_dim <= 256
+
+struct EncodeArgs {
+  CacheView cv;
+  const void *x[2];
+  int64_t sb[2], sh[2], ss[2];
+  int64_t t0;
+  int S;
+};
+
+// Quantise one residual value (codec.py:48-54).  `q` is the dtype-rounded
+// quotient delta/scale_safe.
+__device__ __forceinline__ int quantise_code(float q, float hl, bool zero_scale) {
+  if (zero_scale || isnan(q)) return 0;  // NaN (0/0) is undefined in the reference; defined as 0
+  float r = rintf(q);                    // mx.round: half to even
+  r = fminf(fmaxf(r, -hl), hl - 1.f);
+  return (int)r;
+}
+
+template <int DTYPE>
+__global__ void __launch_bounds__(kEncodeWarps * 32) append_kernel(EncodeArgs A) {
+  __shared__ uint32_t s_words[kEncodeWarps][32];
+  const CacheView &cv = A.cv;
+  const int lane = threadIdx.x & 31;
+  const int wib = threadIdx.x >> 5;
+  const int64_t warp = (int64_t)blockIdx.x * kEncodeWarps + wib;
+  const int64_t total = 2LL * cv.B * cv.H * A.S;
+  if (warp >= total) return;
+  const int s = (int)(warp % A.S);
+  int64_t r = warp / A.S;
+  const int h = (int)(r % cv.H);
+  r /= cv.H;
+  const int b = (int)(r % cv.B);
+  const int comp = (int)(r / cv.B);
+  const CompView &c = cv.c[comp];
+  const int D = cv.D;
+
+  const int64_t t = A.t0 + s;
+  const int64_t lp = t / cv.P;
+  const int tl = (int)(t - lp * cv.P);
+  const int64_t pg = page_of(cv, b, lp);
+  const int a = tl / c.stride;
+  const int phase = tl - a * c.stride;
+  const int64_t xbase = b * A.sb[comp] + h * A.sh[comp];
+
+  float xv[kMaxDimsPerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxDimsPerLane; ++i) {
+    int d = lane + 32 * i;
+    xv[i] = (d < D) ? load_as_float(A.x[comp], xbase + s * A.ss[comp] + d, DTYPE) : 0.f;
+  }
+
+  __half *kf_row = const_cast<__half *>(c.kf) + ((pg * cv.H + h) * c.apg + a) * (int64_t)D;
+  if (phase == 0) {  // I-frame: token.astype(float16) (cache.py:103-105)
+#pragma unroll
+    for (int i = 0; i < kMaxDimsPerLane; ++i) {
+      int d = lane + 32 * i;
+      if (d < D) kf_row[d] = __float2half_rn(xv[i]);
+    }
+    return;
+  }
+
+  // Anchor token: in this call (read and convert the input, exactly as the
+  // stored keyframe) or already in the cache (written by an earlier launch).
+  const int64_t ta = t - phase;
+  float av[kMaxDimsPerLane];
+#pragma unroll
+  for (int i = 0; i < kMaxDimsPerLane; ++i) {
+    int d = lane + 32 * i;
+    float v = 0.f;
+    if (d < D) {
+      if (ta >= A.t0)
+        v = __half2float(__float2half_rn(load_as_float(A.x[comp], xbase + (ta - A.t0) * A.ss[comp] + d, DTYPE)));
+      else
+        v = __half2float(kf_row[d]);
+    }
+    av[i] = v;
+  }
+
+  // delta = token - anchor.astype(token.dtype), in the token dtype (cache.py:113)
+  float dv[kMaxDimsPerLane];
+  float amax = 0.f;
+#pragma unroll
+  for (int i = 0; i < kMaxDimsPerLane; ++i) {
+    float an = (DTYPE == CQ_BF16) ? round_dt(av[i], CQ_BF16) : av[i];
+    dv[i] = round_dt(xv[i] - an, DTYPE);
+    amax = fmaxf(amax, fabsf(dv[i]));
+  }
+  amax = warp_max(amax);
+
+  const int hl_i = (1 << c.bits) / 2;
+  const float hl = (float)hl_i;
+  const float hlm1 = (float)(hl_i - 1);
+  const float tiny = round_dt(1e-10f, DTYPE);  // 0 in fp16
+  float scale = round_dt(__fdiv_rn(amax, hlm1), DTYPE);
+  if (c.dead_zone > 0.f) {  // codec.py:36-45
+    const float ratio = round_dt(c.dead_zone, DTYPE);
+    const float thr = round_dt(amax * ratio, DTYPE);
+    float amax_c = 0.f;
+#pragma unroll
+    for (int i = 0; i < kMaxDimsPerLane; ++i) {
+      if (fabsf(dv[i]) < thr) dv[i] = 0.f;
+      amax_c = fmaxf(amax_c, fabsf(dv[i]));
+    }
+    amax_c = warp_max(amax_c);
+    const float amax_safe = (amax_c < tiny) ? amax : amax_c;
+    scale = round_dt(__fdiv_rn(amax_safe, hlm1), DTYPE);
+  }
+  const bool zero_scale = scale < tiny;
+  const float scale_safe = zero_scale ? 1.f : scale;
+
+  uint32_t *sw = s_words[wib];
+  const int W = words_of(D);
+  sw[lane] = 0u;
+  __syncwarp();
+#pragma unroll
+  for (int i = 0; i < kMaxDimsPerLane; ++i) {
+    int d = lane + 32 * i;
+    if (d < D) {
+      float q = round_dt(__fdiv_rn(dv[i], scale_safe), DTYPE);
+      int code = quantise_code(q, hl, zero_scale);
+      uint32_t nib = (uint32_t)min(max(code + 8, 0), 15);  // kernels.py:40
+      int w, sh;
+      nibble_pos(d, D, c.order, w, sh);
+      atomicOr(&sw[w], nib << sh);
+    }
+  }
+  __syncwarp();
+  const int pf = tl - a - 1;
+  uint32_t *code_row = const_cast<uint32_t *>(c.codes) + ((pg * cv.H + h) * c.ppg + pf) * (int64_t)W;
+  if (lane < W) code_row[lane] = sw[lane];
+  if (lane == 0) {
+    // scale.astype(float16) (codec.py:65, cache.py:116)
+    const_cast<__half *>(c.scales)[(pg * cv.H + h) * c.srow + pf] = __float2half_rn(scale);
+  }
+}
+
+}  // namespace cq
+
+using namespace cq;
+
+extern "C" int cq_append(const cq_paged_cache *cache, const void *keys, int64_t k_sb, int64_t k_sh, int64_t k_ss,
+                         const void *values, int64_t v_sb, int64_t v_sh, int64_t v_ss, int dtype, int64_t t0,
+                         int32_t S, void *stream) {
+  int r = validate_cache(cache);
+  if (r) return r;
+  CQ_REQUIRE(keys && values, CQ_ERR_INVALID, "cq_append: keys/values null");
+  CQ_REQUIRE(dtype == CQ_F16 || dtype == CQ_BF16, CQ_ERR_UNSUPPORTED, "cq_append: dtype must be f16 or bf16");
+  CQ_REQUIRE(S >= 0 && t0 >= 0, CQ_ERR_INVALID, "cq_append: negative S or t0");
+  if (S == 0) return CQ_OK;
+  int64_t last_page = (t0 + S - 1) / cache->page_tokens;
+  CQ_REQUIRE(last_page < cache->max_pages, CQ_ERR_INVALID, "cq_append: tokens beyond max_pages*page_tokens");
+  EncodeArgs A;
+  A.cv = make_view(*cache);
+  A.x[0] = keys;
+  A.x[1] = values;
+  A.sb[0] = k_sb; A.sh[0] = k_sh; A.ss[0] = k_ss;
+  A.sb[1] = v_sb; A.sh[1] = v_sh; A.ss[1] = v_ss;
+  A.t0 = t0;
+  A.S = S;
+  int64_t warps = 2LL * cache->batch * cache->kv_heads * S;
+  int64_t blocks = (warps + kEncodeWarps - 1) / kEncodeWarps;
+  CQ_REQUIRE(blocks < (1LL << 31), CQ_ERR_INVALID, "cq_append: too many tokens in one call");
+  cudaStream_t st = (cudaStream_t)stream;
+  if (dtype == CQ_F16)
+    append_kernel<CQ_F16><<<(unsigned)blocks, kEncodeWarps * 32, 0, st>>>(A);
+  else
+    append_kernel<CQ_BF16><<<(unsigned)blocks, kEncodeWarps * 32, 0, st>>>(A);
+  return check_launch("cq_append");
+}

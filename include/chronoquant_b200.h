@@ -1,0 +1,182 @@
+/*
+ * chronoquant_b200.h -- C ABI of libchronoquant_b200.so (sm_100a).
+ *
+ * The drop-in boundary for ChronoQuant's KV-cache codec and fused
+ * dequant-attention path.  Every entry point:
+ *   - takes device pointers the caller allocated, plain sizes and a CUDA
+ *     stream (cudaStream_t passed as void*; NULL = legacy default stream);
+ *   - is stream-ordered, stateless and safe to call from any host thread;
+ *   - returns CQ_OK (0) or a negative status, never aborts or throws;
+ *     cq_last_error() returns the calling thread's last message.
+ *
+ * Reference interfaces replaced (gauravsaini/chronoquant_mlx):
+ *   codec.py:23-65   ChronoQuantCodecMLX.quantize_delta   -> cq_quantize_delta
+ *   codec.py:67-73   ChronoQuantCodecMLX.dequantize_delta -> cq_dequantize_delta
+ *   kernels.py:34-54 pack_int4_codes (+ Metal kernels.py:9-29) -> cq_pack_int4
+ *   kernels.py:57-61 unpack_int4_codes                   -> cq_unpack_int4
+ *   cache.py:87-129  ChronoQuantCache._append_component   -> cq_append
+ *   cache.py:131-160 _reconstruct_component               -> cq_reconstruct
+ *   cache.py:220-255 state getter / setter                -> cq_export_state / cq_import_state
+ *   kernels.py:248-279 chronoquant_sdpa_kernel (+ Metal kernels.py:79-228)
+ *                                                          -> cq_sdpa_reference_layout
+ *   attention.py:23-74 chronoquant_sdpa (fused + fallback) -> cq_attention
+ *   (no reference counterpart) seq-split partial merge     -> cq_lse_merge
+ */
+#ifndef CHRONOQUANT_B200_H
+#define CHRONOQUANT_B200_H
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+#define CQ_ABI_VERSION 1
+
+/* status codes */
+#define CQ_OK 0
+#define CQ_ERR_INVALID (-1)     /* bad argument (null pointer, size, stride) */
+#define CQ_ERR_UNSUPPORTED (-2) /* valid but not supported (e.g. head_dim) */
+#define CQ_ERR_CUDA (-3)        /* a CUDA runtime call failed */
+#define CQ_ERR_WORKSPACE (-4)   /* workspace too small */
+
+/* element types */
+#define CQ_F16 0
+#define CQ_BF16 1
+#define CQ_F32 2
+
+/* V-code nibble orders (the cache's own storage; the reference layout is order 0) */
+#define CQ_ORDER_NATURAL 0 /* word w holds dims 8w..8w+7, LSB first (kernels.py:15-19) */
+#define CQ_ORDER_MMA 1     /* word 2g+q, nibble j holds dim g + 64q + 8j (head_dim 128) */
+
+/*
+ * One compressed component (K or V) of a paged cache.  Per page and head:
+ *   keyframes fp16  [anchors_per_page][head_dim]
+ *   codes     u32   [pframes_per_page][head_dim/8]
+ *   scales    fp16  [scale_row]            (scale_row >= pframes_per_page, multiple of 8)
+ * Arrays are [n_pages][kv_heads][...] contiguous.  Token t of sequence b lives
+ * in page block_table[b*max_pages + t/page_tokens] at tl = t % page_tokens;
+ * it is an I-frame iff tl % stride == 0 (anchor slot tl/stride), else a
+ * P-frame in slot tl - tl/stride - 1 anchored on slot tl/stride.
+ */
+typedef struct cq_component {
+  int32_t stride;           /* I-frame period (cache.py:100) */
+  int32_t bits;             /* residual bits 2..8, stored in INT4 lanes */
+  float dead_zone;          /* dead-zone ratio (codec.py:36-45) */
+  int32_t anchors_per_page; /* page_tokens / stride */
+  int32_t pframes_per_page; /* page_tokens - anchors_per_page */
+  int32_t scale_row;        /* padded scales per (page, head) */
+  int32_t code_order;       /* CQ_ORDER_* */
+  int32_t _pad;
+  void *keyframes;          /* fp16 */
+  uint32_t *codes;
+  void *scales;             /* fp16 */
+} cq_component;
+
+typedef struct cq_paged_cache {
+  int32_t batch;
+  int32_t kv_heads;
+  int32_t head_dim;    /* multiple of 8, <= 256 */
+  int32_t page_tokens; /* multiple of lcm(stride_k, stride_v) */
+  int32_t max_pages;   /* row length of block_table */
+  int32_t n_pages;     /* pool capacity in pages */
+  const int32_t *block_table; /* device int32 [batch][max_pages] */
+  cq_component k;
+  cq_component v;
+} cq_paged_cache;
+
+int cq_abi_version(void);
+const char *cq_last_error(void);
+
+/* Encode S new tokens at absolute positions t0..t0+S-1 for K and V in one
+ * launch (cache.py:87-129, codec.py:23-65).  keys/values: [batch][kv_heads]
+ * [S][head_dim] with element strides (sb, sh, ss) and unit dim stride, of
+ * type dtype (CQ_F16 or CQ_BF16).  Pages covering t0..t0+S-1 must be mapped
+ * in block_table.  Anchors of P-frames that precede t0 are read from the
+ * cache. */
+int cq_append(const cq_paged_cache *cache, const void *keys, int64_t k_sb, int64_t k_sh, int64_t k_ss,
+              const void *values, int64_t v_sb, int64_t v_sh, int64_t v_ss, int dtype, int64_t t0,
+              int32_t S, void *stream);
+
+/* Attention of q_len queries per sequence against the first T cached tokens
+ * (attention.py:23-74).  q: [batch][n_q_heads][q_len][head_dim] with strides
+ * (q_sb, q_sh, q_sq), dtype CQ_F16/CQ_BF16; the scores use q*scale rounded
+ * to the query dtype (attention.py:46/65).  causal != 0 applies the causal
+ * mask anchored at the end (attention.py:8-20; no effect when q_len == 1);
+ * causal == 0 lets every query see all T keys (mask=None).  out: [batch][n_q_heads][q_len]
+ * [head_dim] contiguous, out_dtype CQ_F16/CQ_BF16/CQ_F32.  workspace: device
+ * memory of at least cq_attention_workspace() bytes (split-KV partials);
+ * num_splits <= 0 picks a split count.  lse_out (optional, may be NULL):
+ * fp32 [batch][n_q_heads][q_len] log-sum-exp of the scaled scores (natural
+ * log), for merging sequence shards. */
+int cq_attention(const cq_paged_cache *cache, int64_t T, const void *q, int q_dtype, int32_t n_q_heads,
+                 int32_t q_len, int32_t causal, int64_t q_sb, int64_t q_sh, int64_t q_sq, float scale, void *out,
+                 int out_dtype, float *lse_out, void *workspace, size_t workspace_bytes, int32_t num_splits,
+                 void *stream);
+int cq_attention_workspace(const cq_paged_cache *cache, int64_t T, int32_t n_q_heads, int32_t q_len,
+                           int32_t num_splits, size_t *bytes);
+
+/* cq_attention with an explicit mask instead of the implicit causal rule
+ * (attention.py:8-20 for array masks): mask_kind 1 = boolean uint8 (nonzero
+ * keeps the key; masked scores become finfo(score dtype).min as
+ * attention.py:19 does), 2 = additive of mask_dtype.  Element (b, h, i, t) is
+ * at b*m_sb + h*m_sh + i*m_sq + t*m_st (a 0 stride broadcasts). */
+int cq_attention_masked(const cq_paged_cache *cache, int64_t T, const void *q, int q_dtype, int32_t n_q_heads,
+                        int32_t q_len, int64_t q_sb, int64_t q_sh, int64_t q_sq, float scale, const void *mask,
+                        int mask_kind, int mask_dtype, int64_t m_sb, int64_t m_sh, int64_t m_sq, int64_t m_st,
+                        void *out, int out_dtype, void *workspace, size_t workspace_bytes, int32_t num_splits,
+                        void *stream);
+
+/* Merge attention outputs of the same rows computed over disjoint key shards
+ * (sequence split): lse fp32 [n_parts][rows] (natural-log log-sum-exp of each
+ * shard's scaled scores, -inf for an empty shard), o fp32 [n_parts][rows][dim]
+ * (each shard's normalised output).  out[r] = sum_i exp(lse_i - L) o_i with
+ * L = logsumexp_i lse_i; out: [rows][dim] in out_dtype. */
+int cq_lse_merge(const float *lse, const float *o, int32_t n_parts, int64_t rows, int32_t dim, void *out,
+                 int out_dtype, void *stream);
+
+/* Decoded fp16 history of one component (0=K, 1=V) for tokens 0..T-1:
+ * out [batch][kv_heads][T][head_dim].  mode 0 rounds like the reference's
+ * fallback (fp16(code*scale), then fp16(anchor + that), cache.py:141-156);
+ * mode 1 rounds the exact anchor + code*scale once. */
+int cq_reconstruct(const cq_paged_cache *cache, int component, int64_t T, void *out, int mode, void *stream);
+
+/* Reference-layout state (cache.py:220-234) of one component for tokens
+ * 0..T-1: keyframes fp16 [batch][kv_heads][n_kf][head_dim], packed u32
+ * [batch][kv_heads][n_pf][head_dim/8] (natural nibble order), scales fp16
+ * [batch][kv_heads][n_pf].  cq_import_state is the inverse (cache.py:236-255). */
+int cq_export_state(const cq_paged_cache *cache, int component, int64_t T, void *keyframes,
+                    uint32_t *packed, void *scales, void *stream);
+int cq_import_state(const cq_paged_cache *cache, int component, int64_t T, const void *keyframes,
+                    const uint32_t *packed, const void *scales, void *stream);
+
+/* Codec on a flat row set (codec.py:23-73).  delta: rows x dim of dtype;
+ * codes int8 rows x dim; scales fp16 rows. */
+int cq_quantize_delta(const void *delta, int dtype, int64_t rows, int32_t dim, int32_t bits, float dead_zone,
+                      int8_t *codes, void *scales, void *stream);
+int cq_dequantize_delta(const int8_t *codes, const void *scales, int64_t rows, int32_t dim, void *out,
+                        void *stream);
+
+/* INT4 packing in the reference layout (kernels.py:34-61): rows x dim int8
+ * <-> rows x ceil(dim/8) uint32. */
+int cq_pack_int4(const int8_t *codes, int64_t rows, int32_t dim, uint32_t *packed, void *stream);
+int cq_unpack_int4(const uint32_t *packed, int64_t rows, int32_t dim, int8_t *codes, void *stream);
+
+/* The fused decode kernel's reference-layout entry (kernels.py:248-279):
+ * q fp32 [n_q_heads][dim] (already scaled), keyframes [kv_heads][n_kf][dim]
+ * fp16, packed [kv_heads][n_pf][ceil(dim/8)] u32, scales [kv_heads][n_pf]
+ * fp16, per K and V; out fp32 [n_q_heads][dim].  n_kf/n_pf are the first
+ * dimension extents of the views (cache.py:162-190). */
+int cq_sdpa_reference_layout(const float *q, int32_t n_q_heads, int32_t dim, const void *kf_k, int32_t n_kf_k,
+                             const uint32_t *packed_k, const void *scales_k, int32_t n_pf_k, const void *kf_v,
+                             int32_t n_kf_v, const uint32_t *packed_v, const void *scales_v, int32_t n_pf_v,
+                             int32_t n_kv_heads, int64_t seq_len, int32_t stride_k, int32_t stride_v,
+                             float *out, void *workspace, size_t workspace_bytes, void *stream);
+int cq_sdpa_reference_layout_workspace(int32_t n_q_heads, int32_t dim, int64_t seq_len, size_t *bytes);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* CHRONOQUANT_B200_H */
