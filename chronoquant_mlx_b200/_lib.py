@@ -24,7 +24,7 @@ CQ_F16, CQ_BF16, CQ_F32 = 0, 1, 2
 CQ_ORDER_NATURAL, CQ_ORDER_MMA = 0, 1
 
 EXPORTED = [
-    "cq_abi_version", "cq_last_error", "cq_append", "cq_attention", "cq_attention_workspace",
+    "cq_abi_version", "cq_last_error", "cq_device_error", "cq_append", "cq_attention", "cq_attention_workspace",
     "cq_attention_masked", "cq_lse_merge", "cq_reconstruct", "cq_export_state", "cq_import_state", "cq_quantize_delta",
     "cq_dequantize_delta", "cq_pack_int4", "cq_unpack_int4", "cq_sdpa_reference_layout",
     "cq_sdpa_reference_layout_workspace",
@@ -64,6 +64,7 @@ def _declare(lib):
     lib.cq_last_error.restype = ctypes.c_char_p
     lib.cq_last_error.argtypes = []
     sig = {
+        "cq_device_error": [ctypes.POINTER(ctypes.c_int), ctypes.c_int],
         "cq_append": [C, P, I64, I64, I64, P, I64, I64, I64, ctypes.c_int, I64, I32, P],
         "cq_attention": [C, I64, P, ctypes.c_int, I32, I32, I32, I64, I64, I64, F, P, ctypes.c_int, P, P, SZ, I32,
                          P],

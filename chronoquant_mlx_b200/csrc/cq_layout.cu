@@ -24,8 +24,8 @@ __global__ void reconstruct_kernel(CacheView cv, int comp, int64_t T, __half *ou
     if (L.codes) {
       int code = nibble_at(L.codes, d, cv.D, c.order) - 8;
       __half s = __float2half_rn(L.scale);
-      if (mode == 0)  // fp16(code) * scale in fp16, then anchor + that in fp16
-        v = __hadd(a, __hmul(__int2half_rn(code), s));
+      if (mode == 0)  // fp16(code) * scale in fp16, then anchor + that in fp16 (two roundings, no FMA)
+        v = __hadd_rn(a, __hmul_rn(__int2half_rn(code), s));
       else
         v = __float2half_rn(fmaf((float)code, L.scale, __half2float(a)));
     }
@@ -152,7 +152,7 @@ __global__ void quantize_kernel(const void *delta, int dtype, int64_t rows, int 
 __global__ void dequantize_kernel(const int8_t *codes, const __half *scales, int64_t rows, int dim, __half *out) {
   const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= rows * dim) return;
-  out[i] = __hmul(__int2half_rn((int)codes[i]), scales[i / dim]);
+  out[i] = __hmul_rn(__int2half_rn((int)codes[i]), scales[i / dim]);
 }
 
 __global__ void pack_kernel(const int8_t *codes, int64_t rows, int dim, uint32_t *packed) {

@@ -1,0 +1,136 @@
+// cq_ptx.cuh -- inline-PTX wrappers: mbarriers, bulk-async copies (the TMA
+// engine's 1-D form), warp-level tensor-core MMA, ldmatrix/movmatrix and the
+// bit tricks that turn packed nibbles into fp16 pairs.
+#pragma once
+
+#include <cuda_fp16.h>
+#include <stdint.h>
+
+namespace cq {
+namespace ptx {
+
+__device__ __forceinline__ uint32_t smem_u32(const void *p) {
+  return (uint32_t)__cvta_generic_to_shared(p);
+}
+
+// ---------------------------------------------------------------- mbarrier
+__device__ __forceinline__ void mbar_init(uint64_t *bar, uint32_t count) {
+  asm volatile("mbarrier.init.shared::cta.b64 [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
+
+__device__ __forceinline__ void fence_mbar_init() {
+  asm volatile("fence.mbarrier_init.release.cluster;" ::: "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
+  asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
+               : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after `budget` clock cycles and returns false.
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, long long budget) {
+  if (mbar_try_wait(bar, parity)) return true;
+  const long long t0 = clock64();
+  while (!mbar_try_wait(bar, parity)) {
+    if (clock64() - t0 > budget) return false;
+  }
+  return true;
+}
+
+// 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
+// Addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes, uint64_t *bar) {
+  asm volatile(
+      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+          smem_u32(dst_smem)),
+      "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void named_barrier_sync(int id, int threads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(threads) : "memory");
+}
+
+// ---------------------------------------------------------------- tensor-core fragments
+// D(16x8 f32) += A(16x16 f16, row) * B(16x8 f16, col)
+__device__ __forceinline__ void mma_f16_16816(float (&c)[4], uint32_t a0, uint32_t a1, uint32_t a2, uint32_t a3,
+                                              uint32_t b0, uint32_t b1) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
+      "{%0,%1,%2,%3};"
+      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1));
+}
+
+__device__ __forceinline__ void ldmatrix_x4(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3,
+                                            uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ void ldmatrix_x4_trans(uint32_t &r0, uint32_t &r1, uint32_t &r2, uint32_t &r3,
+                                                  uint32_t addr) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+
+__device__ __forceinline__ uint32_t movmatrix_trans(uint32_t a) {
+  uint32_t d;
+  asm volatile("movmatrix.sync.aligned.m8n8.trans.b16 %0, %1;" : "=r"(d) : "r"(a));
+  return d;
+}
+
+// ---------------------------------------------------------------- nibble -> fp16
+// (a & b) | c in one LOP3
+__device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t c) {
+  uint32_t d;
+  asm("lop3.b32 %0, %1, %2, %3, 0xea;" : "=r"(d) : "r"(a), "r"(b), "r"(c));
+  return d;
+}
+
+__device__ __forceinline__ __half2 u2h2(uint32_t x) { return *reinterpret_cast<__half2 *>(&x); }
+__device__ __forceinline__ uint32_t h22u(__half2 x) { return *reinterpret_cast<uint32_t *>(&x); }
+
+// The 16-bit halves of x hold nibble lanes; OR-ing a nibble n into the
+// mantissa of fp16 1024.0 (0x6400) gives exactly 1024 + n (or 1024 + 16n for
+// the high nibble of a byte).  Subtracting the bias leaves the signed code
+// n - 8 exactly.  Returns codes of nibbles {0,1,2,3} of each 16-bit half:
+//   out[0] = (nib0(lo), nib0(hi)), out[1] = nib1, out[2] = nib2, out[3] = nib3.
+__device__ __forceinline__ void nibbles_to_half2(uint32_t x, uint32_t (&out)[4]) {
+  const uint32_t MAGIC = 0x64006400u;
+  const __half2 BIAS_LO = u2h2(0x64086408u);   // 1032
+  const __half2 SCALE_HI = u2h2(0x2c002c00u);  // 1/16
+  const __half2 BIAS_HI = u2h2(0xd480d480u);   // -72
+  uint32_t lo0 = lop3_and_or(x, 0x000f000fu, MAGIC);
+  uint32_t hi0 = lop3_and_or(x, 0x00f000f0u, MAGIC);
+  uint32_t x8 = x >> 8;
+  uint32_t lo1 = lop3_and_or(x8, 0x000f000fu, MAGIC);
+  uint32_t hi1 = lop3_and_or(x8, 0x00f000f0u, MAGIC);
+  out[0] = h22u(__hsub2(u2h2(lo0), BIAS_LO));
+  out[1] = h22u(__hfma2(u2h2(hi0), SCALE_HI, BIAS_HI));
+  out[2] = h22u(__hsub2(u2h2(lo1), BIAS_LO));
+  out[3] = h22u(__hfma2(u2h2(hi1), SCALE_HI, BIAS_HI));
+}
+
+__device__ __forceinline__ uint32_t pack_half2(float lo, float hi) { return h22u(__floats2half2_rn(lo, hi)); }
+
+}  // namespace ptx
+}  // namespace cq

@@ -89,6 +89,12 @@ typedef struct cq_paged_cache {
 int cq_abi_version(void);
 const char *cq_last_error(void);
 
+/* Device-side error word: set (non-zero) when a bounded wait inside a kernel
+ * gave up (1 = a stage never filled, 2 = a stage was never released); the
+ * kernel then returned early instead of hanging.  Synchronises the device;
+ * clear != 0 resets the word. */
+int cq_device_error(int *code, int clear);
+
 /* Encode S new tokens at absolute positions t0..t0+S-1 for K and V in one
  * launch (cache.py:87-129, codec.py:23-65).  keys/values: [batch][kv_heads]
  * [S][head_dim] with element strides (sb, sh, ss) and unit dim stride, of

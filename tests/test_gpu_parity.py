@@ -435,3 +435,30 @@ def test_errors():
     with pytest.raises(ValueError, match="head_dim changed"):
         c.update_and_fetch(torch.zeros(1, 2, 3, 64, dtype=torch.float16, device="cuda"),
                            torch.zeros(1, 2, 3, 64, dtype=torch.float16, device="cuda"))
+
+
+def test_no_device_timeouts_recorded():
+    import ctypes
+    from chronoquant_mlx_b200 import _lib
+    code = ctypes.c_int(-1)
+    _lib.check(_lib.lib().cq_device_error(ctypes.byref(code), 1))
+    assert code.value == 0
+
+
+@pytest.mark.parametrize("T", [1, 2, 15, 16, 17, 255, 256, 257, 1000])
+def test_decode_fast_vs_generic_small_T(T):
+    """Decode through the fast kernel (paged cache) and through the general
+    kernel (the reconstruct path, use_fused=False) on the same cache."""
+    from chronoquant_mlx_b200 import chronoquant_sdpa
+    K, V = O.ar1_kv(2, 2, T, 128, seed=T + 100)
+    g = build_cache(K, V, [T], stride_k=32, stride_v=8)
+    o = oracle_cache(K, V, [T], stride_k=32, stride_v=8)
+    q = (np.random.default_rng(T).standard_normal((2, 8, 1, 128)) / math.sqrt(128)).astype(np.float16)
+    scale = 1.0 / math.sqrt(128)
+    out = chronoquant_sdpa(cu(q), None, None, g, scale)
+    qs = (q.astype(np.float64) * float(np.float16(scale))).astype(np.float16)
+    k32, v32 = o.reconstruct_history_f32()
+    close(npy(out), O.exact_sdpa(qs, k32, v32, False))
+    g.use_fused = False
+    out2 = chronoquant_sdpa(cu(q), None, None, g, scale)
+    close(npy(out2), npy(out))
