@@ -7,13 +7,14 @@
 // serves every query head of the GQA group from a single read:
 //
 //   producer warp:  1-D bulk-async copies (TMA engine) of a page's anchors,
-//                   code rows and scales into a shared-memory stage, with
-//                   completion counted on an mbarrier (expect_tx);
-//   4 consumer warps, 64 tokens each per page:
+//                   code rows and scales into a shared-memory stage, counted
+//                   on an mbarrier (expect_tx); once a stage lands it computes
+//                   q . K-anchor for every anchor of the page (tensor-core MMA)
+//                   and releases the stage to the consumers;
+//   8 consumer warps, 32 tokens each per page:
 //     scores  S = q.anchor + scale_t * (q . codes_t)      (kernels.py:152-159)
-//             q.codes: tensor-core MMA, A = INT4 codes turned into exact fp16
-//             integers in registers, B = the query group;  q.anchor: MMA over
-//             the page's K anchors, once per anchor;
+//             q.codes: MMA with A = INT4 codes turned into exact fp16 integers
+//             in registers, B = the query group;
 //     softmax online, base 2, lazily rescaled (a new max is applied only when
 //             it exceeds the running one by 8, so p <= 256);
 //     output  O += anchor_v(t) * p_t + codes_v(t) * (p_t * scale_t)
@@ -22,15 +23,17 @@
 //             registers; P moves from the score layout to the operand layout
 //             with movmatrix.trans.
 //
-// Work is split into items of `ppi` pages of one unit; a persistent grid
-// walks items round-robin and writes one partial (max, sum, unnormalised
-// output) per item; fast_combine merges the partials of each query head.
+// Work is split into items of `ppi` pages of one unit; each CTA of a
+// persistent grid takes a contiguous range of items and writes one partial
+// (max, sum, unnormalised output) per item; fast_combine merges the partials
+// of each query head.
 //
 // Requirements (fast_decode_supported): q_len 1, head_dim 128, GQA group <= 8,
 // page_tokens <= 256 and a multiple of 16, strides >= 2, V codes in the MMA
 // nibble order, 16-byte aligned rows.
 #include <algorithm>
 #include <mutex>
+#include <string>
 
 #include "cq_decode_fast.cuh"
 #include "cq_ptx.cuh"
@@ -38,10 +41,9 @@
 namespace cq {
 namespace fast {
 
-constexpr int NW = 4;               // consumer warps
+constexpr int NW = 8;               // consumer warps
 constexpr int NT = (NW + 1) * 32;   // + one producer warp
 constexpr int HD = 128;             // head_dim
-constexpr int QA_ROWS = 48;         // anchors a warp may touch per page (3 MMA row tiles)
 constexpr float TAU = 8.0f;         // lazy-rescale threshold (log2 units)
 constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
@@ -62,14 +64,20 @@ struct Params {
   int n_items;
   int stages;
   int tpw;           // tiles (16 tokens) per consumer warp per page
+  int qa_rows;       // q.anchor rows per stage (anchors per page rounded up to 16)
   // shared memory layout (bytes)
   int off_tab, off_qa, off_merge, off_stage, stage_bytes;
   int st_kf[2], st_cd[2], st_sc[2];
   float *ws_m, *ws_l, *ws_o;  // [n_items][8], [n_items][8], [n_items][8][128]
-  int *err;
 };
 
 __device__ int g_fast_error;
+
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
 
 __device__ __forceinline__ float q_scaled(const Params &p, int b, int hq, int d) {
   const float sc = round_dt(p.scale, p.q_dtype);
@@ -105,47 +113,158 @@ __device__ __forceinline__ CopyPlan plan_page(const Params &p, int nvalid) {
   return c;
 }
 
-// ---------------------------------------------------------------------------
-// producer: one thread issues every bulk copy of this CTA's pages
-// ---------------------------------------------------------------------------
-__device__ void producer(const Params &p, unsigned char *smem, uint64_t *full, uint64_t *empty) {
-  const CacheView &cv = p.cv;
-  int it = 0;
-  bool ok = true;
-  for (int item = blockIdx.x; item < p.n_items && ok; item += gridDim.x) {
-    const int unit = item / p.ipu, chunk = item - (item / p.ipu) * p.ipu;
-    const int b = unit / cv.H, h = unit - (unit / cv.H) * cv.H;
-    const int lp0 = chunk * p.ppi, lp1 = min(lp0 + p.ppi, p.n_pages_unit);
-    for (int lp = lp0; lp < lp1; ++lp, ++it) {
-      const int s = it % p.stages;
-      if (it >= p.stages && !ptx::mbar_wait_bounded(&empty[s], ((it / p.stages) - 1) & 1, WAIT_BUDGET)) {
-        atomicExch(&g_fast_error, ERR_TIMEOUT_EMPTY);
-        ok = false;
-        break;
-      }
-      const int64_t pg = cv.block_table[(int64_t)b * cv.max_pages + lp];
-      const int nvalid = (int)min((int64_t)cv.P, p.T - (int64_t)lp * cv.P);
-      const CopyPlan cp = plan_page(p, nvalid);
-      unsigned char *stage = smem + p.off_stage + s * p.stage_bytes;
-      ptx::mbar_arrive_expect_tx(&full[s], cp.total);
-      for (int comp = 0; comp < 2; ++comp) {
-        const CompView &cc = cv.c[comp];
-        const int64_t ph = pg * cv.H + h;
-        const unsigned char *kf = (const unsigned char *)(cc.kf + ph * cc.apg * HD);
-        const unsigned char *cd = (const unsigned char *)(cc.codes + ph * cc.ppg * (HD / 8));
-        const unsigned char *sc = (const unsigned char *)(cc.scales + ph * cc.srow);
-        ptx::bulk_g2s(stage + p.st_kf[comp], kf, cp.bytes[comp * 3 + 0], &full[s]);
-        if (cp.bytes[comp * 3 + 1]) {
-          ptx::bulk_g2s(stage + p.st_cd[comp], cd, cp.bytes[comp * 3 + 1], &full[s]);
-          ptx::bulk_g2s(stage + p.st_sc[comp], sc, cp.bytes[comp * 3 + 2], &full[s]);
-        }
-      }
+// Items [first, last) of this CTA: a contiguous share of all items.
+__device__ __forceinline__ void my_items(const Params &p, int &first, int &last) {
+  first = (int)((int64_t)blockIdx.x * p.n_items / gridDim.x);
+  last = (int)((int64_t)(blockIdx.x + 1) * p.n_items / gridDim.x);
+}
+
+struct PageRef {
+  int item, unit, b, h, lp, last_in_item;
+};
+
+// Walk the pages of items [first, last) in order.
+struct PageIter {
+  const Params *p;
+  int item, last, lp, lp1;
+  __device__ void init(const Params &pp, int first, int last_) {
+    p = &pp;
+    item = first;
+    last = last_;
+    set_item();
+  }
+  __device__ void set_item() {
+    if (item < last) {
+      const int chunk = item % p->ipu;
+      lp = chunk * p->ppi;
+      lp1 = min(lp + p->ppi, p->n_pages_unit);
     }
   }
-  if (!ok) {
+  __device__ bool valid() const { return item < last; }
+  __device__ PageRef get() const {
+    PageRef r;
+    r.item = item;
+    r.unit = item / p->ipu;
+    r.b = r.unit / p->cv.H;
+    r.h = r.unit - r.b * p->cv.H;
+    r.lp = lp;
+    r.last_in_item = (lp + 1 == lp1);
+    return r;
+  }
+  __device__ void next() {
+    if (++lp >= lp1) {
+      ++item;
+      set_item();
+    }
+  }
+};
+
+// ---------------------------------------------------------------------------
+// producer warp: bulk copies (lane 0) + q . K-anchor for each landed page
+// ---------------------------------------------------------------------------
+__device__ void issue_page(const Params &p, unsigned char *smem, uint64_t *full, const PageRef &r, int s) {
+  const CacheView &cv = p.cv;
+  const int64_t pg = cv.block_table[(int64_t)r.b * cv.max_pages + r.lp];
+  const int nvalid = (int)min((int64_t)cv.P, p.T - (int64_t)r.lp * cv.P);
+  const CopyPlan cp = plan_page(p, nvalid);
+  unsigned char *stage = smem + p.off_stage + s * p.stage_bytes;
+  ptx::mbar_arrive_expect_tx(&full[s], cp.total);
+  for (int comp = 0; comp < 2; ++comp) {
+    const CompView &cc = cv.c[comp];
+    const int64_t ph = pg * cv.H + r.h;
+    ptx::bulk_g2s(stage + p.st_kf[comp], cc.kf + ph * cc.apg * HD, cp.bytes[comp * 3 + 0], &full[s]);
+    if (cp.bytes[comp * 3 + 1]) {
+      ptx::bulk_g2s(stage + p.st_cd[comp], cc.codes + ph * cc.ppg * (HD / 8), cp.bytes[comp * 3 + 1], &full[s]);
+      ptx::bulk_g2s(stage + p.st_sc[comp], cc.scales + ph * cc.srow, cp.bytes[comp * 3 + 2], &full[s]);
+    }
+  }
+}
+
+__device__ void producer(const Params &p, unsigned char *smem, uint64_t *full, uint64_t *empty, uint64_t *ready,
+                         int lane) {
+  const CacheView &cv = p.cv;
+  const int g = lane >> 2, t = lane & 3;
+  int first, last;
+  my_items(p, first, last);
+  PageIter rd, pf;  // rd: page whose q.anchor is computed next; pf: next page to prefetch
+  rd.init(p, first, last);
+  pf.init(p, first, last);
+  int it_pf = 0;
+  bool ok = true;
+  // prefetch distance stages-1
+  for (; it_pf < p.stages - 1 && pf.valid(); ++it_pf, pf.next())
+    if (lane == 0) issue_page(p, smem, full, pf.get(), it_pf % p.stages);
+
+  uint32_t qBn[8][2];
+  int cur_unit = -1;
+  int it = 0;
+  for (; rd.valid(); ++it, rd.next()) {
+    const PageRef r = rd.get();
+    const int s = it % p.stages;
+    if (!ptx::mbar_wait_bounded(&full[s], (it / p.stages) & 1, WAIT_BUDGET)) {
+      atomicExch(&g_fast_error, ERR_TIMEOUT_FULL);
+      ok = false;
+      break;
+    }
+    if (r.unit != cur_unit) {
+      cur_unit = r.unit;
+      const int hq = r.h * p.gqa + g;
+      const bool real = g < p.gqa;
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        const int d0 = 16 * kk + 2 * t;
+        qBn[kk][0] = real ? ptx::pack_half2(q_scaled(p, r.b, hq, d0), q_scaled(p, r.b, hq, d0 + 1)) : 0u;
+        qBn[kk][1] = real ? ptx::pack_half2(q_scaled(p, r.b, hq, d0 + 8), q_scaled(p, r.b, hq, d0 + 9)) : 0u;
+      }
+    }
+    // q . anchor for every K anchor present in the page (rows = anchors)
+    const int nvalid = (int)min((int64_t)cv.P, p.T - (int64_t)r.lp * cv.P);
+    const int nK = (nvalid - 1) / cv.c[0].stride + 1;
+    const unsigned char *kfK = smem + p.off_stage + s * p.stage_bytes + p.st_kf[0];
+    float *qa = (float *)(smem + p.off_qa) + s * p.qa_rows * 8;
+    const int mi = lane >> 3, rr = lane & 7;
+    for (int mt = 0; mt * 16 < nK; ++mt) {
+      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      const int arow = min(mt * 16 + rr + ((mi & 1) ? 8 : 0), nK - 1);
+      const uint32_t base = ptx::smem_u32(kfK + arow * (HD * 2) + ((mi & 2) ? 16 : 0));
+#pragma unroll
+      for (int kk = 0; kk < 8; ++kk) {
+        uint32_t a0, a1, a2, a3;
+        ptx::ldmatrix_x4(a0, a1, a2, a3, base + kk * 32);
+        ptx::mma_f16_16816(c, a0, a1, a2, a3, qBn[kk][0], qBn[kk][1]);
+      }
+      float *row0 = qa + (mt * 16 + g) * 8 + 2 * t;
+      row0[0] = c[0] * LOG2E;
+      row0[1] = c[1] * LOG2E;
+      row0[64] = c[2] * LOG2E;
+      row0[65] = c[3] * LOG2E;
+    }
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&ready[s]);
+    // prefetch: the stage of page it_pf was last used by page it_pf - stages = it - 1,
+    // which the consumers are finishing while this page is ready for them
+    if (pf.valid()) {
+      const int s2 = it_pf % p.stages;
+      if (lane == 0) {
+        if (it_pf >= p.stages && !ptx::mbar_wait_bounded(&empty[s2], ((it_pf / p.stages) - 1) & 1, WAIT_BUDGET)) {
+          atomicExch(&g_fast_error, ERR_TIMEOUT_EMPTY);
+          ok = false;
+        } else {
+          issue_page(p, smem, full, pf.get(), s2);
+        }
+      }
+      ok = __shfl_sync(0xffffffffu, ok, 0);
+      if (!ok) {
+        ++it;
+        break;
+      }
+      ++it_pf;
+      pf.next();
+    }
+  }
+  if (!ok && lane == 0) {
     // drain: wait (bounded) for copies already issued into stages nobody will read
-    for (int k = max(0, it - p.stages); k < it; ++k)
-      ptx::mbar_wait_bounded(&full[k % p.stages], (k / p.stages) & 1, WAIT_BUDGET);
+    for (int k = it; k < it_pf; ++k) ptx::mbar_wait_bounded(&full[k % p.stages], (k / p.stages) & 1, WAIT_BUDGET);
   }
 }
 
@@ -167,8 +286,10 @@ __device__ __forceinline__ void reset(WarpState &st) {
     for (int j = 0; j < 4; ++j) st.o[i][j] = 0.f;
 }
 
+// Merge the consumer warps' states into one partial per item (real heads only).
 __device__ void flush_item(const Params &p, unsigned char *smem, WarpState &st, int item, int warp, int lane) {
   const int g = lane >> 2, t = lane & 3;
+  const int G = p.gqa;
   float l0 = st.l[0], l1 = st.l[1];
 #pragma unroll
   for (int o = 4; o < 32; o <<= 1) {
@@ -177,25 +298,33 @@ __device__ void flush_item(const Params &p, unsigned char *smem, WarpState &st, 
   }
   float *wm = (float *)(smem + p.off_merge);  // [NW][8]
   float *wl = wm + NW * 8;                     // [NW][8]
-  float *wo = wl + NW * 8;                     // [NW][8][HD]
+  float *wo = wl + NW * 8;                     // [NW][G][HD]
   if (g == 0) {
     wm[warp * 8 + 2 * t] = st.m[0];
     wm[warp * 8 + 2 * t + 1] = st.m[1];
     wl[warp * 8 + 2 * t] = l0;
     wl[warp * 8 + 2 * t + 1] = l1;
   }
-  float *w0 = wo + (warp * 8 + 2 * t) * HD;
-  float *w1 = w0 + HD;
+  if (2 * t < G) {
+    float *w0 = wo + (warp * G + 2 * t) * HD;
 #pragma unroll
-  for (int i = 0; i < 8; ++i) {
-    w0[16 * i + g] = st.o[i][0];
-    w1[16 * i + g] = st.o[i][1];
-    w0[16 * i + g + 8] = st.o[i][2];
-    w1[16 * i + g + 8] = st.o[i][3];
+    for (int i = 0; i < 8; ++i) {
+      w0[16 * i + g] = st.o[i][0];
+      w0[16 * i + g + 8] = st.o[i][2];
+    }
+  }
+  if (2 * t + 1 < G) {
+    float *w1 = wo + (warp * G + 2 * t + 1) * HD;
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      w1[16 * i + g] = st.o[i][1];
+      w1[16 * i + g + 8] = st.o[i][3];
+    }
   }
   ptx::named_barrier_sync(1, NW * 32);
-  const int d = threadIdx.x;  // 0..127 -> output dim
-  for (int hh = 0; hh < p.gqa; ++hh) {
+  // thread -> (head, dim): NW*32 = 256 threads cover 2 heads x 128 dims per round
+  for (int idx = threadIdx.x; idx < G * HD; idx += NW * 32) {
+    const int hh = idx / HD, d = idx - (idx / HD) * HD;
     float M = -INFINITY;
 #pragma unroll
     for (int w = 0; w < NW; ++w) M = fmaxf(M, wm[w * 8 + hh]);
@@ -203,9 +332,9 @@ __device__ void flush_item(const Params &p, unsigned char *smem, WarpState &st, 
 #pragma unroll
     for (int w = 0; w < NW; ++w) {
       const float mw = wm[w * 8 + hh];
-      const float f = (mw == -INFINITY) ? 0.f : exp2f(mw - M);
+      const float f = (mw == -INFINITY) ? 0.f : fast_exp2(mw - M);
       L += wl[w * 8 + hh] * f;
-      acc += wo[(w * 8 + hh) * HD + d] * f;
+      acc += wo[(w * G + hh) * HD + d] * f;
     }
     p.ws_o[((int64_t)item * 8 + hh) * HD + d] = acc;
     if (d == 0) {
@@ -217,227 +346,194 @@ __device__ void flush_item(const Params &p, unsigned char *smem, WarpState &st, 
   reset(st);
 }
 
-__device__ void consumer(const Params &p, unsigned char *smem, uint64_t *full, uint64_t *empty, int warp, int lane) {
+__device__ __forceinline__ void process_tile(const Params &p, WarpState &st, const uint32_t *tab, const float *qa,
+                                             const unsigned char *cdK, const __half *scK, const unsigned char *kfV,
+                                             const unsigned char *cdV, const __half *scV, const uint32_t (&qB)[4][4],
+                                             int tb, int nvalid, int lane) {
+  const int g = lane >> 2, t = lane & 3;
+  // ---------------- scores S^T[token][head] = q.codes (MMA), then anchors + scale
+  const uint32_t e0 = tab[tb + g], e1 = tab[tb + g + 8];
+  const int pk0 = e0 & 0xff, pk1 = e1 & 0xff;
+  const int rk0 = (pk0 == 255) ? 0 : pk0, rk1 = (pk1 == 255) ? 0 : pk1;
+  const uint4 wk0 = *(const uint4 *)(cdK + rk0 * 64 + t * 16);
+  const uint4 wk1 = *(const uint4 *)(cdK + rk1 * 64 + t * 16);
+  float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
+  {
+    const uint32_t w0[4] = {wk0.x, wk0.y, wk0.z, wk0.w};
+    const uint32_t w1[4] = {wk1.x, wk1.y, wk1.z, wk1.w};
+#pragma unroll
+    for (int J = 0; J < 4; ++J) {
+      uint32_t h0[4], h1[4];
+      ptx::nibbles_to_half2(w0[J], h0);  // (d0,d4) (d1,d5) (d2,d6) (d3,d7)
+      ptx::nibbles_to_half2(w1[J], h1);
+      ptx::mma_f16_16816(ca, h0[0], h1[0], h0[1], h1[1], qB[J][0], qB[J][1]);
+      ptx::mma_f16_16816(cb, h0[2], h1[2], h0[3], h1[3], qB[J][2], qB[J][3]);
+    }
+  }
+  const float sk0 = (pk0 == 255) ? 0.f : __half2float(scK[rk0]) * LOG2E;
+  const float sk1 = (pk1 == 255) ? 0.f : __half2float(scK[rk1]) * LOG2E;
+  const float2 qa0 = *(const float2 *)(qa + ((e0 >> 8) & 0xff) * 8 + 2 * t);
+  const float2 qa1 = *(const float2 *)(qa + ((e1 >> 8) & 0xff) * 8 + 2 * t);
+  float s0 = fmaf(sk0, ca[0] + cb[0], qa0.x), s1 = fmaf(sk0, ca[1] + cb[1], qa0.y);
+  float s2 = fmaf(sk1, ca[2] + cb[2], qa1.x), s3 = fmaf(sk1, ca[3] + cb[3], qa1.y);
+  if (tb + g >= nvalid) s0 = s1 = -INFINITY;
+  if (tb + g + 8 >= nvalid) s2 = s3 = -INFINITY;
+
+  // ---------------- online softmax (base 2), lazy rescale
+  {
+    float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
+    const bool need = (mx0 > st.m[0] + TAU) || (mx1 > st.m[1] + TAU);
+    if (__any_sync(0xffffffffu, need)) {
+#pragma unroll
+      for (int o = 4; o < 32; o <<= 1) {
+        mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
+        mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
+      }
+      const float n0 = fmaxf(st.m[0], mx0), n1 = fmaxf(st.m[1], mx1);
+      const float f0 = (n0 == -INFINITY) ? 1.f : fast_exp2(st.m[0] - n0);
+      const float f1 = (n1 == -INFINITY) ? 1.f : fast_exp2(st.m[1] - n1);
+      st.m[0] = n0;
+      st.m[1] = n1;
+      st.l[0] *= f0;
+      st.l[1] *= f1;
+#pragma unroll
+      for (int i = 0; i < 8; ++i) {
+        st.o[i][0] *= f0;
+        st.o[i][1] *= f1;
+        st.o[i][2] *= f0;
+        st.o[i][3] *= f1;
+      }
+    }
+  }
+  // masked scores are -inf and the running max is finite here: ex2(-inf) = 0
+  const float p0 = fast_exp2(s0 - st.m[0]);
+  const float p1 = fast_exp2(s1 - st.m[1]);
+  const float p2 = fast_exp2(s2 - st.m[0]);
+  const float p3 = fast_exp2(s3 - st.m[1]);
+  st.l[0] += p0 + p2;
+  st.l[1] += p1 + p3;
+
+  // ---------------- P (anchor term) and P' = P * scale_v (code term) as B operands
+  const int pv0 = (e0 >> 16) & 0xff, pv1 = (e1 >> 16) & 0xff;
+  const float sv0 = (pv0 == 255) ? 0.f : __half2float(scV[pv0]);
+  const float sv1 = (pv1 == 255) ? 0.f : __half2float(scV[pv1]);
+  const uint32_t bP0 = ptx::movmatrix_trans(ptx::pack_half2(p0, p1));
+  const uint32_t bP1 = ptx::movmatrix_trans(ptx::pack_half2(p2, p3));
+  const uint32_t bS0 = ptx::movmatrix_trans(ptx::pack_half2(p0 * sv0, p1 * sv0));
+  const uint32_t bS1 = ptx::movmatrix_trans(ptx::pack_half2(p2 * sv1, p3 * sv1));
+
+  // ---------------- V anchors: O += A_v^T P  (ldmatrix.trans gathers each token's anchor)
+  {
+    const int mi = lane >> 3, r = lane & 7;
+    const int tok = tb + r + ((mi & 2) ? 8 : 0);
+    const int av = (tok < nvalid) ? (int)(tab[tok] >> 24) : 0;
+    const uint32_t base = ptx::smem_u32(kfV + av * (HD * 2) + ((mi & 1) ? 16 : 0));
+#pragma unroll
+    for (int i = 0; i < 8; ++i) {
+      uint32_t a0, a1, a2, a3;
+      ptx::ldmatrix_x4_trans(a0, a1, a2, a3, base + i * 32);
+      ptx::mma_f16_16816(st.o[i], a0, a1, a2, a3, bP0, bP1);
+    }
+  }
+  // ---------------- V codes: O += C_v^T P'  (tokens 2t,2t+1 | 2t+8,2t+9; words 2g, 2g+1)
+  {
+    const uint2 ea = *(const uint2 *)(tab + tb + 2 * t);
+    const uint2 ec = *(const uint2 *)(tab + tb + 2 * t + 8);
+    int ra = (ea.x >> 16) & 0xff, rb = (ea.y >> 16) & 0xff;
+    int rc = (ec.x >> 16) & 0xff, rd = (ec.y >> 16) & 0xff;
+    ra = (ra == 255) ? 0 : ra;
+    rb = (rb == 255) ? 0 : rb;
+    rc = (rc == 255) ? 0 : rc;
+    rd = (rd == 255) ? 0 : rd;
+    const uint2 va = *(const uint2 *)(cdV + ra * 64 + g * 8);
+    const uint2 vb = *(const uint2 *)(cdV + rb * 64 + g * 8);
+    const uint2 vc = *(const uint2 *)(cdV + rc * 64 + g * 8);
+    const uint2 vd = *(const uint2 *)(cdV + rd * 64 + g * 8);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const uint32_t wa = q ? va.y : va.x, wb = q ? vb.y : vb.x;
+      const uint32_t wc = q ? vc.y : vc.x, wd = q ? vd.y : vd.x;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const uint32_t sel = half ? 0x7632u : 0x5410u;
+        uint32_t xa[4], xc[4];
+        ptx::nibbles_to_half2(__byte_perm(wa, wb, sel), xa);  // nibbles 4*half + 0..3 of tokens (a, b)
+        ptx::nibbles_to_half2(__byte_perm(wc, wd, sel), xc);
+        // nibble j of word q <-> m-tile 4q + j/2, row g (+8 when j is odd)
+        const int i0 = 4 * q + 2 * half;
+        ptx::mma_f16_16816(st.o[i0], xa[0], xa[1], xc[0], xc[1], bS0, bS1);
+        ptx::mma_f16_16816(st.o[i0 + 1], xa[2], xa[3], xc[2], xc[3], bS0, bS1);
+      }
+    }
+  }
+}
+
+__device__ void consumer(const Params &p, unsigned char *smem, uint64_t *empty, uint64_t *ready, int warp,
+                         int lane) {
   const CacheView &cv = p.cv;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t *tab = (const uint32_t *)(smem + p.off_tab);
-  float *qa = (float *)(smem + p.off_qa) + warp * (QA_ROWS * 8);
-  const int sk = cv.c[0].stride;
   const int tiles_page = cv.P / 16;
   const int tile0 = warp * p.tpw;
   const int tile1 = min(tile0 + p.tpw, tiles_page);
-  const int tok_lo = tile0 * 16;
-  const int a_base = tok_lo / sk;
-  const int n_anch = (tile1 > tile0) ? ((tile1 * 16 - 1) / sk - a_base + 1) : 0;
-  const int qa_tiles = (n_anch + 15) / 16;
 
   WarpState st;
   reset(st);
-  int it = 0;
+  int first, last;
+  my_items(p, first, last);
+  PageIter pi;
+  pi.init(p, first, last);
   int cur_unit = -1;
-  uint32_t qB[4][4];   // query in the K-code order (k-permuted)
-  uint32_t qBn[8][2];  // query in natural dim order (for anchors)
-
-  for (int item = blockIdx.x; item < p.n_items; item += gridDim.x) {
-    const int unit = item / p.ipu, chunk = item - (item / p.ipu) * p.ipu;
-    const int b = unit / cv.H, h = unit - (unit / cv.H) * cv.H;
-    if (unit != cur_unit) {
-      cur_unit = unit;
-      const int hq = h * p.gqa + g;
+  uint32_t qB[4][4];  // query in the K-code order (k-permuted)
+  for (int it = 0; pi.valid(); ++it, pi.next()) {
+    const PageRef r = pi.get();
+    if (r.unit != cur_unit) {
+      cur_unit = r.unit;
+      const int hq = r.h * p.gqa + g;
       const bool real = g < p.gqa;
 #pragma unroll
       for (int J = 0; J < 4; ++J) {
         const int d0 = 32 * t + 8 * J;
         float v[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = real ? q_scaled(p, b, hq, d0 + i) : 0.f;
+        for (int i = 0; i < 8; ++i) v[i] = real ? q_scaled(p, r.b, hq, d0 + i) : 0.f;
         qB[J][0] = ptx::pack_half2(v[0], v[4]);
         qB[J][1] = ptx::pack_half2(v[1], v[5]);
         qB[J][2] = ptx::pack_half2(v[2], v[6]);
         qB[J][3] = ptx::pack_half2(v[3], v[7]);
       }
-#pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        const int d0 = 16 * kk + 2 * t;
-        qBn[kk][0] = real ? ptx::pack_half2(q_scaled(p, b, hq, d0), q_scaled(p, b, hq, d0 + 1)) : 0u;
-        qBn[kk][1] = real ? ptx::pack_half2(q_scaled(p, b, hq, d0 + 8), q_scaled(p, b, hq, d0 + 9)) : 0u;
-      }
     }
-    const int lp0 = chunk * p.ppi, lp1 = min(lp0 + p.ppi, p.n_pages_unit);
-    for (int lp = lp0; lp < lp1; ++lp, ++it) {
-      const int s = it % p.stages;
-      if (!ptx::mbar_wait_bounded(&full[s], (it / p.stages) & 1, WAIT_BUDGET)) {
-        atomicExch(&g_fast_error, ERR_TIMEOUT_FULL);
-        return;
-      }
-      const int nvalid = (int)min((int64_t)cv.P, p.T - (int64_t)lp * cv.P);
-      unsigned char *stage = smem + p.off_stage + s * p.stage_bytes;
-      const unsigned char *kfK = stage + p.st_kf[0];
-      const unsigned char *cdK = stage + p.st_cd[0];
-      const __half *scK = (const __half *)(stage + p.st_sc[0]);
-      const unsigned char *kfV = stage + p.st_kf[1];
-      const unsigned char *cdV = stage + p.st_cd[1];
-      const __half *scV = (const __half *)(stage + p.st_sc[1]);
-      const int nK = (nvalid - 1) / sk + 1;  // anchors present
-
-      if (tok_lo < nvalid) {
-        // ---- q . K-anchor for this warp's anchors (MMA over rows = anchors)
-        for (int mt = 0; mt < qa_tiles; ++mt) {
-          float c[4] = {0.f, 0.f, 0.f, 0.f};
-          const int mi = lane >> 3, r = lane & 7;
-          int arow = a_base + mt * 16 + r + ((mi & 1) ? 8 : 0);
-          arow = min(arow, nK - 1);
-          const uint32_t base = ptx::smem_u32(kfK + arow * (HD * 2) + ((mi & 2) ? 16 : 0));
-#pragma unroll
-          for (int kk = 0; kk < 8; ++kk) {
-            uint32_t a0, a1, a2, a3;
-            ptx::ldmatrix_x4(a0, a1, a2, a3, base + kk * 32);
-            ptx::mma_f16_16816(c, a0, a1, a2, a3, qBn[kk][0], qBn[kk][1]);
-          }
-          float *row0 = qa + (mt * 16 + g) * 8 + 2 * t;
-          float *row1 = row0 + 8 * 8;
-          row0[0] = c[0] * LOG2E;
-          row0[1] = c[1] * LOG2E;
-          row1[0] = c[2] * LOG2E;
-          row1[1] = c[3] * LOG2E;
-        }
-        __syncwarp();
-
-        for (int tile = tile0; tile < tile1; ++tile) {
-          const int tb = tile * 16;
-          if (tb >= nvalid) break;
-          // ---------------- scores S^T[token][head] = q.codes (MMA), then anchors + scale
-          const uint32_t e0 = tab[tb + g], e1 = tab[tb + g + 8];
-          const int pk0 = e0 & 0xff, pk1 = e1 & 0xff;
-          const int rk0 = (pk0 == 255) ? 0 : pk0, rk1 = (pk1 == 255) ? 0 : pk1;
-          const uint4 wk0 = *(const uint4 *)(cdK + rk0 * 64 + t * 16);
-          const uint4 wk1 = *(const uint4 *)(cdK + rk1 * 64 + t * 16);
-          float c[4] = {0.f, 0.f, 0.f, 0.f};
-          {
-            const uint32_t w0[4] = {wk0.x, wk0.y, wk0.z, wk0.w};
-            const uint32_t w1[4] = {wk1.x, wk1.y, wk1.z, wk1.w};
-#pragma unroll
-            for (int J = 0; J < 4; ++J) {
-              uint32_t h0[4], h1[4];
-              ptx::nibbles_to_half2(w0[J], h0);  // (d0,d4) (d1,d5) (d2,d6) (d3,d7)
-              ptx::nibbles_to_half2(w1[J], h1);
-              ptx::mma_f16_16816(c, h0[0], h1[0], h0[1], h1[1], qB[J][0], qB[J][1]);
-              ptx::mma_f16_16816(c, h0[2], h1[2], h0[3], h1[3], qB[J][2], qB[J][3]);
-            }
-          }
-          const float sk0 = (pk0 == 255) ? 0.f : __half2float(scK[rk0]) * LOG2E;
-          const float sk1 = (pk1 == 255) ? 0.f : __half2float(scK[rk1]) * LOG2E;
-          const float2 qa0 = *(const float2 *)(qa + (((e0 >> 8) & 0xff) - a_base) * 8 + 2 * t);
-          const float2 qa1 = *(const float2 *)(qa + (((e1 >> 8) & 0xff) - a_base) * 8 + 2 * t);
-          float s0 = fmaf(sk0, c[0], qa0.x), s1 = fmaf(sk0, c[1], qa0.y);
-          float s2 = fmaf(sk1, c[2], qa1.x), s3 = fmaf(sk1, c[3], qa1.y);
-          if (tb + g >= nvalid) s0 = s1 = -INFINITY;
-          if (tb + g + 8 >= nvalid) s2 = s3 = -INFINITY;
-
-          // ---------------- online softmax (base 2), lazy rescale
-          {
-            float mx0 = fmaxf(s0, s2), mx1 = fmaxf(s1, s3);
-            const bool need = (mx0 > st.m[0] + TAU) || (mx1 > st.m[1] + TAU);
-            if (__any_sync(0xffffffffu, need)) {
-#pragma unroll
-              for (int o = 4; o < 32; o <<= 1) {
-                mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, o));
-                mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, o));
-              }
-              const float n0 = fmaxf(st.m[0], mx0), n1 = fmaxf(st.m[1], mx1);
-              const float f0 = (n0 == -INFINITY) ? 1.f : exp2f(st.m[0] - n0);
-              const float f1 = (n1 == -INFINITY) ? 1.f : exp2f(st.m[1] - n1);
-              st.m[0] = n0;
-              st.m[1] = n1;
-              st.l[0] *= f0;
-              st.l[1] *= f1;
-#pragma unroll
-              for (int i = 0; i < 8; ++i) {
-                st.o[i][0] *= f0;
-                st.o[i][1] *= f1;
-                st.o[i][2] *= f0;
-                st.o[i][3] *= f1;
-              }
-            }
-          }
-          const float p0 = (s0 == -INFINITY) ? 0.f : exp2f(s0 - st.m[0]);
-          const float p1 = (s1 == -INFINITY) ? 0.f : exp2f(s1 - st.m[1]);
-          const float p2 = (s2 == -INFINITY) ? 0.f : exp2f(s2 - st.m[0]);
-          const float p3 = (s3 == -INFINITY) ? 0.f : exp2f(s3 - st.m[1]);
-          st.l[0] += p0 + p2;
-          st.l[1] += p1 + p3;
-
-          // ---------------- P (anchor term) and P' = P * scale_v (code term) as B operands
-          const int pv0 = (e0 >> 16) & 0xff, pv1 = (e1 >> 16) & 0xff;
-          const float sv0 = (pv0 == 255) ? 0.f : __half2float(scV[pv0]);
-          const float sv1 = (pv1 == 255) ? 0.f : __half2float(scV[pv1]);
-          const uint32_t bP0 = ptx::movmatrix_trans(ptx::pack_half2(p0, p1));
-          const uint32_t bP1 = ptx::movmatrix_trans(ptx::pack_half2(p2, p3));
-          const uint32_t bS0 = ptx::movmatrix_trans(ptx::pack_half2(p0 * sv0, p1 * sv0));
-          const uint32_t bS1 = ptx::movmatrix_trans(ptx::pack_half2(p2 * sv1, p3 * sv1));
-
-          // ---------------- V anchors: O += A_v^T P  (ldmatrix.trans gathers each token's anchor)
-          {
-            const int mi = lane >> 3, r = lane & 7;
-            const int tok = tb + r + ((mi & 2) ? 8 : 0);
-            const int av = (tok < nvalid) ? (int)(tab[tok] >> 24) : 0;
-            const uint32_t base = ptx::smem_u32(kfV + av * (HD * 2) + ((mi & 1) ? 16 : 0));
-#pragma unroll
-            for (int i = 0; i < 8; ++i) {
-              uint32_t a0, a1, a2, a3;
-              ptx::ldmatrix_x4_trans(a0, a1, a2, a3, base + i * 32);
-              ptx::mma_f16_16816(st.o[i], a0, a1, a2, a3, bP0, bP1);
-            }
-          }
-          // ---------------- V codes: O += C_v^T P'  (tokens 2t,2t+1 | 2t+8,2t+9; words 2g, 2g+1)
-          {
-            const uint2 ea = *(const uint2 *)(tab + tb + 2 * t);
-            const uint2 ec = *(const uint2 *)(tab + tb + 2 * t + 8);
-            int ra = (ea.x >> 16) & 0xff, rb = (ea.y >> 16) & 0xff;
-            int rc = (ec.x >> 16) & 0xff, rd = (ec.y >> 16) & 0xff;
-            ra = (ra == 255) ? 0 : ra;
-            rb = (rb == 255) ? 0 : rb;
-            rc = (rc == 255) ? 0 : rc;
-            rd = (rd == 255) ? 0 : rd;
-            const uint2 va = *(const uint2 *)(cdV + ra * 64 + g * 8);
-            const uint2 vb = *(const uint2 *)(cdV + rb * 64 + g * 8);
-            const uint2 vc = *(const uint2 *)(cdV + rc * 64 + g * 8);
-            const uint2 vd = *(const uint2 *)(cdV + rd * 64 + g * 8);
-#pragma unroll
-            for (int q = 0; q < 2; ++q) {
-              const uint32_t wa = q ? va.y : va.x, wb = q ? vb.y : vb.x;
-              const uint32_t wc = q ? vc.y : vc.x, wd = q ? vd.y : vd.x;
-#pragma unroll
-              for (int half = 0; half < 2; ++half) {
-                const uint32_t sel = half ? 0x7632u : 0x5410u;
-                uint32_t xa[4], xc[4];
-                ptx::nibbles_to_half2(__byte_perm(wa, wb, sel), xa);  // nibbles 4*half + 0..3 of tokens (a, b)
-                ptx::nibbles_to_half2(__byte_perm(wc, wd, sel), xc);
-                // nibble j of word q <-> m-tile 4q + j/2, row g (+8 when j is odd)
-                const int i0 = 4 * q + 2 * half;
-                ptx::mma_f16_16816(st.o[i0], xa[0], xa[1], xc[0], xc[1], bS0, bS1);
-                ptx::mma_f16_16816(st.o[i0 + 1], xa[2], xa[3], xc[2], xc[3], bS0, bS1);
-              }
-            }
-          }
-        }
-      }
-      __syncwarp();
-      if (lane == 0) ptx::mbar_arrive(&empty[s]);
-      if (lp + 1 == lp1) flush_item(p, smem, st, item, warp, lane);
+    const int s = it % p.stages;
+    if (!ptx::mbar_wait_bounded(&ready[s], (it / p.stages) & 1, WAIT_BUDGET)) {
+      atomicExch(&g_fast_error, ERR_TIMEOUT_FULL);
+      return;
     }
+    const int nvalid = (int)min((int64_t)cv.P, p.T - (int64_t)r.lp * cv.P);
+    const unsigned char *stage = smem + p.off_stage + s * p.stage_bytes;
+    const float *qa = (const float *)(smem + p.off_qa) + s * p.qa_rows * 8;
+    for (int tile = tile0; tile < tile1; ++tile) {
+      const int tb = tile * 16;
+      if (tb >= nvalid) break;
+      process_tile(p, st, tab, qa, stage + p.st_cd[0], (const __half *)(stage + p.st_sc[0]), stage + p.st_kf[1],
+                   stage + p.st_cd[1], (const __half *)(stage + p.st_sc[1]), qB, tb, nvalid, lane);
+    }
+    __syncwarp();
+    if (lane == 0) ptx::mbar_arrive(&empty[s]);
+    if (r.last_in_item) flush_item(p, smem, st, r.item, warp, lane);
   }
 }
 
-__global__ void __launch_bounds__(NT) decode_kernel(const __grid_constant__ Params p) {
+__global__ void __launch_bounds__(NT, 2) decode_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t *full = (uint64_t *)smem;
   uint64_t *empty = full + p.stages;
+  uint64_t *ready = empty + p.stages;
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   if (threadIdx.x == 0) {
     for (int s = 0; s < p.stages; ++s) {
       ptx::mbar_init(&full[s], 1);
       ptx::mbar_init(&empty[s], NW);
+      ptx::mbar_init(&ready[s], 1);
     }
     ptx::fence_mbar_init();
   }
@@ -445,55 +541,47 @@ __global__ void __launch_bounds__(NT) decode_kernel(const __grid_constant__ Para
   for (int i = threadIdx.x; i < p.cv.P; i += NT) tab[i] = tab_entry(i, p.cv.c[0].stride, p.cv.c[1].stride);
   __syncthreads();
   if (warp == NW) {
-    if (lane == 0) producer(p, smem, full, empty);
+    producer(p, smem, full, empty, ready, lane);
     return;
   }
-  consumer(p, smem, full, empty, warp, lane);
+  consumer(p, smem, empty, ready, warp, lane);
 }
 
-// Merge the item partials of one (sequence, query head) row; one warp per row.
-__global__ void fast_combine(const float *ws_m, const float *ws_l, const float *ws_o, int ipu, int H, int gqa,
-                             int Hq, int64_t rows, void *out, int out_dtype, float *lse_out) {
-  const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
-  const int lane = threadIdx.x & 31;
-  if (row >= rows) return;
-  const int b = (int)(row / Hq), hq = (int)(row - (row / Hq) * Hq);
-  const int u = b * H + hq / gqa, hh = hq % gqa;
+// Merge the item partials of one (sequence, kv-head) unit: one CTA per unit,
+// thread = (head, dim); sums over the unit's items.
+__global__ void fast_combine(const float *ws_m, const float *ws_l, const float *ws_o, int ipu, int H, int gqa, int Hq,
+                             void *out, int out_dtype, float *lse_out) {
+  const int u = blockIdx.x;
+  const int b = u / H, h = u - (u / H) * H;
   const int64_t i0 = (int64_t)u * ipu;
-  float M = -INFINITY;
-  for (int j = 0; j < ipu; ++j) M = fmaxf(M, ws_m[(i0 + j) * 8 + hh]);
-  float L = 0.f;
-  float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int j = 0; j < ipu; ++j) {
-    const float m = ws_m[(i0 + j) * 8 + hh];
-    const float f = (m == -INFINITY) ? 0.f : exp2f(m - M);
-    L += ws_l[(i0 + j) * 8 + hh] * f;
-    const float4 o = *(const float4 *)(ws_o + ((i0 + j) * 8 + hh) * HD + lane * 4);
-    acc.x += o.x * f;
-    acc.y += o.y * f;
-    acc.z += o.z * f;
-    acc.w += o.w * f;
+  for (int idx = threadIdx.x; idx < gqa * HD; idx += blockDim.x) {
+    const int hh = idx / HD, d = idx - (idx / HD) * HD;
+    float M = -INFINITY;
+    for (int j = 0; j < ipu; ++j) M = fmaxf(M, ws_m[(i0 + j) * 8 + hh]);
+    float L = 0.f, acc = 0.f;
+    for (int j = 0; j < ipu; ++j) {
+      const float m = ws_m[(i0 + j) * 8 + hh];
+      const float f = (m == -INFINITY) ? 0.f : exp2f(m - M);
+      L += ws_l[(i0 + j) * 8 + hh] * f;
+      acc += ws_o[((i0 + j) * 8 + hh) * HD + d] * f;
+    }
+    const int64_t row = (int64_t)b * Hq + h * gqa + hh;
+    store_from_float(out, row * HD + d, (L > 0.f) ? acc / L : 0.f, out_dtype);
+    if (lse_out && d == 0) lse_out[row] = (L > 0.f) ? (M + log2f(L)) * LN2 : -INFINITY;
   }
-  const float inv = (L > 0.f) ? 1.f / L : 0.f;
-  const int64_t ob = row * HD + lane * 4;
-  store_from_float(out, ob + 0, acc.x * inv, out_dtype);
-  store_from_float(out, ob + 1, acc.y * inv, out_dtype);
-  store_from_float(out, ob + 2, acc.z * inv, out_dtype);
-  store_from_float(out, ob + 3, acc.w * inv, out_dtype);
-  if (lse_out && lane == 0) lse_out[row] = (L > 0.f) ? (M + log2f(L)) * LN2 : -INFINITY;
 }
 
 // ---------------------------------------------------------------------------
 // host side
 // ---------------------------------------------------------------------------
 struct Layout {
-  int stages, stage_bytes, off_tab, off_qa, off_merge, off_stage, total;
+  int stages, stage_bytes, off_tab, off_qa, off_merge, off_stage, total, qa_rows;
   int st_kf[2], st_cd[2], st_sc[2];
 };
 
 static inline int up128(int x) { return (x + 127) & ~127; }
 
-static Layout make_layout(const cq_paged_cache &c, int stages) {
+static Layout make_layout(const cq_paged_cache &c, int stages, int gqa) {
   Layout L;
   const cq_component *cc[2] = {&c.k, &c.v};
   int off = 0;
@@ -507,25 +595,36 @@ static Layout make_layout(const cq_paged_cache &c, int stages) {
   }
   L.stage_bytes = off;
   L.stages = stages;
+  L.qa_rows = ((c.k.anchors_per_page + 15) / 16) * 16;
   L.off_tab = 128;  // mbarriers live in the first 128 bytes
   L.off_qa = up128(L.off_tab + c.page_tokens * 4);
-  L.off_merge = up128(L.off_qa + NW * QA_ROWS * 8 * 4);
-  L.off_stage = up128(L.off_merge + (NW * 8 * 2 + NW * 8 * HD) * 4);
+  L.off_merge = up128(L.off_qa + stages * L.qa_rows * 8 * 4);
+  L.off_stage = up128(L.off_merge + (NW * 8 * 2 + NW * gqa * HD) * 4);
   L.total = L.off_stage + stages * L.stage_bytes;
   return L;
 }
 
 static constexpr int kMaxSmem = 227 * 1024;
+static constexpr int kSmPerSm = 228 * 1024;
 
-static int pick_stages(const cq_paged_cache &c) {
-  // two stages keep two CTAs per SM for the common presets; more when a
-  // stage is small
+static int pick_stages(const cq_paged_cache &c, int gqa, int &per_sm) {
+  // prefer two CTAs per SM (16 consumer warps), then the deepest pipeline
   for (int s = 4; s >= 2; --s) {
-    Layout L = make_layout(c, s);
-    if (L.total * 2 + 2048 <= 228 * 1024) return s;
+    Layout L = make_layout(c, s, gqa);
+    if (2 * (L.total + 1024) <= kSmPerSm) {
+      per_sm = 2;
+      return s;
+    }
   }
-  Layout L2 = make_layout(c, 2);
-  return (L2.total <= kMaxSmem) ? 2 : 0;
+  for (int s = 4; s >= 2; --s) {
+    Layout L = make_layout(c, s, gqa);
+    if (L.total <= kMaxSmem) {
+      per_sm = 1;
+      return s;
+    }
+  }
+  per_sm = 0;
+  return 0;
 }
 
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
@@ -542,10 +641,8 @@ bool fast_decode_supported(const cq_paged_cache &c, int n_q_heads, int q_len) {
   if (!aligned16(c.k.keyframes) || !aligned16(c.v.keyframes) || !aligned16(c.k.codes) || !aligned16(c.v.codes) ||
       !aligned16(c.k.scales) || !aligned16(c.v.scales))
     return false;
-  // anchors one warp's 64-token block can touch must fit the q.anchor rows
-  const int tpw = (c.page_tokens / 16 + NW - 1) / NW;
-  if ((tpw * 16) / c.k.stride + 1 > QA_ROWS) return false;
-  return pick_stages(c) >= 2;
+  int per_sm;
+  return pick_stages(c, gqa, per_sm) >= 2;
 }
 
 static int items_plan(const cq_paged_cache &c, int64_t T, int splits_req, int &ppi, int &ipu) {
@@ -565,14 +662,16 @@ size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, 
 }
 
 static int sm_count() {
-  static int n = 0;
-  if (!n) {
-    int dev = 0;
-    cudaGetDevice(&dev);
-    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
-    if (n <= 0) n = 148;
+  static int n[64] = {};
+  int dev = 0;
+  cudaGetDevice(&dev);
+  if (dev < 0 || dev >= 64) return 148;
+  if (!n[dev]) {
+    int v = 0;
+    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    n[dev] = v > 0 ? v : 148;
   }
-  return n;
+  return n[dev];
 }
 
 int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, const void *q, int q_dtype,
@@ -589,10 +688,12 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
   p.T = T;
   p.n_pages_unit = items_plan(c, T, splits_req, p.ppi, p.ipu);
   p.n_items = c.batch * c.kv_heads * p.ipu;
-  const int stages = pick_stages(c);
-  Layout L = make_layout(c, stages);
+  int per_sm = 0;
+  const int stages = pick_stages(c, p.gqa, per_sm);
+  Layout L = make_layout(c, stages, p.gqa);
   p.stages = stages;
   p.tpw = (c.page_tokens / 16 + NW - 1) / NW;
+  p.qa_rows = L.qa_rows;
   p.off_tab = L.off_tab;
   p.off_qa = L.off_qa;
   p.off_merge = L.off_merge;
@@ -608,7 +709,6 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
   p.ws_m = (float *)ws;
   p.ws_l = p.ws_m + (size_t)p.n_items * 8;
   p.ws_o = p.ws_l + (size_t)p.n_items * 8;
-  p.err = nullptr;
 
   static std::mutex mu;
   static bool attr_set[64] = {};
@@ -618,18 +718,17 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 0 || dev >= 64 || !attr_set[dev]) {
       cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
-      if (e != cudaSuccess) return set_error(CQ_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
+      if (e != cudaSuccess)
+        return set_error(CQ_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
       if (dev >= 0 && dev < 64) attr_set[dev] = true;
     }
   }
-  const int per_sm = (L.total * 2 + 2048 <= 228 * 1024) ? 2 : 1;
   const int grid = std::min(p.n_items, sm_count() * per_sm);
   decode_kernel<<<grid, NT, L.total, st>>>(p);
   int r = check_launch("decode_kernel");
   if (r) return r;
-  const int64_t rows = (int64_t)c.batch * n_q_heads;
-  fast_combine<<<(unsigned)((rows * 32 + 255) / 256), 256, 0, st>>>(p.ws_m, p.ws_l, p.ws_o, p.ipu, c.kv_heads, p.gqa,
-                                                                     n_q_heads, rows, out, out_dtype, lse_out);
+  fast_combine<<<c.batch * c.kv_heads, 256, 0, st>>>(p.ws_m, p.ws_l, p.ws_o, p.ipu, c.kv_heads, p.gqa, n_q_heads,
+                                                      out, out_dtype, lse_out);
   return check_launch("fast_combine");
 }
 

@@ -20,7 +20,8 @@ __global__ void reconstruct_kernel(CacheView cv, int comp, int64_t T, __half *ou
   TokLoc L = locate(cv, comp, b, h, t);
   for (int d = lane; d < cv.D; d += 32) {
     __half a = L.anchor[d];
-    __half v = a;
+    // I-frames: anchor + 0 as the reference's where(is_pframe, delta, 0) sum does (-0.0 becomes +0.0)
+    __half v = __hadd_rn(a, __float2half_rn(0.f));
     if (L.codes) {
       int code = nibble_at(L.codes, d, cv.D, c.order) - 8;
       __half s = __float2half_rn(L.scale);
