@@ -468,8 +468,8 @@ __device__ __forceinline__ void process_tile(const Params &p, WarpState &st, con
   }
 }
 
-__device__ void consumer(const Params &p, unsigned char *smem, uint64_t *empty, uint64_t *ready, int warp,
-                         int lane) {
+__device__ void consumer(const Params &p, unsigned char *smem, uint64_t *full, uint64_t *empty, uint64_t *ready,
+                         int warp, int lane) {
   const CacheView &cv = p.cv;
   const int g = lane >> 2, t = lane & 3;
   const uint32_t *tab = (const uint32_t *)(smem + p.off_tab);
@@ -504,7 +504,10 @@ __device__ void consumer(const Params &p, unsigned char *smem, uint64_t *empty, 
       }
     }
     const int s = it % p.stages;
-    if (!ptx::mbar_wait_bounded(&ready[s], (it / p.stages) & 1, WAIT_BUDGET)) {
+    // the bulk copies' own barrier makes their bytes visible to this thread;
+    // `ready` adds the producer's q.anchor rows
+    if (!ptx::mbar_wait_bounded(&full[s], (it / p.stages) & 1, WAIT_BUDGET) ||
+        !ptx::mbar_wait_bounded(&ready[s], (it / p.stages) & 1, WAIT_BUDGET)) {
       atomicExch(&g_fast_error, ERR_TIMEOUT_FULL);
       return;
     }
@@ -544,31 +547,71 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const __grid_constant__ P
     producer(p, smem, full, empty, ready, lane);
     return;
   }
-  consumer(p, smem, empty, ready, warp, lane);
+  consumer(p, smem, full, empty, ready, warp, lane);
 }
 
-// Merge the item partials of one (sequence, kv-head) unit: one CTA per unit,
-// thread = (head, dim); sums over the unit's items.
-__global__ void fast_combine(const float *ws_m, const float *ws_l, const float *ws_o, int ipu, int H, int gqa, int Hq,
-                             void *out, int out_dtype, float *lse_out) {
-  const int u = blockIdx.x;
-  const int b = u / H, h = u - (u / H) * H;
+// Merge the item partials of one (sequence, query head) row: one CTA of 128
+// threads per row, thread = output dim.  The per-item weights exp2(m_i - M)/L
+// are computed once into shared memory, then every thread streams its dim of
+// the item outputs with independent loads.
+constexpr int kCombineMaxItems = 1024;
+
+__global__ void __launch_bounds__(HD) fast_combine(const float *ws_m, const float *ws_l, const float *ws_o, int ipu,
+                                                   int H, int gqa, int Hq, void *out, int out_dtype, float *lse_out) {
+  __shared__ float s_w[kCombineMaxItems];
+  __shared__ float s_red[HD / 32];
+  __shared__ float s_ML[2];
+  const int row = blockIdx.x;  // b * Hq + hq
+  const int b = row / Hq, hq = row - (row / Hq) * Hq;
+  const int u = b * H + hq / gqa, hh = hq % gqa;
   const int64_t i0 = (int64_t)u * ipu;
-  for (int idx = threadIdx.x; idx < gqa * HD; idx += blockDim.x) {
-    const int hh = idx / HD, d = idx - (idx / HD) * HD;
-    float M = -INFINITY;
-    for (int j = 0; j < ipu; ++j) M = fmaxf(M, ws_m[(i0 + j) * 8 + hh]);
-    float L = 0.f, acc = 0.f;
-    for (int j = 0; j < ipu; ++j) {
-      const float m = ws_m[(i0 + j) * 8 + hh];
-      const float f = (m == -INFINITY) ? 0.f : exp2f(m - M);
-      L += ws_l[(i0 + j) * 8 + hh] * f;
-      acc += ws_o[((i0 + j) * 8 + hh) * HD + d] * f;
-    }
-    const int64_t row = (int64_t)b * Hq + h * gqa + hh;
-    store_from_float(out, row * HD + d, (L > 0.f) ? acc / L : 0.f, out_dtype);
-    if (lse_out && d == 0) lse_out[row] = (L > 0.f) ? (M + log2f(L)) * LN2 : -INFINITY;
+  const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
+  // pass 1: max over items
+  float M = -INFINITY;
+  for (int j = d; j < ipu; j += HD) M = fmaxf(M, ws_m[(i0 + j) * 8 + hh]);
+  M = warp_max(M);
+  if (lane == 0) s_red[warp] = M;
+  __syncthreads();
+  if (d == 0) {
+    float v = s_red[0];
+    for (int w = 1; w < HD / 32; ++w) v = fmaxf(v, s_red[w]);
+    s_ML[0] = v;
   }
+  __syncthreads();
+  M = s_ML[0];
+  // pass 2: weights and the denominator
+  float L = 0.f;
+  for (int j = d; j < ipu; j += HD) {
+    const float m = ws_m[(i0 + j) * 8 + hh];
+    const float f = (m == -INFINITY) ? 0.f : exp2f(m - M);
+    s_w[j] = f;
+    L += ws_l[(i0 + j) * 8 + hh] * f;
+  }
+  L = warp_sum(L);
+  __syncthreads();
+  if (lane == 0) s_red[warp] = L;
+  __syncthreads();
+  if (d == 0) {
+    float v = 0.f;
+    for (int w = 0; w < HD / 32; ++w) v += s_red[w];
+    s_ML[1] = v;
+  }
+  __syncthreads();
+  L = s_ML[1];
+  // pass 3: weighted sum of the item outputs
+  const float *o = ws_o + (i0 * 8 + hh) * HD + d;
+  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  int j = 0;
+  for (; j + 4 <= ipu; j += 4) {
+    a0 += o[(int64_t)(j + 0) * 8 * HD] * s_w[j + 0];
+    a1 += o[(int64_t)(j + 1) * 8 * HD] * s_w[j + 1];
+    a2 += o[(int64_t)(j + 2) * 8 * HD] * s_w[j + 2];
+    a3 += o[(int64_t)(j + 3) * 8 * HD] * s_w[j + 3];
+  }
+  for (; j < ipu; ++j) a0 += o[(int64_t)j * 8 * HD] * s_w[j];
+  const float acc = (a0 + a1) + (a2 + a3);
+  store_from_float(out, (int64_t)row * HD + d, (L > 0.f) ? acc / L : 0.f, out_dtype);
+  if (lse_out && d == 0) lse_out[row] = (L > 0.f) ? (M + log2f(L)) * LN2 : -INFINITY;
 }
 
 // ---------------------------------------------------------------------------
@@ -649,6 +692,7 @@ static int items_plan(const cq_paged_cache &c, int64_t T, int splits_req, int &p
   const int npu = (int)((T + c.page_tokens - 1) / c.page_tokens);
   ppi = 2;
   if (splits_req > 0) ppi = std::max(1, (npu + splits_req - 1) / splits_req);
+  ppi = std::max(ppi, (npu + kCombineMaxItems - 1) / kCombineMaxItems);  // the combine holds <= 1024 weights
   ipu = (npu + ppi - 1) / ppi;
   return npu;
 }
@@ -727,8 +771,8 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
   decode_kernel<<<grid, NT, L.total, st>>>(p);
   int r = check_launch("decode_kernel");
   if (r) return r;
-  fast_combine<<<c.batch * c.kv_heads, 256, 0, st>>>(p.ws_m, p.ws_l, p.ws_o, p.ipu, c.kv_heads, p.gqa, n_q_heads,
-                                                      out, out_dtype, lse_out);
+  fast_combine<<<c.batch * n_q_heads, HD, 0, st>>>(p.ws_m, p.ws_l, p.ws_o, p.ipu, c.kv_heads, p.gqa, n_q_heads,
+                                                    out, out_dtype, lse_out);
   return check_launch("fast_combine");
 }
 
