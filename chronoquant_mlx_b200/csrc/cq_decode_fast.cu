@@ -11,7 +11,8 @@
 //                   on an mbarrier (expect_tx); once a stage lands it computes
 //                   q . K-anchor for every anchor of the page (tensor-core MMA)
 //                   and releases the stage to the consumers;
-//   8 consumer warps, 32 tokens each per page:
+//   8 consumer warps, 32 tokens each per page (the producer also expands the
+//   page's per-token scales):
 //     scores  S = q.anchor + scale_t * (q . codes_t)      (kernels.py:152-159)
 //             q.codes: MMA with A = INT4 codes turned into exact fp16 integers
 //             in registers, B = the query group;
@@ -23,15 +24,16 @@
 //             registers; P moves from the score layout to the operand layout
 //             with movmatrix.trans.
 //
-// Work is split into items of `ppi` pages of one unit; each CTA of a
-// persistent grid takes a contiguous range of items and writes one partial
-// (max, sum, unnormalised output) per item; fast_combine merges the partials
-// of each query head.
+// Work: every CTA of a persistent grid takes a balanced, contiguous range of
+// the global page index (unit-major) and writes one partial (max, sum,
+// unnormalised output) per unit its range touches; fast_combine merges the
+// partials of each query head.
 //
 // Requirements (fast_decode_supported): q_len 1, head_dim 128, GQA group <= 8,
 // page_tokens <= 256 and a multiple of 16, strides >= 2, V codes in the MMA
 // nibble order, 16-byte aligned rows.
 #include <algorithm>
+#include <cstdlib>
 #include <mutex>
 #include <string>
 
@@ -41,8 +43,8 @@
 namespace cq {
 namespace fast {
 
-constexpr int NW = 8;               // consumer warps
-constexpr int NT = (NW + 1) * 32;   // + one producer warp
+// consumer warps per CTA (template parameter NW): 16 (one CTA per SM) or 8
+constexpr int kMaxNW = 16;
 constexpr int HD = 128;             // head_dim
 constexpr float TAU = 8.0f;         // lazy-rescale threshold (log2 units)
 constexpr float LOG2E = 1.4426950408889634f;
@@ -58,17 +60,17 @@ struct Params {
   float scale;
   int gqa;
   int64_t T;
-  int n_pages_unit;  // pages per (sequence, kv-head) unit
-  int ppi;           // pages per item
-  int ipu;           // items per unit
-  int n_items;
+  int npu;            // pages per (sequence, kv-head) unit
+  int64_t tp;         // total pages = units * npu
+  int smax;           // partial slots per CTA (unit segments a CTA's page range can touch)
   int stages;
   int tpw;           // tiles (16 tokens) per consumer warp per page
   int qa_rows;       // q.anchor rows per stage (anchors per page rounded up to 16)
   // shared memory layout (bytes)
-  int off_tab, off_qa, off_merge, off_stage, stage_bytes;
+  int off_tab, off_qa, off_sc, off_merge, off_stage, stage_bytes;
   int st_kf[2], st_cd[2], st_sc[2];
-  float *ws_m, *ws_l, *ws_o;  // [n_items][8], [n_items][8], [n_items][8][128]
+  uint32_t full_bytes[6], full_total;  // bulk-copy sizes of a full page
+  float *ws_m, *ws_l, *ws_o;  // [grid*smax][8], [grid*smax][8], [grid*smax][8][128]
 };
 
 __device__ int g_fast_error;
@@ -85,12 +87,18 @@ __device__ __forceinline__ float q_scaled(const Params &p, int b, int hq, int d)
   return round_dt(v, p.q_dtype);  // q * scale in the query dtype (attention.py:46)
 }
 
-// Table entry per page-local token: [pfK:8][aK:8][pfV:8][aV:8], pf 255 = I-frame.
-__device__ __forceinline__ uint32_t tab_entry(int tl, int sk, int sv) {
+// Per page-local token, two words of shared-memory byte offsets:
+//   K: [code row offset:14][I-frame:1][0:1][q.anchor row offset:16]
+//   V: [code row offset:14][I-frame:1][0:1][anchor row offset:16]
+// I-frames point at code row 0; their scale is 0, so the row never counts.
+constexpr uint32_t TAB_OFF = 0x3fffu, TAB_IFRAME = 0x4000u;
+
+__device__ __forceinline__ uint2 tab_entry(int tl, int sk, int sv) {
   const int ak = tl / sk, av = tl / sv;
-  const int pk = (tl - ak * sk) ? (tl - ak - 1) : 255;
-  const int pv = (tl - av * sv) ? (tl - av - 1) : 255;
-  return (uint32_t)pk | ((uint32_t)ak << 8) | ((uint32_t)pv << 16) | ((uint32_t)av << 24);
+  const bool ik = (tl - ak * sk) == 0, iv = (tl - av * sv) == 0;
+  const uint32_t ck = ik ? TAB_IFRAME : (uint32_t)((tl - ak - 1) * 64);
+  const uint32_t cv = iv ? TAB_IFRAME : (uint32_t)((tl - av - 1) * 64);
+  return make_uint2(ck | ((uint32_t)(ak * 32) << 16), cv | ((uint32_t)(av * 256) << 16));
 }
 
 struct CopyPlan {
@@ -98,8 +106,16 @@ struct CopyPlan {
   uint32_t total;
 };
 
+// Bytes of the six bulk copies of a page holding `nvalid` tokens (only the
+// anchors, code rows and 16-byte-rounded scales those tokens use).
 __device__ __forceinline__ CopyPlan plan_page(const Params &p, int nvalid) {
   CopyPlan c;
+  if (nvalid == p.cv.P) {
+#pragma unroll
+    for (int i = 0; i < 6; ++i) c.bytes[i] = p.full_bytes[i];
+    c.total = p.full_total;
+    return c;
+  }
   c.total = 0;
   for (int comp = 0; comp < 2; ++comp) {
     const CompView &cc = p.cv.c[comp];
@@ -113,69 +129,72 @@ __device__ __forceinline__ CopyPlan plan_page(const Params &p, int nvalid) {
   return c;
 }
 
-// Items [first, last) of this CTA: a contiguous share of all items.
-__device__ __forceinline__ void my_items(const Params &p, int &first, int &last) {
-  first = (int)((int64_t)blockIdx.x * p.n_items / gridDim.x);
-  last = (int)((int64_t)(blockIdx.x + 1) * p.n_items / gridDim.x);
+// Pages [first, last) of the global page index (unit * npu + page) that this
+// CTA processes: a contiguous, balanced share.
+__device__ __forceinline__ void my_pages(const Params &p, int64_t &first, int64_t &last) {
+  first = (int64_t)blockIdx.x * p.tp / gridDim.x;
+  last = (int64_t)(blockIdx.x + 1) * p.tp / gridDim.x;
 }
 
-struct PageRef {
-  int item, unit, b, h, lp, last_in_item;
-};
-
-// Walk the pages of items [first, last) in order.
-struct PageIter {
-  const Params *p;
-  int item, last, lp, lp1;
-  __device__ void init(const Params &pp, int first, int last_) {
-    p = &pp;
-    item = first;
-    last = last_;
-    set_item();
+// Walks this CTA's pages in order with running counters (no per-page
+// division): unit, its (sequence, head), page within the unit, partial-slot
+// segment, pipeline stage and barrier phase.
+struct Cursor {
+  int unit, b, h, lp, seg, s;
+  uint32_t ph;
+  int64_t left;  // pages left including the current one
+  __device__ void init(const Params &p, int64_t first, int64_t last) {
+    unit = (int)(first / p.npu);
+    lp = (int)(first - (int64_t)unit * p.npu);
+    b = unit / p.cv.H;
+    h = unit - b * p.cv.H;
+    seg = 0;
+    s = 0;
+    ph = 0;
+    left = last - first;
   }
-  __device__ void set_item() {
-    if (item < last) {
-      const int chunk = item % p->ipu;
-      lp = chunk * p->ppi;
-      lp1 = min(lp + p->ppi, p->n_pages_unit);
+  __device__ bool valid() const { return left > 0; }
+  __device__ bool last_in_seg(const Params &p) const { return left == 1 || lp + 1 == p.npu; }
+  __device__ int nvalid(const Params &p) const {
+    return (int)min((int64_t)p.cv.P, p.T - (int64_t)lp * p.cv.P);
+  }
+  __device__ void next(const Params &p) {
+    if (++lp == p.npu) {
+      lp = 0;
+      ++unit;
+      ++seg;
+      if (++h == p.cv.H) {
+        h = 0;
+        ++b;
+      }
     }
-  }
-  __device__ bool valid() const { return item < last; }
-  __device__ PageRef get() const {
-    PageRef r;
-    r.item = item;
-    r.unit = item / p->ipu;
-    r.b = r.unit / p->cv.H;
-    r.h = r.unit - r.b * p->cv.H;
-    r.lp = lp;
-    r.last_in_item = (lp + 1 == lp1);
-    return r;
-  }
-  __device__ void next() {
-    if (++lp >= lp1) {
-      ++item;
-      set_item();
+    if (++s == p.stages) {
+      s = 0;
+      ph ^= 1u;
     }
+    --left;
   }
 };
 
 // ---------------------------------------------------------------------------
 // producer warp: bulk copies (lane 0) + q . K-anchor for each landed page
 // ---------------------------------------------------------------------------
-__device__ void issue_page(const Params &p, unsigned char *smem, uint64_t *full, const PageRef &r, int s) {
+__device__ __forceinline__ int64_t page_id(const Params &p, const Cursor &c) {
+  return p.cv.block_table[(int64_t)c.b * p.cv.max_pages + c.lp];
+}
+
+__device__ void issue_page(const Params &p, unsigned char *smem, uint64_t *full, const Cursor &c, int64_t pg) {
   const CacheView &cv = p.cv;
-  const int64_t pg = cv.block_table[(int64_t)r.b * cv.max_pages + r.lp];
-  const int nvalid = (int)min((int64_t)cv.P, p.T - (int64_t)r.lp * cv.P);
-  const CopyPlan cp = plan_page(p, nvalid);
-  unsigned char *stage = smem + p.off_stage + s * p.stage_bytes;
-  ptx::mbar_arrive_expect_tx(&full[s], cp.total);
+  const CopyPlan cp = plan_page(p, c.nvalid(p));
+  unsigned char *stage = smem + p.off_stage + c.s * p.stage_bytes;
+  ptx::mbar_arrive_expect_tx(&full[c.s], cp.total);
   for (int comp = 0; comp < 2; ++comp) {
     const CompView &cc = cv.c[comp];
-    const int64_t ph = pg * cv.H + r.h;
-    ptx::bulk_g2s(stage + p.st_kf[comp], cc.kf + ph * cc.apg * HD, cp.bytes[comp * 3 + 0], &full[s]);
+    const int64_t ph = pg * cv.H + c.h;
+    ptx::bulk_g2s(stage + p.st_kf[comp], cc.kf + ph * cc.apg * HD, cp.bytes[comp * 3 + 0], &full[c.s]);
     if (cp.bytes[comp * 3 + 1]) {
-      ptx::bulk_g2s(stage + p.st_cd[comp], cc.codes + ph * cc.ppg * (HD / 8), cp.bytes[comp * 3 + 1], &full[s]);
-      ptx::bulk_g2s(stage + p.st_sc[comp], cc.scales + ph * cc.srow, cp.bytes[comp * 3 + 2], &full[s]);
+      ptx::bulk_g2s(stage + p.st_cd[comp], cc.codes + ph * cc.ppg * (HD / 8), cp.bytes[comp * 3 + 1], &full[c.s]);
+      ptx::bulk_g2s(stage + p.st_sc[comp], cc.scales + ph * cc.srow, cp.bytes[comp * 3 + 2], &full[c.s]);
     }
   }
 }
@@ -184,44 +203,63 @@ __device__ void producer(const Params &p, unsigned char *smem, uint64_t *full, u
                          int lane) {
   const CacheView &cv = p.cv;
   const int g = lane >> 2, t = lane & 3;
-  int first, last;
-  my_items(p, first, last);
-  PageIter rd, pf;  // rd: page whose q.anchor is computed next; pf: next page to prefetch
+  int64_t first, last;
+  my_pages(p, first, last);
+  const uint2 *tab = (const uint2 *)(smem + p.off_tab);
+  Cursor rd, pf;  // rd: page whose q.anchor is computed next; pf: next page to prefetch
   rd.init(p, first, last);
   pf.init(p, first, last);
-  int it_pf = 0;
+  int64_t issued = 0;
   bool ok = true;
   // prefetch distance stages-1
-  for (; it_pf < p.stages - 1 && pf.valid(); ++it_pf, pf.next())
-    if (lane == 0) issue_page(p, smem, full, pf.get(), it_pf % p.stages);
+  for (; issued < p.stages - 1 && pf.valid(); ++issued, pf.next(p))
+    if (lane == 0) issue_page(p, smem, full, pf, page_id(p, pf));
 
   uint32_t qBn[8][2];
   int cur_unit = -1;
-  int it = 0;
-  for (; rd.valid(); ++it, rd.next()) {
-    const PageRef r = rd.get();
-    const int s = it % p.stages;
-    if (!ptx::mbar_wait_bounded(&full[s], (it / p.stages) & 1, WAIT_BUDGET)) {
+  int64_t done = 0;
+  for (; rd.valid(); ++done, rd.next(p)) {
+    // block-table entry of the page prefetched at the end of this iteration,
+    // loaded now so its latency hides behind this page's work
+    int64_t pg_next = 0;
+    if (lane == 0 && pf.valid()) pg_next = page_id(p, pf);
+    if (!ptx::mbar_wait_bounded(&full[rd.s], rd.ph, WAIT_BUDGET)) {
       atomicExch(&g_fast_error, ERR_TIMEOUT_FULL);
       ok = false;
       break;
     }
-    if (r.unit != cur_unit) {
-      cur_unit = r.unit;
-      const int hq = r.h * p.gqa + g;
+    if (rd.unit != cur_unit) {
+      cur_unit = rd.unit;
+      const int hq = rd.h * p.gqa + g;
       const bool real = g < p.gqa;
 #pragma unroll
       for (int kk = 0; kk < 8; ++kk) {
         const int d0 = 16 * kk + 2 * t;
-        qBn[kk][0] = real ? ptx::pack_half2(q_scaled(p, r.b, hq, d0), q_scaled(p, r.b, hq, d0 + 1)) : 0u;
-        qBn[kk][1] = real ? ptx::pack_half2(q_scaled(p, r.b, hq, d0 + 8), q_scaled(p, r.b, hq, d0 + 9)) : 0u;
+        qBn[kk][0] = real ? ptx::pack_half2(q_scaled(p, rd.b, hq, d0), q_scaled(p, rd.b, hq, d0 + 1)) : 0u;
+        qBn[kk][1] = real ? ptx::pack_half2(q_scaled(p, rd.b, hq, d0 + 8), q_scaled(p, rd.b, hq, d0 + 9)) : 0u;
+      }
+    }
+    const int nvalid = rd.nvalid(p);
+    const unsigned char *stage = smem + p.off_stage + rd.s * p.stage_bytes;
+    // per-token scales (K pre-multiplied by log2 e; 0 for I-frames) for the consumers
+    {
+      float2 *sc = (float2 *)(smem + p.off_sc) + rd.s * cv.P;
+      const __half *scK = (const __half *)(stage + p.st_sc[0]);
+      const __half *scV = (const __half *)(stage + p.st_sc[1]);
+      for (int tl = lane; tl < cv.P; tl += 32) {
+        float a = 0.f, v = 0.f;
+        if (tl < nvalid) {
+          const uint2 e = tab[tl];
+          if (!(e.x & TAB_IFRAME)) a = __half2float(scK[(e.x & TAB_OFF) >> 6]) * LOG2E;
+          if (!(e.y & TAB_IFRAME)) v = __half2float(scV[(e.y & TAB_OFF) >> 6]);
+        }
+        sc[tl] = make_float2(a, v);
       }
     }
     // q . anchor for every K anchor present in the page (rows = anchors)
-    const int nvalid = (int)min((int64_t)cv.P, p.T - (int64_t)r.lp * cv.P);
-    const int nK = (nvalid - 1) / cv.c[0].stride + 1;
-    const unsigned char *kfK = smem + p.off_stage + s * p.stage_bytes + p.st_kf[0];
-    float *qa = (float *)(smem + p.off_qa) + s * p.qa_rows * 8;
+    const int nK = (nvalid == cv.P) ? cv.c[0].apg : (nvalid - 1) / cv.c[0].stride + 1;
+    const unsigned char *kfK = stage + p.st_kf[0];
+    float *qa = (float *)(smem + p.off_qa) + rd.s * p.qa_rows * 8;
     const int mi = lane >> 3, rr = lane & 7;
     for (int mt = 0; mt * 16 < nK; ++mt) {
       float c[4] = {0.f, 0.f, 0.f, 0.f};
@@ -240,31 +278,33 @@ __device__ void producer(const Params &p, unsigned char *smem, uint64_t *full, u
       row0[65] = c[3] * LOG2E;
     }
     __syncwarp();
-    if (lane == 0) ptx::mbar_arrive(&ready[s]);
-    // prefetch: the stage of page it_pf was last used by page it_pf - stages = it - 1,
+    if (lane == 0) ptx::mbar_arrive(&ready[rd.s]);
+    // prefetch: the stage of the next page was last used by page done + 1 - stages,
     // which the consumers are finishing while this page is ready for them
     if (pf.valid()) {
-      const int s2 = it_pf % p.stages;
       if (lane == 0) {
-        if (it_pf >= p.stages && !ptx::mbar_wait_bounded(&empty[s2], ((it_pf / p.stages) - 1) & 1, WAIT_BUDGET)) {
+        if (issued >= p.stages && !ptx::mbar_wait_bounded(&empty[pf.s], pf.ph ^ 1u, WAIT_BUDGET)) {
           atomicExch(&g_fast_error, ERR_TIMEOUT_EMPTY);
           ok = false;
         } else {
-          issue_page(p, smem, full, pf.get(), s2);
+          issue_page(p, smem, full, pf, pg_next);
         }
       }
       ok = __shfl_sync(0xffffffffu, ok, 0);
       if (!ok) {
-        ++it;
+        ++done;
         break;
       }
-      ++it_pf;
-      pf.next();
+      ++issued;
+      pf.next(p);
     }
   }
   if (!ok && lane == 0) {
     // drain: wait (bounded) for copies already issued into stages nobody will read
-    for (int k = it; k < it_pf; ++k) ptx::mbar_wait_bounded(&full[k % p.stages], (k / p.stages) & 1, WAIT_BUDGET);
+    Cursor d;
+    d.init(p, first, last);
+    for (int64_t j = 0; j < issued; ++j, d.next(p))
+      if (j >= done) ptx::mbar_wait_bounded(&full[d.s], d.ph, WAIT_BUDGET);
   }
 }
 
@@ -286,8 +326,10 @@ __device__ __forceinline__ void reset(WarpState &st) {
     for (int j = 0; j < 4; ++j) st.o[i][j] = 0.f;
 }
 
-// Merge the consumer warps' states into one partial per item (real heads only).
-__device__ void flush_item(const Params &p, unsigned char *smem, WarpState &st, int item, int warp, int lane) {
+// Merge the consumer warps' states into one partial (real heads only) in
+// slot `slot` of the workspace.
+template <int NW>
+__device__ void flush_partial(const Params &p, unsigned char *smem, WarpState &st, int64_t slot, int warp, int lane) {
   const int g = lane >> 2, t = lane & 3;
   const int G = p.gqa;
   float l0 = st.l[0], l1 = st.l[1];
@@ -322,7 +364,6 @@ __device__ void flush_item(const Params &p, unsigned char *smem, WarpState &st, 
     }
   }
   ptx::named_barrier_sync(1, NW * 32);
-  // thread -> (head, dim): NW*32 = 256 threads cover 2 heads x 128 dims per round
   for (int idx = threadIdx.x; idx < G * HD; idx += NW * 32) {
     const int hh = idx / HD, d = idx - (idx / HD) * HD;
     float M = -INFINITY;
@@ -336,46 +377,45 @@ __device__ void flush_item(const Params &p, unsigned char *smem, WarpState &st, 
       L += wl[w * 8 + hh] * f;
       acc += wo[(w * G + hh) * HD + d] * f;
     }
-    p.ws_o[((int64_t)item * 8 + hh) * HD + d] = acc;
+    p.ws_o[(slot * 8 + hh) * HD + d] = acc;
     if (d == 0) {
-      p.ws_m[(int64_t)item * 8 + hh] = M;
-      p.ws_l[(int64_t)item * 8 + hh] = L;
+      p.ws_m[slot * 8 + hh] = M;
+      p.ws_l[slot * 8 + hh] = L;
     }
   }
   ptx::named_barrier_sync(1, NW * 32);
   reset(st);
 }
 
-__device__ __forceinline__ void process_tile(const Params &p, WarpState &st, const uint32_t *tab, const float *qa,
-                                             const unsigned char *cdK, const __half *scK, const unsigned char *kfV,
-                                             const unsigned char *cdV, const __half *scV, const uint32_t (&qB)[4][4],
-                                             int tb, int nvalid, int lane) {
+__device__ __forceinline__ void process_tile(WarpState &st, const uint2 *tab, const float2 *sc, const float *qa,
+                                             const unsigned char *cdK, const unsigned char *kfV,
+                                             const unsigned char *cdV, const uint32_t (&qB)[4][4], float2 qc, int tb,
+                                             int nvalid, int lane) {
   const int g = lane >> 2, t = lane & 3;
   // ---------------- scores S^T[token][head] = q.codes (MMA), then anchors + scale
-  const uint32_t e0 = tab[tb + g], e1 = tab[tb + g + 8];
-  const int pk0 = e0 & 0xff, pk1 = e1 & 0xff;
-  const int rk0 = (pk0 == 255) ? 0 : pk0, rk1 = (pk1 == 255) ? 0 : pk1;
-  const uint4 wk0 = *(const uint4 *)(cdK + rk0 * 64 + t * 16);
-  const uint4 wk1 = *(const uint4 *)(cdK + rk1 * 64 + t * 16);
+  const uint32_t e0 = tab[tb + g].x, e1 = tab[tb + g + 8].x;
+  const uint4 wk0 = *(const uint4 *)(cdK + (e0 & TAB_OFF) + t * 16);
+  const uint4 wk1 = *(const uint4 *)(cdK + (e1 & TAB_OFF) + t * 16);
   float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
   {
+    // raw nibble values (1024+n, 1024+16n) against q (q/16 on the 16n lanes):
+    // q . codes = result - qc, qc = the same product for the all-8 word
     const uint32_t w0[4] = {wk0.x, wk0.y, wk0.z, wk0.w};
     const uint32_t w1[4] = {wk1.x, wk1.y, wk1.z, wk1.w};
 #pragma unroll
     for (int J = 0; J < 4; ++J) {
       uint32_t h0[4], h1[4];
-      ptx::nibbles_to_half2(w0[J], h0);  // (d0,d4) (d1,d5) (d2,d6) (d3,d7)
-      ptx::nibbles_to_half2(w1[J], h1);
+      ptx::nibbles_to_half2_raw(w0[J], h0);  // (d0,d4) (d1,d5) (d2,d6) (d3,d7)
+      ptx::nibbles_to_half2_raw(w1[J], h1);
       ptx::mma_f16_16816(ca, h0[0], h1[0], h0[1], h1[1], qB[J][0], qB[J][1]);
       ptx::mma_f16_16816(cb, h0[2], h1[2], h0[3], h1[3], qB[J][2], qB[J][3]);
     }
   }
-  const float sk0 = (pk0 == 255) ? 0.f : __half2float(scK[rk0]) * LOG2E;
-  const float sk1 = (pk1 == 255) ? 0.f : __half2float(scK[rk1]) * LOG2E;
-  const float2 qa0 = *(const float2 *)(qa + ((e0 >> 8) & 0xff) * 8 + 2 * t);
-  const float2 qa1 = *(const float2 *)(qa + ((e1 >> 8) & 0xff) * 8 + 2 * t);
-  float s0 = fmaf(sk0, ca[0] + cb[0], qa0.x), s1 = fmaf(sk0, ca[1] + cb[1], qa0.y);
-  float s2 = fmaf(sk1, ca[2] + cb[2], qa1.x), s3 = fmaf(sk1, ca[3] + cb[3], qa1.y);
+  const float2 sc0 = sc[tb + g], sc1 = sc[tb + g + 8];  // (K scale * log2 e, V scale), 0 on I-frames
+  const float2 qa0 = *(const float2 *)((const unsigned char *)qa + (e0 >> 16) + t * 8);
+  const float2 qa1 = *(const float2 *)((const unsigned char *)qa + (e1 >> 16) + t * 8);
+  float s0 = fmaf(sc0.x, (ca[0] + cb[0]) - qc.x, qa0.x), s1 = fmaf(sc0.x, (ca[1] + cb[1]) - qc.y, qa0.y);
+  float s2 = fmaf(sc1.x, (ca[2] + cb[2]) - qc.x, qa1.x), s3 = fmaf(sc1.x, (ca[3] + cb[3]) - qc.y, qa1.y);
   if (tb + g >= nvalid) s0 = s1 = -INFINITY;
   if (tb + g + 8 >= nvalid) s2 = s3 = -INFINITY;
 
@@ -414,20 +454,17 @@ __device__ __forceinline__ void process_tile(const Params &p, WarpState &st, con
   st.l[1] += p1 + p3;
 
   // ---------------- P (anchor term) and P' = P * scale_v (code term) as B operands
-  const int pv0 = (e0 >> 16) & 0xff, pv1 = (e1 >> 16) & 0xff;
-  const float sv0 = (pv0 == 255) ? 0.f : __half2float(scV[pv0]);
-  const float sv1 = (pv1 == 255) ? 0.f : __half2float(scV[pv1]);
   const uint32_t bP0 = ptx::movmatrix_trans(ptx::pack_half2(p0, p1));
   const uint32_t bP1 = ptx::movmatrix_trans(ptx::pack_half2(p2, p3));
-  const uint32_t bS0 = ptx::movmatrix_trans(ptx::pack_half2(p0 * sv0, p1 * sv0));
-  const uint32_t bS1 = ptx::movmatrix_trans(ptx::pack_half2(p2 * sv1, p3 * sv1));
+  const uint32_t bS0 = ptx::movmatrix_trans(ptx::pack_half2(p0 * sc0.y, p1 * sc0.y));
+  const uint32_t bS1 = ptx::movmatrix_trans(ptx::pack_half2(p2 * sc1.y, p3 * sc1.y));
 
   // ---------------- V anchors: O += A_v^T P  (ldmatrix.trans gathers each token's anchor)
   {
     const int mi = lane >> 3, r = lane & 7;
     const int tok = tb + r + ((mi & 2) ? 8 : 0);
-    const int av = (tok < nvalid) ? (int)(tab[tok] >> 24) : 0;
-    const uint32_t base = ptx::smem_u32(kfV + av * (HD * 2) + ((mi & 1) ? 16 : 0));
+    const uint32_t aoff = (tok < nvalid) ? (tab[tok].y >> 16) : 0u;
+    const uint32_t base = ptx::smem_u32(kfV + aoff + ((mi & 1) ? 16 : 0));
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       uint32_t a0, a1, a2, a3;
@@ -437,18 +474,12 @@ __device__ __forceinline__ void process_tile(const Params &p, WarpState &st, con
   }
   // ---------------- V codes: O += C_v^T P'  (tokens 2t,2t+1 | 2t+8,2t+9; words 2g, 2g+1)
   {
-    const uint2 ea = *(const uint2 *)(tab + tb + 2 * t);
-    const uint2 ec = *(const uint2 *)(tab + tb + 2 * t + 8);
-    int ra = (ea.x >> 16) & 0xff, rb = (ea.y >> 16) & 0xff;
-    int rc = (ec.x >> 16) & 0xff, rd = (ec.y >> 16) & 0xff;
-    ra = (ra == 255) ? 0 : ra;
-    rb = (rb == 255) ? 0 : rb;
-    rc = (rc == 255) ? 0 : rc;
-    rd = (rd == 255) ? 0 : rd;
-    const uint2 va = *(const uint2 *)(cdV + ra * 64 + g * 8);
-    const uint2 vb = *(const uint2 *)(cdV + rb * 64 + g * 8);
-    const uint2 vc = *(const uint2 *)(cdV + rc * 64 + g * 8);
-    const uint2 vd = *(const uint2 *)(cdV + rd * 64 + g * 8);
+    const uint4 ev = *(const uint4 *)(tab + tb + 2 * t);      // entries of tokens 2t, 2t+1
+    const uint4 ew = *(const uint4 *)(tab + tb + 2 * t + 8);  // entries of tokens 2t+8, 2t+9
+    const uint2 va = *(const uint2 *)(cdV + (ev.y & TAB_OFF) + g * 8);
+    const uint2 vb = *(const uint2 *)(cdV + (ev.w & TAB_OFF) + g * 8);
+    const uint2 vc = *(const uint2 *)(cdV + (ew.y & TAB_OFF) + g * 8);
+    const uint2 vd = *(const uint2 *)(cdV + (ew.w & TAB_OFF) + g * 8);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const uint32_t wa = q ? va.y : va.x, wb = q ? vb.y : vb.x;
@@ -468,65 +499,73 @@ __device__ __forceinline__ void process_tile(const Params &p, WarpState &st, con
   }
 }
 
+template <int NW>
 __device__ void consumer(const Params &p, unsigned char *smem, uint64_t *full, uint64_t *empty, uint64_t *ready,
                          int warp, int lane) {
   const CacheView &cv = p.cv;
   const int g = lane >> 2, t = lane & 3;
-  const uint32_t *tab = (const uint32_t *)(smem + p.off_tab);
+  const uint2 *tab = (const uint2 *)(smem + p.off_tab);
   const int tiles_page = cv.P / 16;
   const int tile0 = warp * p.tpw;
   const int tile1 = min(tile0 + p.tpw, tiles_page);
 
   WarpState st;
   reset(st);
-  int first, last;
-  my_items(p, first, last);
-  PageIter pi;
-  pi.init(p, first, last);
+  int64_t first, last;
+  my_pages(p, first, last);
   int cur_unit = -1;
-  uint32_t qB[4][4];  // query in the K-code order (k-permuted)
-  for (int it = 0; pi.valid(); ++it, pi.next()) {
-    const PageRef r = pi.get();
-    if (r.unit != cur_unit) {
-      cur_unit = r.unit;
-      const int hq = r.h * p.gqa + g;
+  uint32_t qB[4][4];  // query in the K-code order (k-permuted); lanes paired with 16n values carry q/16
+  float2 qc = make_float2(0.f, 0.f);  // q . (raw values of code 0) for heads 2t, 2t+1
+  Cursor cu;
+  for (cu.init(p, first, last); cu.valid(); cu.next(p)) {
+    if (cu.unit != cur_unit) {
+      cur_unit = cu.unit;
+      const int hq = cu.h * p.gqa + g;
       const bool real = g < p.gqa;
+      float cc[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
       for (int J = 0; J < 4; ++J) {
         const int d0 = 32 * t + 8 * J;
         float v[8];
 #pragma unroll
-        for (int i = 0; i < 8; ++i) v[i] = real ? q_scaled(p, r.b, hq, d0 + i) : 0.f;
+        for (int i = 0; i < 8; ++i) v[i] = real ? q_scaled(p, cu.b, hq, d0 + i) : 0.f;
         qB[J][0] = ptx::pack_half2(v[0], v[4]);
-        qB[J][1] = ptx::pack_half2(v[1], v[5]);
+        qB[J][1] = ptx::pack_half2(v[1] * 0.0625f, v[5] * 0.0625f);
         qB[J][2] = ptx::pack_half2(v[2], v[6]);
-        qB[J][3] = ptx::pack_half2(v[3], v[7]);
+        qB[J][3] = ptx::pack_half2(v[3] * 0.0625f, v[7] * 0.0625f);
+        ptx::mma_f16_16816(cc, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_HI, ptx::RAW_CODE0_HI, qB[J][0],
+                           qB[J][1]);
+        ptx::mma_f16_16816(cc, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_HI, ptx::RAW_CODE0_HI, qB[J][2],
+                           qB[J][3]);
       }
+      qc = make_float2(cc[0], cc[1]);
     }
-    const int s = it % p.stages;
+    const int s = cu.s;
     // the bulk copies' own barrier makes their bytes visible to this thread;
-    // `ready` adds the producer's q.anchor rows
-    if (!ptx::mbar_wait_bounded(&full[s], (it / p.stages) & 1, WAIT_BUDGET) ||
-        !ptx::mbar_wait_bounded(&ready[s], (it / p.stages) & 1, WAIT_BUDGET)) {
+    // `ready` adds the producer's q.anchor rows and per-token scales
+    if (!ptx::mbar_wait_bounded(&full[s], cu.ph, WAIT_BUDGET) || !ptx::mbar_wait_bounded(&ready[s], cu.ph, WAIT_BUDGET)) {
       atomicExch(&g_fast_error, ERR_TIMEOUT_FULL);
       return;
     }
-    const int nvalid = (int)min((int64_t)cv.P, p.T - (int64_t)r.lp * cv.P);
+    const int nvalid = cu.nvalid(p);
     const unsigned char *stage = smem + p.off_stage + s * p.stage_bytes;
     const float *qa = (const float *)(smem + p.off_qa) + s * p.qa_rows * 8;
+    const float2 *sc = (const float2 *)(smem + p.off_sc) + s * cv.P;
     for (int tile = tile0; tile < tile1; ++tile) {
       const int tb = tile * 16;
       if (tb >= nvalid) break;
-      process_tile(p, st, tab, qa, stage + p.st_cd[0], (const __half *)(stage + p.st_sc[0]), stage + p.st_kf[1],
-                   stage + p.st_cd[1], (const __half *)(stage + p.st_sc[1]), qB, tb, nvalid, lane);
+      process_tile(st, tab, sc, qa, stage + p.st_cd[0], stage + p.st_kf[1], stage + p.st_cd[1], qB, qc, tb, nvalid,
+                   lane);
     }
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&empty[s]);
-    if (r.last_in_item) flush_item(p, smem, st, r.item, warp, lane);
+    if (cu.last_in_seg(p)) flush_partial<NW>(p, smem, st, (int64_t)blockIdx.x * p.smax + cu.seg, warp, lane);
   }
 }
 
-__global__ void __launch_bounds__(NT, 2) decode_kernel(const __grid_constant__ Params p) {
+template <int NW>
+__global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) decode_kernel(const __grid_constant__ Params p) {
+  constexpr int NT = (NW + 1) * 32;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t *full = (uint64_t *)smem;
   uint64_t *empty = full + p.stages;
@@ -540,35 +579,50 @@ __global__ void __launch_bounds__(NT, 2) decode_kernel(const __grid_constant__ P
     }
     ptx::fence_mbar_init();
   }
-  uint32_t *tab = (uint32_t *)(smem + p.off_tab);
+  uint2 *tab = (uint2 *)(smem + p.off_tab);
   for (int i = threadIdx.x; i < p.cv.P; i += NT) tab[i] = tab_entry(i, p.cv.c[0].stride, p.cv.c[1].stride);
   __syncthreads();
   if (warp == NW) {
     producer(p, smem, full, empty, ready, lane);
     return;
   }
-  consumer(p, smem, full, empty, ready, warp, lane);
+  consumer<NW>(p, smem, full, empty, ready, warp, lane);
 }
 
-// Merge the item partials of one (sequence, query head) row: one CTA of 128
-// threads per row, thread = output dim.  The per-item weights exp2(m_i - M)/L
-// are computed once into shared memory, then every thread streams its dim of
-// the item outputs with independent loads.
-constexpr int kCombineMaxItems = 1024;
+// Merge the partials of one (sequence, query head) row: one CTA of 128
+// threads per row, thread = output dim.  The row's unit spans the page
+// ranges of CTAs c_lo..c_hi; CTA c holds the unit's partial in slot
+// c*smax + (unit - first unit of c).  Weights exp2(m_i - M) are computed once
+// into shared memory, then every thread streams its dim with independent loads.
+constexpr int kCombineMaxParts = 1024;
 
-__global__ void __launch_bounds__(HD) fast_combine(const float *ws_m, const float *ws_l, const float *ws_o, int ipu,
-                                                   int H, int gqa, int Hq, void *out, int out_dtype, float *lse_out) {
-  __shared__ float s_w[kCombineMaxItems];
+__device__ __forceinline__ int64_t cta_of_page(int64_t x, int64_t tp, int grid) {
+  return ((x + 1) * grid + tp - 1) / tp - 1;
+}
+
+__global__ void __launch_bounds__(HD) fast_combine(const float *ws_m, const float *ws_l, const float *ws_o,
+                                                   int64_t tp, int npu, int grid, int smax, int H, int gqa, int Hq,
+                                                   void *out, int out_dtype, float *lse_out) {
+  __shared__ float s_w[kCombineMaxParts];
+  __shared__ int64_t s_slot[kCombineMaxParts];
   __shared__ float s_red[HD / 32];
   __shared__ float s_ML[2];
   const int row = blockIdx.x;  // b * Hq + hq
   const int b = row / Hq, hq = row - (row / Hq) * Hq;
   const int u = b * H + hq / gqa, hh = hq % gqa;
-  const int64_t i0 = (int64_t)u * ipu;
+  const int64_t c_lo = cta_of_page((int64_t)u * npu, tp, grid);
+  const int64_t c_hi = cta_of_page((int64_t)u * npu + npu - 1, tp, grid);
+  const int np = (int)(c_hi - c_lo + 1);
   const int d = threadIdx.x, lane = d & 31, warp = d >> 5;
-  // pass 1: max over items
+  // pass 1: slots and max
   float M = -INFINITY;
-  for (int j = d; j < ipu; j += HD) M = fmaxf(M, ws_m[(i0 + j) * 8 + hh]);
+  for (int j = d; j < np; j += HD) {
+    const int64_t c = c_lo + j;
+    const int64_t first = c * tp / grid;
+    const int64_t slot = c * smax + (u - first / npu);
+    s_slot[j] = slot;
+    M = fmaxf(M, ws_m[slot * 8 + hh]);
+  }
   M = warp_max(M);
   if (lane == 0) s_red[warp] = M;
   __syncthreads();
@@ -581,11 +635,12 @@ __global__ void __launch_bounds__(HD) fast_combine(const float *ws_m, const floa
   M = s_ML[0];
   // pass 2: weights and the denominator
   float L = 0.f;
-  for (int j = d; j < ipu; j += HD) {
-    const float m = ws_m[(i0 + j) * 8 + hh];
+  for (int j = d; j < np; j += HD) {
+    const int64_t slot = s_slot[j];
+    const float m = ws_m[slot * 8 + hh];
     const float f = (m == -INFINITY) ? 0.f : exp2f(m - M);
     s_w[j] = f;
-    L += ws_l[(i0 + j) * 8 + hh] * f;
+    L += ws_l[slot * 8 + hh] * f;
   }
   L = warp_sum(L);
   __syncthreads();
@@ -598,18 +653,15 @@ __global__ void __launch_bounds__(HD) fast_combine(const float *ws_m, const floa
   }
   __syncthreads();
   L = s_ML[1];
-  // pass 3: weighted sum of the item outputs
-  const float *o = ws_o + (i0 * 8 + hh) * HD + d;
-  float a0 = 0.f, a1 = 0.f, a2 = 0.f, a3 = 0.f;
+  // pass 3: weighted sum of the partial outputs
+  float a0 = 0.f, a1 = 0.f;
   int j = 0;
-  for (; j + 4 <= ipu; j += 4) {
-    a0 += o[(int64_t)(j + 0) * 8 * HD] * s_w[j + 0];
-    a1 += o[(int64_t)(j + 1) * 8 * HD] * s_w[j + 1];
-    a2 += o[(int64_t)(j + 2) * 8 * HD] * s_w[j + 2];
-    a3 += o[(int64_t)(j + 3) * 8 * HD] * s_w[j + 3];
+  for (; j + 2 <= np; j += 2) {
+    a0 += ws_o[(s_slot[j] * 8 + hh) * HD + d] * s_w[j];
+    a1 += ws_o[(s_slot[j + 1] * 8 + hh) * HD + d] * s_w[j + 1];
   }
-  for (; j < ipu; ++j) a0 += o[(int64_t)j * 8 * HD] * s_w[j];
-  const float acc = (a0 + a1) + (a2 + a3);
+  if (j < np) a0 += ws_o[(s_slot[j] * 8 + hh) * HD + d] * s_w[j];
+  const float acc = a0 + a1;
   store_from_float(out, (int64_t)row * HD + d, (L > 0.f) ? acc / L : 0.f, out_dtype);
   if (lse_out && d == 0) lse_out[row] = (L > 0.f) ? (M + log2f(L)) * LN2 : -INFINITY;
 }
@@ -618,13 +670,13 @@ __global__ void __launch_bounds__(HD) fast_combine(const float *ws_m, const floa
 // host side
 // ---------------------------------------------------------------------------
 struct Layout {
-  int stages, stage_bytes, off_tab, off_qa, off_merge, off_stage, total, qa_rows;
+  int stages, stage_bytes, off_tab, off_qa, off_sc, off_merge, off_stage, total, qa_rows;
   int st_kf[2], st_cd[2], st_sc[2];
 };
 
 static inline int up128(int x) { return (x + 127) & ~127; }
 
-static Layout make_layout(const cq_paged_cache &c, int stages, int gqa) {
+static Layout make_layout(const cq_paged_cache &c, int stages, int gqa, int NW) {
   Layout L;
   const cq_component *cc[2] = {&c.k, &c.v};
   int off = 0;
@@ -640,8 +692,9 @@ static Layout make_layout(const cq_paged_cache &c, int stages, int gqa) {
   L.stages = stages;
   L.qa_rows = ((c.k.anchors_per_page + 15) / 16) * 16;
   L.off_tab = 128;  // mbarriers live in the first 128 bytes
-  L.off_qa = up128(L.off_tab + c.page_tokens * 4);
-  L.off_merge = up128(L.off_qa + stages * L.qa_rows * 8 * 4);
+  L.off_qa = up128(L.off_tab + c.page_tokens * 8);
+  L.off_sc = up128(L.off_qa + stages * L.qa_rows * 8 * 4);
+  L.off_merge = up128(L.off_sc + stages * c.page_tokens * 8);
   L.off_stage = up128(L.off_merge + (NW * 8 * 2 + NW * gqa * HD) * 4);
   L.total = L.off_stage + stages * L.stage_bytes;
   return L;
@@ -650,17 +703,19 @@ static Layout make_layout(const cq_paged_cache &c, int stages, int gqa) {
 static constexpr int kMaxSmem = 227 * 1024;
 static constexpr int kSmPerSm = 228 * 1024;
 
-static int pick_stages(const cq_paged_cache &c, int gqa, int &per_sm) {
-  // prefer two CTAs per SM (16 consumer warps), then the deepest pipeline
-  for (int s = 4; s >= 2; --s) {
-    Layout L = make_layout(c, s, gqa);
-    if (2 * (L.total + 1024) <= kSmPerSm) {
-      per_sm = 2;
-      return s;
+static int pick_stages(const cq_paged_cache &c, int gqa, int NW, int &per_sm) {
+  if (NW == 8) {  // two CTAs per SM when they fit
+    for (int s = 4; s >= 2; --s) {
+      Layout L = make_layout(c, s, gqa, NW);
+      if (2 * (L.total + 1024) <= kSmPerSm) {
+        per_sm = 2;
+        return s;
+      }
     }
   }
+  // one CTA per SM with the deepest pipeline that fits
   for (int s = 4; s >= 2; --s) {
-    Layout L = make_layout(c, s, gqa);
+    Layout L = make_layout(c, s, gqa, NW);
     if (L.total <= kMaxSmem) {
       per_sm = 1;
       return s;
@@ -685,37 +740,59 @@ bool fast_decode_supported(const cq_paged_cache &c, int n_q_heads, int q_len) {
       !aligned16(c.k.scales) || !aligned16(c.v.scales))
     return false;
   int per_sm;
-  return pick_stages(c, gqa, per_sm) >= 2;
-}
-
-static int items_plan(const cq_paged_cache &c, int64_t T, int splits_req, int &ppi, int &ipu) {
-  const int npu = (int)((T + c.page_tokens - 1) / c.page_tokens);
-  ppi = 2;
-  if (splits_req > 0) ppi = std::max(1, (npu + splits_req - 1) / splits_req);
-  ppi = std::max(ppi, (npu + kCombineMaxItems - 1) / kCombineMaxItems);  // the combine holds <= 1024 weights
-  ipu = (npu + ppi - 1) / ppi;
-  return npu;
-}
-
-size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len, int splits_req) {
-  if (!fast_decode_supported(c, n_q_heads, q_len)) return 0;
-  int ppi, ipu;
-  items_plan(c, T, splits_req, ppi, ipu);
-  const size_t items = (size_t)c.batch * c.kv_heads * ipu;
-  return items * 8 * (2 + HD) * sizeof(float);
+  return pick_stages(c, gqa, kMaxNW, per_sm) >= 2;
 }
 
 static int sm_count() {
   static int n[64] = {};
   int dev = 0;
-  cudaGetDevice(&dev);
-  if (dev < 0 || dev >= 64) return 148;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) {
+    cudaGetLastError();
+    return 148;
+  }
   if (!n[dev]) {
     int v = 0;
-    cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev);
+    if (cudaDeviceGetAttribute(&v, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess) cudaGetLastError();
     n[dev] = v > 0 ? v : 148;
   }
   return n[dev];
+}
+
+struct Plan {
+  int npu, grid, smax, stages, per_sm, nw;
+  int64_t tp;
+};
+
+// Consumer warps per CTA: 8 by default (two CTAs per SM); CQ_DECODE_WARPS=16
+// selects one 16-warp CTA per SM (a tuning knob, same results).
+static int pick_nw() {
+  static int nw = 0;
+  if (!nw) {
+    const char *e = getenv("CQ_DECODE_WARPS");
+    nw = (e && atoi(e) == 16) ? 16 : 8;
+  }
+  return nw;
+}
+
+static Plan make_plan(const cq_paged_cache &c, int64_t T, int gqa, int splits_req) {
+  Plan pl;
+  pl.npu = (int)((T + c.page_tokens - 1) / c.page_tokens);
+  const int64_t units = (int64_t)c.batch * c.kv_heads;
+  pl.tp = units * pl.npu;
+  pl.nw = pick_nw();
+  pl.stages = pick_stages(c, gqa, pl.nw, pl.per_sm);
+  int64_t g = (int64_t)sm_count() * std::max(1, pl.per_sm);
+  if (splits_req > 0) g = std::min<int64_t>(g, units * splits_req);
+  pl.grid = (int)std::max<int64_t>(1, std::min<int64_t>(g, pl.tp));
+  const int64_t ppc = (pl.tp + pl.grid - 1) / pl.grid;  // pages per CTA, at most
+  pl.smax = (int)((ppc + pl.npu - 1) / pl.npu + 1);
+  return pl;
+}
+
+size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len, int splits_req) {
+  if (!fast_decode_supported(c, n_q_heads, q_len)) return 0;
+  const Plan pl = make_plan(c, T, n_q_heads / c.kv_heads, splits_req);
+  return (size_t)pl.grid * pl.smax * 8 * (2 + HD) * sizeof(float);
 }
 
 int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, const void *q, int q_dtype,
@@ -730,16 +807,17 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
   p.scale = scale;
   p.gqa = n_q_heads / c.kv_heads;
   p.T = T;
-  p.n_pages_unit = items_plan(c, T, splits_req, p.ppi, p.ipu);
-  p.n_items = c.batch * c.kv_heads * p.ipu;
-  int per_sm = 0;
-  const int stages = pick_stages(c, p.gqa, per_sm);
-  Layout L = make_layout(c, stages, p.gqa);
-  p.stages = stages;
-  p.tpw = (c.page_tokens / 16 + NW - 1) / NW;
+  const Plan pl = make_plan(c, T, p.gqa, splits_req);
+  p.npu = pl.npu;
+  p.tp = pl.tp;
+  p.smax = pl.smax;
+  Layout L = make_layout(c, pl.stages, p.gqa, pl.nw);
+  p.stages = pl.stages;
+  p.tpw = (c.page_tokens / 16 + pl.nw - 1) / pl.nw;
   p.qa_rows = L.qa_rows;
   p.off_tab = L.off_tab;
   p.off_qa = L.off_qa;
+  p.off_sc = L.off_sc;
   p.off_merge = L.off_merge;
   p.off_stage = L.off_stage;
   p.stage_bytes = L.stage_bytes;
@@ -748,31 +826,46 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
     p.st_cd[i] = L.st_cd[i];
     p.st_sc[i] = L.st_sc[i];
   }
-  const size_t need = (size_t)p.n_items * 8 * (2 + HD) * sizeof(float);
+  {
+    const cq_component *cc[2] = {&c.k, &c.v};
+    p.full_total = 0;
+    for (int i = 0; i < 2; ++i) {
+      p.full_bytes[i * 3 + 0] = (uint32_t)cc[i]->anchors_per_page * HD * 2;
+      p.full_bytes[i * 3 + 1] = (uint32_t)cc[i]->pframes_per_page * (HD / 8) * 4;
+      p.full_bytes[i * 3 + 2] = (uint32_t)((cc[i]->pframes_per_page * 2 + 15) & ~15);
+      for (int j = 0; j < 3; ++j) p.full_total += p.full_bytes[i * 3 + j];
+    }
+  }
+  const size_t slots = (size_t)pl.grid * pl.smax;
+  const size_t need = slots * 8 * (2 + HD) * sizeof(float);
   CQ_REQUIRE(ws && ws_bytes >= need, CQ_ERR_WORKSPACE, "cq_attention: workspace too small");
   p.ws_m = (float *)ws;
-  p.ws_l = p.ws_m + (size_t)p.n_items * 8;
-  p.ws_o = p.ws_l + (size_t)p.n_items * 8;
+  p.ws_l = p.ws_m + slots * 8;
+  p.ws_o = p.ws_l + slots * 8;
 
   static std::mutex mu;
-  static bool attr_set[64] = {};
+  static bool attr_set[64][2] = {};
   {
     int dev = 0;
     cudaGetDevice(&dev);
+    const int v = pl.nw == 8 ? 1 : 0;
     std::lock_guard<std::mutex> lk(mu);
-    if (dev < 0 || dev >= 64 || !attr_set[dev]) {
-      cudaError_t e = cudaFuncSetAttribute(decode_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+    if (dev < 0 || dev >= 64 || !attr_set[dev][v]) {
+      cudaError_t e = v ? cudaFuncSetAttribute(decode_kernel<8>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)
+                        : cudaFuncSetAttribute(decode_kernel<16>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
       if (e != cudaSuccess)
         return set_error(CQ_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
-      if (dev >= 0 && dev < 64) attr_set[dev] = true;
+      if (dev >= 0 && dev < 64) attr_set[dev][v] = true;
     }
   }
-  const int grid = std::min(p.n_items, sm_count() * per_sm);
-  decode_kernel<<<grid, NT, L.total, st>>>(p);
+  if (pl.nw == 8)
+    decode_kernel<8><<<pl.grid, 9 * 32, L.total, st>>>(p);
+  else
+    decode_kernel<16><<<pl.grid, 17 * 32, L.total, st>>>(p);
   int r = check_launch("decode_kernel");
   if (r) return r;
-  fast_combine<<<c.batch * n_q_heads, HD, 0, st>>>(p.ws_m, p.ws_l, p.ws_o, p.ipu, c.kv_heads, p.gqa, n_q_heads,
-                                                    out, out_dtype, lse_out);
+  fast_combine<<<c.batch * n_q_heads, HD, 0, st>>>(p.ws_m, p.ws_l, p.ws_o, pl.tp, pl.npu, pl.grid, pl.smax,
+                                                    c.kv_heads, p.gqa, n_q_heads, out, out_dtype, lse_out);
   return check_launch("fast_combine");
 }
 

@@ -43,14 +43,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Bounded wait: gives up after `budget` clock cycles and returns false.
+// try_wait with a suspend-time hint: the warp sleeps (up to `ns`) until the
+// phase completes instead of spinning.
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t *bar, uint32_t parity, uint32_t ns) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(ns)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded wait: gives up after `budget` clock cycles and returns false.  The
+// clock is read once per 16 suspended tries.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity, long long budget) {
   if (mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
-  while (!mbar_try_wait(bar, parity)) {
+  for (;;) {
+#pragma unroll 1
+    for (int i = 0; i < 16; ++i)
+      if (mbar_try_wait_sleep(bar, parity, 1000u)) return true;
     if (clock64() - t0 > budget) return false;
   }
-  return true;
 }
 
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
@@ -129,6 +146,23 @@ __device__ __forceinline__ void nibbles_to_half2(uint32_t x, uint32_t (&out)[4])
   out[2] = h22u(__hsub2(u2h2(lo1), BIAS_LO));
   out[3] = h22u(__hfma2(u2h2(hi1), SCALE_HI, BIAS_HI));
 }
+
+// Raw form of nibbles_to_half2 without the bias removal: out[0], out[2] hold
+// 1024 + n (nibbles 0 and 2 of each 16-bit half), out[1], out[3] hold 1024 + 16n
+// (nibbles 1 and 3).  A dot product with these values equals the dot product
+// with the codes n - 8 plus a constant that does not depend on the codes; the
+// caller removes that constant (computed from the all-8 nibble pattern).
+__device__ __forceinline__ void nibbles_to_half2_raw(uint32_t x, uint32_t (&out)[4]) {
+  const uint32_t MAGIC = 0x64006400u;
+  out[0] = lop3_and_or(x, 0x000f000fu, MAGIC);
+  out[1] = lop3_and_or(x, 0x00f000f0u, MAGIC);
+  const uint32_t x8 = x >> 8;
+  out[2] = lop3_and_or(x8, 0x000f000fu, MAGIC);
+  out[3] = lop3_and_or(x8, 0x00f000f0u, MAGIC);
+}
+
+// The raw values of the all-8 nibble word (code 0): 1032 and 1152 = 1024 + 16*8.
+constexpr uint32_t RAW_CODE0_LO = 0x64086408u, RAW_CODE0_HI = 0x64806480u;
 
 __device__ __forceinline__ uint32_t pack_half2(float lo, float hi) { return h22u(__floats2half2_rn(lo, hi)); }
 
