@@ -199,7 +199,7 @@ def run_ours(args, cfg):
     K, V = ar1_host(B, H, T0 + 2 * n_new, D, cfg["rho_k"], cfg["rho_v"], seed=1000 + rank)
     cache = ChronoQuantCache(stride_k=cfg["stride_k"], stride_v=cfg["stride_v"], delta_bits_k=cfg["bits_k"],
                              delta_bits_v=cfg["bits_v"], dead_zone_k=cfg["dz_k"], dead_zone_v=cfg["dz_v"],
-                             max_tokens=T0 + 2 * n_new + 8)
+                             max_tokens=T0 + 2 * n_new + 8, page_tokens=args.page_tokens)
     # prefill (untimed) in chunks
     for t in range(0, T0, 4096):
         n = min(4096, T0 - t)
@@ -317,6 +317,7 @@ def run_ours(args, cfg):
             "config": {"workload": cfg["name"], "batch": B, "q_heads": Hq, "kv_heads": H, "head_dim": D,
                        "context_tokens_start": T_start, "stride_k": cfg["stride_k"], "stride_v": cfg["stride_v"],
                        "bits_k": cfg["bits_k"], "bits_v": cfg["bits_v"], "dead_zone_v": cfg["dz_v"],
+                       "page_tokens": cache.page_tokens,
                        "step": "append 1 token (encode) + decode attention",
                        "l2": "cache active bytes %.0f MB per GPU > 126 MB L2; no flush" %
                              (active_bytes(B, H, T_start, D, cfg["stride_k"], cfg["stride_v"]) / 1e6),
@@ -460,6 +461,7 @@ def main():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
+    ap.add_argument("--page-tokens", type=int, default=None, help="cache page size (default: the cache's choice)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3

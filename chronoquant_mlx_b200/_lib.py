@@ -22,6 +22,7 @@ CQ_ERR_WORKSPACE = -4
 
 CQ_F16, CQ_BF16, CQ_F32 = 0, 1, 2
 CQ_ORDER_NATURAL, CQ_ORDER_MMA = 0, 1
+CQ_SCALE_BY_PFRAME, CQ_SCALE_BY_TOKEN = 0, 1
 
 EXPORTED = [
     "cq_abi_version", "cq_last_error", "cq_device_error", "cq_append", "cq_attention", "cq_attention_workspace",
@@ -35,7 +36,7 @@ class CqComponent(ctypes.Structure):
     _fields_ = [
         ("stride", ctypes.c_int32), ("bits", ctypes.c_int32), ("dead_zone", ctypes.c_float),
         ("anchors_per_page", ctypes.c_int32), ("pframes_per_page", ctypes.c_int32),
-        ("scale_row", ctypes.c_int32), ("code_order", ctypes.c_int32), ("_pad", ctypes.c_int32),
+        ("scale_row", ctypes.c_int32), ("code_order", ctypes.c_int32), ("scale_index", ctypes.c_int32),
         ("keyframes", ctypes.c_void_p), ("codes", ctypes.c_void_p), ("scales", ctypes.c_void_p),
     ]
 

@@ -38,6 +38,7 @@ def _dense_descriptor(k: torch.Tensor, v: torch.Tensor, table: torch.Tensor) -> 
         c.stride, c.bits, c.dead_zone = 1, 4, 0.0
         c.anchors_per_page, c.pframes_per_page, c.scale_row = T, 0, 0
         c.code_order = _lib.CQ_ORDER_NATURAL
+        c.scale_index = _lib.CQ_SCALE_BY_PFRAME
         c.keyframes, c.codes, c.scales = t.data_ptr(), None, None
     return d
 

@@ -63,7 +63,7 @@ class _Component:
         self.dead_zone = float(dead_zone)
         self.apg = page_tokens // stride
         self.ppg = page_tokens - self.apg
-        self.srow = max(8, ((self.ppg + 7) // 8) * 8)
+        self.srow = max(8, ((page_tokens + 7) // 8) * 8)  # scales indexed by token position
         self.order = order
         self.kf = self.codes = self.scales = None
 
@@ -131,6 +131,7 @@ class PagedStore:
                 cc.stride, cc.bits, cc.dead_zone = c.stride, c.bits, c.dead_zone
                 cc.anchors_per_page, cc.pframes_per_page, cc.scale_row = c.apg, c.ppg, c.srow
                 cc.code_order = c.order
+                cc.scale_index = _lib.CQ_SCALE_BY_TOKEN
                 cc.keyframes, cc.codes, cc.scales = c.kf.data_ptr(), c.codes.data_ptr(), c.scales.data_ptr()
             self._desc = d
         return self._desc

@@ -348,6 +348,7 @@ extern "C" int cq_sdpa_reference_layout(const float *q, int32_t n_q_heads, int32
     cv.c[i].ppg = npf[i];
     cv.c[i].srow = npf[i];
     cv.c[i].order = CQ_ORDER_NATURAL;
+    cv.c[i].stok = 0;
     cv.c[i].bits = 4;
     cv.c[i].dead_zone = 0.f;
   }

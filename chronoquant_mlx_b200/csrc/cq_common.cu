@@ -27,7 +27,10 @@ static int validate_component(const cq_paged_cache *c, const cq_component &k, co
              n + ": anchors_per_page != page_tokens/stride");
   CQ_REQUIRE(k.pframes_per_page == c->page_tokens - k.anchors_per_page, CQ_ERR_INVALID,
              n + ": pframes_per_page != page_tokens - anchors_per_page");
-  CQ_REQUIRE(k.scale_row >= k.pframes_per_page, CQ_ERR_INVALID, n + ": scale_row too small");
+  CQ_REQUIRE(k.scale_index == CQ_SCALE_BY_PFRAME || k.scale_index == CQ_SCALE_BY_TOKEN, CQ_ERR_INVALID,
+             n + ": scale_index must be CQ_SCALE_BY_PFRAME or CQ_SCALE_BY_TOKEN");
+  CQ_REQUIRE(k.scale_row >= (k.scale_index == CQ_SCALE_BY_TOKEN ? c->page_tokens : k.pframes_per_page),
+             CQ_ERR_INVALID, n + ": scale_row too small");
   CQ_REQUIRE(k.bits >= 2 && k.bits <= 8, CQ_ERR_INVALID, n + ": bits must be in [2, 8]");
   CQ_REQUIRE(k.code_order == CQ_ORDER_NATURAL || (k.code_order == CQ_ORDER_MMA && c->head_dim % 64 == 0),
              CQ_ERR_INVALID, n + ": code_order MMA needs head_dim % 64 == 0");

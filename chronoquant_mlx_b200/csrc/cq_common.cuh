@@ -35,6 +35,7 @@ struct CompView {
   int ppg;    // P-frames per page
   int srow;   // scale row length
   int order;  // CQ_ORDER_*
+  int stok;   // scales indexed by token position (CQ_SCALE_BY_TOKEN)
   int bits;
   float dead_zone;
 };
@@ -64,6 +65,7 @@ inline CacheView make_view(const cq_paged_cache &c) {
     v.c[i].ppg = src[i]->pframes_per_page;
     v.c[i].srow = src[i]->scale_row;
     v.c[i].order = src[i]->code_order;
+    v.c[i].stok = src[i]->scale_index == CQ_SCALE_BY_TOKEN;
     v.c[i].bits = src[i]->bits;
     v.c[i].dead_zone = src[i]->dead_zone;
   }
@@ -98,6 +100,7 @@ struct TokLoc {
   const __half *anchor;   // fp16 [D]
   const uint32_t *codes;  // nullptr for an I-frame
   float scale;
+  int tl;                 // page-local token position
 };
 
 __device__ __forceinline__ TokLoc locate(const CacheView &cv, int comp, int b, int h, int64_t t) {
@@ -108,13 +111,14 @@ __device__ __forceinline__ TokLoc locate(const CacheView &cv, int comp, int b, i
   int a = tl / c.stride;
   TokLoc L;
   L.anchor = c.kf + ((pg * cv.H + h) * c.apg + a) * (int64_t)cv.D;
+  L.tl = tl;
   if (tl - a * c.stride == 0) {
     L.codes = nullptr;
     L.scale = 0.f;
   } else {
     int pf = tl - a - 1;
     L.codes = c.codes + ((pg * cv.H + h) * c.ppg + pf) * (int64_t)words_of(cv.D);
-    L.scale = __half2float(c.scales[(pg * cv.H + h) * c.srow + pf]);
+    L.scale = __half2float(c.scales[(pg * cv.H + h) * c.srow + (c.stok ? tl : pf)]);
   }
   return L;
 }

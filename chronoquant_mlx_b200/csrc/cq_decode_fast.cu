@@ -60,16 +60,19 @@ struct Params {
   float scale;
   int gqa;
   int64_t T;
-  int npu;            // pages per (sequence, kv-head) unit
-  int64_t tp;         // total pages = units * npu
+  int sub;            // tokens per sub-page (the pipeline unit)
+  int nsub;           // sub-pages per page (1 or 2)
+  int npu;            // sub-pages per (sequence, kv-head) unit
+  int64_t tp;         // total sub-pages = units * npu
   int smax;           // partial slots per CTA (unit segments a CTA's page range can touch)
   int stages;
   int tpw;           // tiles (16 tokens) per consumer warp per page
-  int qa_rows;       // q.anchor rows per stage (anchors per page rounded up to 16)
+  int qa_rows;       // q.anchor rows per stage (K anchors per sub-page rounded up to 16)
   // shared memory layout (bytes)
-  int off_tab, off_qa, off_sc, off_merge, off_stage, stage_bytes;
+  int off_tab, off_qa, off_qb, off_merge, off_stage, stage_bytes;
   int st_kf[2], st_cd[2], st_sc[2];
-  uint32_t full_bytes[6], full_total;  // bulk-copy sizes of a full page
+  uint32_t full_bytes[6], full_total;  // bulk-copy sizes of a full sub-page
+  int asub[2], rsub[2];                // anchors / code rows per full sub-page
   float *ws_m, *ws_l, *ws_o;  // [grid*smax][8], [grid*smax][8], [grid*smax][8][128]
 };
 
@@ -110,7 +113,7 @@ struct CopyPlan {
 // anchors, code rows and 16-byte-rounded scales those tokens use).
 __device__ __forceinline__ CopyPlan plan_page(const Params &p, int nvalid) {
   CopyPlan c;
-  if (nvalid == p.cv.P) {
+  if (nvalid == p.sub) {
 #pragma unroll
     for (int i = 0; i < 6; ++i) c.bytes[i] = p.full_bytes[i];
     c.total = p.full_total;
@@ -123,13 +126,13 @@ __device__ __forceinline__ CopyPlan plan_page(const Params &p, int nvalid) {
     const int r = nvalid - a;
     c.bytes[comp * 3 + 0] = (uint32_t)a * HD * 2;
     c.bytes[comp * 3 + 1] = (uint32_t)r * (HD / 8) * 4;
-    c.bytes[comp * 3 + 2] = (uint32_t)((r * 2 + 15) & ~15);
+    c.bytes[comp * 3 + 2] = (uint32_t)((nvalid * 2 + 15) & ~15);  // token-indexed scales
     c.total += c.bytes[comp * 3 + 0] + c.bytes[comp * 3 + 1] + c.bytes[comp * 3 + 2];
   }
   return c;
 }
 
-// Pages [first, last) of the global page index (unit * npu + page) that this
+// Sub-pages [first, last) of the global page index (unit * npu + page) that this
 // CTA processes: a contiguous, balanced share.
 __device__ __forceinline__ void my_pages(const Params &p, int64_t &first, int64_t &last) {
   first = (int64_t)blockIdx.x * p.tp / gridDim.x;
@@ -156,7 +159,7 @@ struct Cursor {
   __device__ bool valid() const { return left > 0; }
   __device__ bool last_in_seg(const Params &p) const { return left == 1 || lp + 1 == p.npu; }
   __device__ int nvalid(const Params &p) const {
-    return (int)min((int64_t)p.cv.P, p.T - (int64_t)lp * p.cv.P);
+    return (int)min((int64_t)p.sub, p.T - (int64_t)lp * p.sub);
   }
   __device__ void next(const Params &p) {
     if (++lp == p.npu) {
@@ -180,54 +183,62 @@ struct Cursor {
 // producer warp: bulk copies (lane 0) + q . K-anchor for each landed page
 // ---------------------------------------------------------------------------
 __device__ __forceinline__ int64_t page_id(const Params &p, const Cursor &c) {
-  return p.cv.block_table[(int64_t)c.b * p.cv.max_pages + c.lp];
+  return p.cv.block_table[(int64_t)c.b * p.cv.max_pages + (c.lp >> (p.nsub - 1))];
 }
 
 __device__ void issue_page(const Params &p, unsigned char *smem, uint64_t *full, const Cursor &c, int64_t pg) {
   const CacheView &cv = p.cv;
   const CopyPlan cp = plan_page(p, c.nvalid(p));
+  const int sl = c.lp & (p.nsub - 1);  // which slice of the page
   unsigned char *stage = smem + p.off_stage + c.s * p.stage_bytes;
   ptx::mbar_arrive_expect_tx(&full[c.s], cp.total);
   for (int comp = 0; comp < 2; ++comp) {
     const CompView &cc = cv.c[comp];
     const int64_t ph = pg * cv.H + c.h;
-    ptx::bulk_g2s(stage + p.st_kf[comp], cc.kf + ph * cc.apg * HD, cp.bytes[comp * 3 + 0], &full[c.s]);
-    if (cp.bytes[comp * 3 + 1]) {
-      ptx::bulk_g2s(stage + p.st_cd[comp], cc.codes + ph * cc.ppg * (HD / 8), cp.bytes[comp * 3 + 1], &full[c.s]);
-      ptx::bulk_g2s(stage + p.st_sc[comp], cc.scales + ph * cc.srow, cp.bytes[comp * 3 + 2], &full[c.s]);
-    }
+    ptx::bulk_g2s(stage + p.st_kf[comp], cc.kf + (ph * cc.apg + (int64_t)sl * p.asub[comp]) * HD,
+                  cp.bytes[comp * 3 + 0], &full[c.s]);
+    if (cp.bytes[comp * 3 + 1])
+      ptx::bulk_g2s(stage + p.st_cd[comp], cc.codes + (ph * cc.ppg + (int64_t)sl * p.rsub[comp]) * (HD / 8),
+                    cp.bytes[comp * 3 + 1], &full[c.s]);
+    ptx::bulk_g2s(stage + p.st_sc[comp], cc.scales + ph * cc.srow + (int64_t)sl * p.sub, cp.bytes[comp * 3 + 2],
+                  &full[c.s]);
   }
 }
 
-__device__ void producer(const Params &p, unsigned char *smem, uint64_t *full, uint64_t *empty, uint64_t *ready,
-                         int lane) {
+// Copy warp (one thread): issues the bulk copies of every sub-page of this
+// CTA's range, up to `stages` ahead of the consumers, and nothing else.
+__device__ void copier(const Params &p, unsigned char *smem, uint64_t *full, uint64_t *empty) {
+  int64_t first, last;
+  my_pages(p, first, last);
+  Cursor c;
+  c.init(p, first, last);
+  int64_t pg_next = c.valid() ? page_id(p, c) : 0;
+  for (int64_t k = 0; c.valid(); ++k) {
+    const int64_t pg = pg_next;
+    if (k >= p.stages && !ptx::mbar_wait_bounded(&empty[c.s], c.ph ^ 1u, WAIT_BUDGET)) {
+      atomicExch(&g_fast_error, ERR_TIMEOUT_EMPTY);
+      // the consumers give up on their own bounded waits; copies already
+      // issued complete into stages that stay resident until the CTA exits
+      // only after the q.anchor warp and consumers drained them
+      return;
+    }
+    issue_page(p, smem, full, c, pg);
+    c.next(p);
+    if (c.valid()) pg_next = page_id(p, c);  // next entry's load overlaps the wait above
+  }
+}
+
+// q.anchor warp: once a sub-page lands, computes q . anchor for each of its
+// K anchors (tensor-core MMA, rows = anchors) and marks the stage ready.
+__device__ void qa_warp(const Params &p, unsigned char *smem, uint64_t *full, uint64_t *ready, int lane) {
   const CacheView &cv = p.cv;
   const int g = lane >> 2, t = lane & 3;
   int64_t first, last;
   my_pages(p, first, last);
-  const uint2 *tab = (const uint2 *)(smem + p.off_tab);
-  Cursor rd, pf;  // rd: page whose q.anchor is computed next; pf: next page to prefetch
-  rd.init(p, first, last);
-  pf.init(p, first, last);
-  int64_t issued = 0;
-  bool ok = true;
-  // prefetch distance stages-1
-  for (; issued < p.stages - 1 && pf.valid(); ++issued, pf.next(p))
-    if (lane == 0) issue_page(p, smem, full, pf, page_id(p, pf));
-
   uint32_t qBn[8][2];
   int cur_unit = -1;
-  int64_t done = 0;
-  for (; rd.valid(); ++done, rd.next(p)) {
-    // block-table entry of the page prefetched at the end of this iteration,
-    // loaded now so its latency hides behind this page's work
-    int64_t pg_next = 0;
-    if (lane == 0 && pf.valid()) pg_next = page_id(p, pf);
-    if (!ptx::mbar_wait_bounded(&full[rd.s], rd.ph, WAIT_BUDGET)) {
-      atomicExch(&g_fast_error, ERR_TIMEOUT_FULL);
-      ok = false;
-      break;
-    }
+  Cursor rd;
+  for (rd.init(p, first, last); rd.valid(); rd.next(p)) {
     if (rd.unit != cur_unit) {
       cur_unit = rd.unit;
       const int hq = rd.h * p.gqa + g;
@@ -239,72 +250,36 @@ __device__ void producer(const Params &p, unsigned char *smem, uint64_t *full, u
         qBn[kk][1] = real ? ptx::pack_half2(q_scaled(p, rd.b, hq, d0 + 8), q_scaled(p, rd.b, hq, d0 + 9)) : 0u;
       }
     }
-    const int nvalid = rd.nvalid(p);
-    const unsigned char *stage = smem + p.off_stage + rd.s * p.stage_bytes;
-    // per-token scales (K pre-multiplied by log2 e; 0 for I-frames) for the consumers
-    {
-      float2 *sc = (float2 *)(smem + p.off_sc) + rd.s * cv.P;
-      const __half *scK = (const __half *)(stage + p.st_sc[0]);
-      const __half *scV = (const __half *)(stage + p.st_sc[1]);
-      for (int tl = lane; tl < cv.P; tl += 32) {
-        float a = 0.f, v = 0.f;
-        if (tl < nvalid) {
-          const uint2 e = tab[tl];
-          if (!(e.x & TAB_IFRAME)) a = __half2float(scK[(e.x & TAB_OFF) >> 6]) * LOG2E;
-          if (!(e.y & TAB_IFRAME)) v = __half2float(scV[(e.y & TAB_OFF) >> 6]);
-        }
-        sc[tl] = make_float2(a, v);
-      }
+    if (!ptx::mbar_wait_bounded(&full[rd.s], rd.ph, WAIT_BUDGET)) {
+      atomicExch(&g_fast_error, ERR_TIMEOUT_FULL);
+      return;
     }
-    // q . anchor for every K anchor present in the page (rows = anchors)
-    const int nK = (nvalid == cv.P) ? cv.c[0].apg : (nvalid - 1) / cv.c[0].stride + 1;
-    const unsigned char *kfK = stage + p.st_kf[0];
+    const int nvalid = rd.nvalid(p);
+    const int nK = (nvalid == p.sub) ? p.asub[0] : (nvalid - 1) / cv.c[0].stride + 1;
+    const unsigned char *kfK = smem + p.off_stage + rd.s * p.stage_bytes + p.st_kf[0];
     float *qa = (float *)(smem + p.off_qa) + rd.s * p.qa_rows * 8;
     const int mi = lane >> 3, rr = lane & 7;
     for (int mt = 0; mt * 16 < nK; ++mt) {
-      float c[4] = {0.f, 0.f, 0.f, 0.f};
+      // two accumulators halve the dependent MMA chain
+      float c0[4] = {0.f, 0.f, 0.f, 0.f}, c1[4] = {0.f, 0.f, 0.f, 0.f};
       const int arow = min(mt * 16 + rr + ((mi & 1) ? 8 : 0), nK - 1);
       const uint32_t base = ptx::smem_u32(kfK + arow * (HD * 2) + ((mi & 2) ? 16 : 0));
 #pragma unroll
-      for (int kk = 0; kk < 8; ++kk) {
-        uint32_t a0, a1, a2, a3;
+      for (int kk = 0; kk < 8; kk += 2) {
+        uint32_t a0, a1, a2, a3, b0, b1, b2, b3;
         ptx::ldmatrix_x4(a0, a1, a2, a3, base + kk * 32);
-        ptx::mma_f16_16816(c, a0, a1, a2, a3, qBn[kk][0], qBn[kk][1]);
+        ptx::ldmatrix_x4(b0, b1, b2, b3, base + kk * 32 + 32);
+        ptx::mma_f16_16816(c0, a0, a1, a2, a3, qBn[kk][0], qBn[kk][1]);
+        ptx::mma_f16_16816(c1, b0, b1, b2, b3, qBn[kk + 1][0], qBn[kk + 1][1]);
       }
       float *row0 = qa + (mt * 16 + g) * 8 + 2 * t;
-      row0[0] = c[0] * LOG2E;
-      row0[1] = c[1] * LOG2E;
-      row0[64] = c[2] * LOG2E;
-      row0[65] = c[3] * LOG2E;
+      row0[0] = (c0[0] + c1[0]) * LOG2E;
+      row0[1] = (c0[1] + c1[1]) * LOG2E;
+      row0[64] = (c0[2] + c1[2]) * LOG2E;
+      row0[65] = (c0[3] + c1[3]) * LOG2E;
     }
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&ready[rd.s]);
-    // prefetch: the stage of the next page was last used by page done + 1 - stages,
-    // which the consumers are finishing while this page is ready for them
-    if (pf.valid()) {
-      if (lane == 0) {
-        if (issued >= p.stages && !ptx::mbar_wait_bounded(&empty[pf.s], pf.ph ^ 1u, WAIT_BUDGET)) {
-          atomicExch(&g_fast_error, ERR_TIMEOUT_EMPTY);
-          ok = false;
-        } else {
-          issue_page(p, smem, full, pf, pg_next);
-        }
-      }
-      ok = __shfl_sync(0xffffffffu, ok, 0);
-      if (!ok) {
-        ++done;
-        break;
-      }
-      ++issued;
-      pf.next(p);
-    }
-  }
-  if (!ok && lane == 0) {
-    // drain: wait (bounded) for copies already issued into stages nobody will read
-    Cursor d;
-    d.init(p, first, last);
-    for (int64_t j = 0; j < issued; ++j, d.next(p))
-      if (j >= done) ptx::mbar_wait_bounded(&full[d.s], d.ph, WAIT_BUDGET);
   }
 }
 
@@ -387,15 +362,34 @@ __device__ void flush_partial(const Params &p, unsigned char *smem, WarpState &s
   reset(st);
 }
 
-__device__ __forceinline__ void process_tile(WarpState &st, const uint2 *tab, const float2 *sc, const float *qa,
-                                             const unsigned char *cdK, const unsigned char *kfV,
-                                             const unsigned char *cdV, const uint32_t (&qB)[4][4], float2 qc, int tb,
-                                             int nvalid, int lane) {
+// Shared-memory byte addresses a consumer thread uses for one page.
+struct StageAddr {
+  uint32_t tab;  // token table (uint2 per token)
+  uint32_t scK, scV;  // token-indexed fp16 scales (0 on I-frames)
+  uint32_t qa;   // q . anchor rows (8 floats per K anchor)
+  uint32_t cdK, kfV, cdV;
+  uint32_t qb;   // query fragments: [J][lane][4 words]
+};
+
+__device__ __forceinline__ float lds_half_as_float(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return __half2float(__ushort_as_half(v));
+}
+
+__device__ __forceinline__ void process_tile(WarpState &st, const StageAddr &A, float2 qc, int tb, int nvalid,
+                                             int lane) {
   const int g = lane >> 2, t = lane & 3;
   // ---------------- scores S^T[token][head] = q.codes (MMA), then anchors + scale
-  const uint32_t e0 = tab[tb + g].x, e1 = tab[tb + g + 8].x;
-  const uint4 wk0 = *(const uint4 *)(cdK + (e0 & TAB_OFF) + t * 16);
-  const uint4 wk1 = *(const uint4 *)(cdK + (e1 & TAB_OFF) + t * 16);
+  const uint32_t e0 = ptx::lds_u32(A.tab + (tb + g) * 8), e1 = ptx::lds_u32(A.tab + (tb + g + 8) * 8);
+  const uint4 wk0 = ptx::lds_u128(A.cdK + (e0 & TAB_OFF) + t * 16);
+  const uint4 wk1 = ptx::lds_u128(A.cdK + (e1 & TAB_OFF) + t * 16);
+  // token-indexed scales (0 on I-frames): K in log2 units, V as stored
+  const float2 sc0 = make_float2(lds_half_as_float(A.scK + (tb + g) * 2) * LOG2E, lds_half_as_float(A.scV + (tb + g) * 2));
+  const float2 sc1 =
+      make_float2(lds_half_as_float(A.scK + (tb + g + 8) * 2) * LOG2E, lds_half_as_float(A.scV + (tb + g + 8) * 2));
+  const float2 qa0 = ptx::lds_f2(A.qa + (e0 >> 16) + t * 8);
+  const float2 qa1 = ptx::lds_f2(A.qa + (e1 >> 16) + t * 8);
   float ca[4] = {0.f, 0.f, 0.f, 0.f}, cb[4] = {0.f, 0.f, 0.f, 0.f};
   {
     // raw nibble values (1024+n, 1024+16n) against q (q/16 on the 16n lanes):
@@ -404,16 +398,14 @@ __device__ __forceinline__ void process_tile(WarpState &st, const uint2 *tab, co
     const uint32_t w1[4] = {wk1.x, wk1.y, wk1.z, wk1.w};
 #pragma unroll
     for (int J = 0; J < 4; ++J) {
+      const uint4 qb = ptx::lds_u128(A.qb + J * 512);
       uint32_t h0[4], h1[4];
       ptx::nibbles_to_half2_raw(w0[J], h0);  // (d0,d4) (d1,d5) (d2,d6) (d3,d7)
       ptx::nibbles_to_half2_raw(w1[J], h1);
-      ptx::mma_f16_16816(ca, h0[0], h1[0], h0[1], h1[1], qB[J][0], qB[J][1]);
-      ptx::mma_f16_16816(cb, h0[2], h1[2], h0[3], h1[3], qB[J][2], qB[J][3]);
+      ptx::mma_f16_16816(ca, h0[0], h1[0], h0[1], h1[1], qb.x, qb.y);
+      ptx::mma_f16_16816(cb, h0[2], h1[2], h0[3], h1[3], qb.z, qb.w);
     }
   }
-  const float2 sc0 = sc[tb + g], sc1 = sc[tb + g + 8];  // (K scale * log2 e, V scale), 0 on I-frames
-  const float2 qa0 = *(const float2 *)((const unsigned char *)qa + (e0 >> 16) + t * 8);
-  const float2 qa1 = *(const float2 *)((const unsigned char *)qa + (e1 >> 16) + t * 8);
   float s0 = fmaf(sc0.x, (ca[0] + cb[0]) - qc.x, qa0.x), s1 = fmaf(sc0.x, (ca[1] + cb[1]) - qc.y, qa0.y);
   float s2 = fmaf(sc1.x, (ca[2] + cb[2]) - qc.x, qa1.x), s3 = fmaf(sc1.x, (ca[3] + cb[3]) - qc.y, qa1.y);
   if (tb + g >= nvalid) s0 = s1 = -INFINITY;
@@ -463,8 +455,8 @@ __device__ __forceinline__ void process_tile(WarpState &st, const uint2 *tab, co
   {
     const int mi = lane >> 3, r = lane & 7;
     const int tok = tb + r + ((mi & 2) ? 8 : 0);
-    const uint32_t aoff = (tok < nvalid) ? (tab[tok].y >> 16) : 0u;
-    const uint32_t base = ptx::smem_u32(kfV + aoff + ((mi & 1) ? 16 : 0));
+    const uint32_t aoff = (tok < nvalid) ? (ptx::lds_u32(A.tab + tok * 8 + 4) >> 16) : 0u;
+    const uint32_t base = A.kfV + aoff + ((mi & 1) ? 16 : 0);
 #pragma unroll
     for (int i = 0; i < 8; ++i) {
       uint32_t a0, a1, a2, a3;
@@ -474,12 +466,12 @@ __device__ __forceinline__ void process_tile(WarpState &st, const uint2 *tab, co
   }
   // ---------------- V codes: O += C_v^T P'  (tokens 2t,2t+1 | 2t+8,2t+9; words 2g, 2g+1)
   {
-    const uint4 ev = *(const uint4 *)(tab + tb + 2 * t);      // entries of tokens 2t, 2t+1
-    const uint4 ew = *(const uint4 *)(tab + tb + 2 * t + 8);  // entries of tokens 2t+8, 2t+9
-    const uint2 va = *(const uint2 *)(cdV + (ev.y & TAB_OFF) + g * 8);
-    const uint2 vb = *(const uint2 *)(cdV + (ev.w & TAB_OFF) + g * 8);
-    const uint2 vc = *(const uint2 *)(cdV + (ew.y & TAB_OFF) + g * 8);
-    const uint2 vd = *(const uint2 *)(cdV + (ew.w & TAB_OFF) + g * 8);
+    const uint4 ev = ptx::lds_u128(A.tab + (tb + 2 * t) * 8);      // entries of tokens 2t, 2t+1
+    const uint4 ew = ptx::lds_u128(A.tab + (tb + 2 * t + 8) * 8);  // entries of tokens 2t+8, 2t+9
+    const uint2 va = ptx::lds_u64(A.cdV + (ev.y & TAB_OFF) + g * 8);
+    const uint2 vb = ptx::lds_u64(A.cdV + (ev.w & TAB_OFF) + g * 8);
+    const uint2 vc = ptx::lds_u64(A.cdV + (ew.y & TAB_OFF) + g * 8);
+    const uint2 vd = ptx::lds_u64(A.cdV + (ew.w & TAB_OFF) + g * 8);
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
       const uint32_t wa = q ? va.y : va.x, wb = q ? vb.y : vb.x;
@@ -504,41 +496,47 @@ __device__ void consumer(const Params &p, unsigned char *smem, uint64_t *full, u
                          int warp, int lane) {
   const CacheView &cv = p.cv;
   const int g = lane >> 2, t = lane & 3;
-  const uint2 *tab = (const uint2 *)(smem + p.off_tab);
-  const int tiles_page = cv.P / 16;
   const int tile0 = warp * p.tpw;
-  const int tile1 = min(tile0 + p.tpw, tiles_page);
+  const int tile1 = min(tile0 + p.tpw, p.sub / 16);
+  const uint32_t smem0 = ptx::smem_u32(smem);
 
   WarpState st;
   reset(st);
   int64_t first, last;
   my_pages(p, first, last);
   int cur_unit = -1;
-  uint32_t qB[4][4];  // query in the K-code order (k-permuted); lanes paired with 16n values carry q/16
   float2 qc = make_float2(0.f, 0.f);  // q . (raw values of code 0) for heads 2t, 2t+1
+  StageAddr A;
+  A.tab = smem0 + p.off_tab;
+  A.qb = smem0 + p.off_qb + lane * 16;
   Cursor cu;
   for (cu.init(p, first, last); cu.valid(); cu.next(p)) {
     if (cu.unit != cur_unit) {
+      // New query group.  Every warp writes the same fragments to the shared
+      // copy (a unit changes only right after flush_partial's barriers, so no
+      // warp still reads the previous group's).
       cur_unit = cu.unit;
       const int hq = cu.h * p.gqa + g;
       const bool real = g < p.gqa;
       float cc[4] = {0.f, 0.f, 0.f, 0.f};
+      uint32_t *qbs = (uint32_t *)(smem + p.off_qb);
 #pragma unroll
       for (int J = 0; J < 4; ++J) {
         const int d0 = 32 * t + 8 * J;
         float v[8];
 #pragma unroll
         for (int i = 0; i < 8; ++i) v[i] = real ? q_scaled(p, cu.b, hq, d0 + i) : 0.f;
-        qB[J][0] = ptx::pack_half2(v[0], v[4]);
-        qB[J][1] = ptx::pack_half2(v[1] * 0.0625f, v[5] * 0.0625f);
-        qB[J][2] = ptx::pack_half2(v[2], v[6]);
-        qB[J][3] = ptx::pack_half2(v[3] * 0.0625f, v[7] * 0.0625f);
-        ptx::mma_f16_16816(cc, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_HI, ptx::RAW_CODE0_HI, qB[J][0],
-                           qB[J][1]);
-        ptx::mma_f16_16816(cc, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_HI, ptx::RAW_CODE0_HI, qB[J][2],
-                           qB[J][3]);
+        // query in the K-code order (k-permuted); lanes paired with 16n values carry q/16
+        const uint32_t b0 = ptx::pack_half2(v[0], v[4]);
+        const uint32_t b1 = ptx::pack_half2(v[1] * 0.0625f, v[5] * 0.0625f);
+        const uint32_t b2 = ptx::pack_half2(v[2], v[6]);
+        const uint32_t b3 = ptx::pack_half2(v[3] * 0.0625f, v[7] * 0.0625f);
+        *(uint4 *)(qbs + (J * 32 + lane) * 4) = make_uint4(b0, b1, b2, b3);
+        ptx::mma_f16_16816(cc, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_HI, ptx::RAW_CODE0_HI, b0, b1);
+        ptx::mma_f16_16816(cc, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_LO, ptx::RAW_CODE0_HI, ptx::RAW_CODE0_HI, b2, b3);
       }
       qc = make_float2(cc[0], cc[1]);
+      __syncwarp();
     }
     const int s = cu.s;
     // the bulk copies' own barrier makes their bytes visible to this thread;
@@ -548,14 +546,17 @@ __device__ void consumer(const Params &p, unsigned char *smem, uint64_t *full, u
       return;
     }
     const int nvalid = cu.nvalid(p);
-    const unsigned char *stage = smem + p.off_stage + s * p.stage_bytes;
-    const float *qa = (const float *)(smem + p.off_qa) + s * p.qa_rows * 8;
-    const float2 *sc = (const float2 *)(smem + p.off_sc) + s * cv.P;
+    const uint32_t stage = smem0 + p.off_stage + s * p.stage_bytes;
+    A.qa = smem0 + p.off_qa + s * p.qa_rows * 32;
+    A.scK = stage + p.st_sc[0];
+    A.scV = stage + p.st_sc[1];
+    A.cdK = stage + p.st_cd[0];
+    A.kfV = stage + p.st_kf[1];
+    A.cdV = stage + p.st_cd[1];
     for (int tile = tile0; tile < tile1; ++tile) {
       const int tb = tile * 16;
       if (tb >= nvalid) break;
-      process_tile(st, tab, sc, qa, stage + p.st_cd[0], stage + p.st_kf[1], stage + p.st_cd[1], qB, qc, tb, nvalid,
-                   lane);
+      process_tile(st, A, qc, tb, nvalid, lane);
     }
     __syncwarp();
     if (lane == 0) ptx::mbar_arrive(&empty[s]);
@@ -564,8 +565,8 @@ __device__ void consumer(const Params &p, unsigned char *smem, uint64_t *full, u
 }
 
 template <int NW>
-__global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) decode_kernel(const __grid_constant__ Params p) {
-  constexpr int NT = (NW + 1) * 32;
+__global__ void __launch_bounds__((NW + 2) * 32, NW == 8 ? 2 : 1) decode_kernel(const __grid_constant__ Params p) {
+  constexpr int NT = (NW + 2) * 32;
   extern __shared__ __align__(128) unsigned char smem[];
   uint64_t *full = (uint64_t *)smem;
   uint64_t *empty = full + p.stages;
@@ -580,10 +581,14 @@ __global__ void __launch_bounds__((NW + 1) * 32, NW == 8 ? 2 : 1) decode_kernel(
     ptx::fence_mbar_init();
   }
   uint2 *tab = (uint2 *)(smem + p.off_tab);
-  for (int i = threadIdx.x; i < p.cv.P; i += NT) tab[i] = tab_entry(i, p.cv.c[0].stride, p.cv.c[1].stride);
+  for (int i = threadIdx.x; i < p.sub; i += NT) tab[i] = tab_entry(i, p.cv.c[0].stride, p.cv.c[1].stride);
   __syncthreads();
   if (warp == NW) {
-    producer(p, smem, full, empty, ready, lane);
+    if (lane == 0) copier(p, smem, full, empty);
+    return;
+  }
+  if (warp == NW + 1) {
+    qa_warp(p, smem, full, ready, lane);
     return;
   }
   consumer<NW>(p, smem, full, empty, ready, warp, lane);
@@ -670,31 +675,39 @@ __global__ void __launch_bounds__(HD) fast_combine(const float *ws_m, const floa
 // host side
 // ---------------------------------------------------------------------------
 struct Layout {
-  int stages, stage_bytes, off_tab, off_qa, off_sc, off_merge, off_stage, total, qa_rows;
+  int stages, stage_bytes, off_tab, off_qa, off_qb, off_merge, off_stage, total, qa_rows;
   int st_kf[2], st_cd[2], st_sc[2];
 };
 
 static inline int up128(int x) { return (x + 127) & ~127; }
 
+// Sub-page size: 128 tokens when pages hold more and both strides divide 128.
+static int sub_tokens(const cq_paged_cache &c) {
+  if (c.page_tokens > 128 && c.page_tokens % 128 == 0 && 128 % c.k.stride == 0 && 128 % c.v.stride == 0) return 128;
+  return c.page_tokens;
+}
+
 static Layout make_layout(const cq_paged_cache &c, int stages, int gqa, int NW) {
   Layout L;
+  const int sub = sub_tokens(c);
   const cq_component *cc[2] = {&c.k, &c.v};
   int off = 0;
   for (int i = 0; i < 2; ++i) {
+    const int a = sub / cc[i]->stride;
     L.st_kf[i] = off;
-    off = up128(off + cc[i]->anchors_per_page * HD * 2);
+    off = up128(off + a * HD * 2);
     L.st_cd[i] = off;
-    off = up128(off + cc[i]->pframes_per_page * (HD / 8) * 4);
+    off = up128(off + (sub - a) * (HD / 8) * 4);
     L.st_sc[i] = off;
-    off = up128(off + cc[i]->scale_row * 2);
+    off = up128(off + sub * 2);
   }
   L.stage_bytes = off;
   L.stages = stages;
-  L.qa_rows = ((c.k.anchors_per_page + 15) / 16) * 16;
+  L.qa_rows = ((sub / c.k.stride + 15) / 16) * 16;
   L.off_tab = 128;  // mbarriers live in the first 128 bytes
-  L.off_qa = up128(L.off_tab + c.page_tokens * 8);
-  L.off_sc = up128(L.off_qa + stages * L.qa_rows * 8 * 4);
-  L.off_merge = up128(L.off_sc + stages * c.page_tokens * 8);
+  L.off_qa = up128(L.off_tab + sub * 8);
+  L.off_qb = up128(L.off_qa + stages * L.qa_rows * 8 * 4);
+  L.off_merge = up128(L.off_qb + 4 * 32 * 16);
   L.off_stage = up128(L.off_merge + (NW * 8 * 2 + NW * gqa * HD) * 4);
   L.total = L.off_stage + stages * L.stage_bytes;
   return L;
@@ -735,6 +748,7 @@ bool fast_decode_supported(const cq_paged_cache &c, int n_q_heads, int q_len) {
   if (c.page_tokens > 256 || c.page_tokens % 16) return false;
   if (c.k.stride < 2 || c.v.stride < 2) return false;
   if (c.k.code_order != CQ_ORDER_NATURAL || c.v.code_order != CQ_ORDER_MMA) return false;
+  if (c.k.scale_index != CQ_SCALE_BY_TOKEN || c.v.scale_index != CQ_SCALE_BY_TOKEN) return false;
   if (c.k.scale_row % 8 || c.v.scale_row % 8) return false;
   if (!aligned16(c.k.keyframes) || !aligned16(c.v.keyframes) || !aligned16(c.k.codes) || !aligned16(c.v.codes) ||
       !aligned16(c.k.scales) || !aligned16(c.v.scales))
@@ -759,7 +773,7 @@ static int sm_count() {
 }
 
 struct Plan {
-  int npu, grid, smax, stages, per_sm, nw;
+  int sub, npu, grid, smax, stages, per_sm, nw;
   int64_t tp;
 };
 
@@ -776,7 +790,8 @@ static int pick_nw() {
 
 static Plan make_plan(const cq_paged_cache &c, int64_t T, int gqa, int splits_req) {
   Plan pl;
-  pl.npu = (int)((T + c.page_tokens - 1) / c.page_tokens);
+  pl.sub = sub_tokens(c);
+  pl.npu = (int)((T + pl.sub - 1) / pl.sub);
   const int64_t units = (int64_t)c.batch * c.kv_heads;
   pl.tp = units * pl.npu;
   pl.nw = pick_nw();
@@ -784,7 +799,7 @@ static Plan make_plan(const cq_paged_cache &c, int64_t T, int gqa, int splits_re
   int64_t g = (int64_t)sm_count() * std::max(1, pl.per_sm);
   if (splits_req > 0) g = std::min<int64_t>(g, units * splits_req);
   pl.grid = (int)std::max<int64_t>(1, std::min<int64_t>(g, pl.tp));
-  const int64_t ppc = (pl.tp + pl.grid - 1) / pl.grid;  // pages per CTA, at most
+  const int64_t ppc = (pl.tp + pl.grid - 1) / pl.grid;  // sub-pages per CTA, at most
   pl.smax = (int)((ppc + pl.npu - 1) / pl.npu + 1);
   return pl;
 }
@@ -808,16 +823,18 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
   p.gqa = n_q_heads / c.kv_heads;
   p.T = T;
   const Plan pl = make_plan(c, T, p.gqa, splits_req);
+  p.sub = pl.sub;
+  p.nsub = c.page_tokens / pl.sub;
   p.npu = pl.npu;
   p.tp = pl.tp;
   p.smax = pl.smax;
   Layout L = make_layout(c, pl.stages, p.gqa, pl.nw);
   p.stages = pl.stages;
-  p.tpw = (c.page_tokens / 16 + pl.nw - 1) / pl.nw;
+  p.tpw = (pl.sub / 16 + pl.nw - 1) / pl.nw;
   p.qa_rows = L.qa_rows;
   p.off_tab = L.off_tab;
   p.off_qa = L.off_qa;
-  p.off_sc = L.off_sc;
+  p.off_qb = L.off_qb;
   p.off_merge = L.off_merge;
   p.off_stage = L.off_stage;
   p.stage_bytes = L.stage_bytes;
@@ -830,9 +847,11 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
     const cq_component *cc[2] = {&c.k, &c.v};
     p.full_total = 0;
     for (int i = 0; i < 2; ++i) {
-      p.full_bytes[i * 3 + 0] = (uint32_t)cc[i]->anchors_per_page * HD * 2;
-      p.full_bytes[i * 3 + 1] = (uint32_t)cc[i]->pframes_per_page * (HD / 8) * 4;
-      p.full_bytes[i * 3 + 2] = (uint32_t)((cc[i]->pframes_per_page * 2 + 15) & ~15);
+      p.asub[i] = pl.sub / cc[i]->stride;
+      p.rsub[i] = pl.sub - p.asub[i];
+      p.full_bytes[i * 3 + 0] = (uint32_t)p.asub[i] * HD * 2;
+      p.full_bytes[i * 3 + 1] = (uint32_t)p.rsub[i] * (HD / 8) * 4;
+      p.full_bytes[i * 3 + 2] = (uint32_t)pl.sub * 2;
       for (int j = 0; j < 3; ++j) p.full_total += p.full_bytes[i * 3 + j];
     }
   }
@@ -859,9 +878,9 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
     }
   }
   if (pl.nw == 8)
-    decode_kernel<8><<<pl.grid, 9 * 32, L.total, st>>>(p);
+    decode_kernel<8><<<pl.grid, (8 + 2) * 32, L.total, st>>>(p);
   else
-    decode_kernel<16><<<pl.grid, 17 * 32, L.total, st>>>(p);
+    decode_kernel<16><<<pl.grid, (16 + 2) * 32, L.total, st>>>(p);
   int r = check_launch("decode_kernel");
   if (r) return r;
   fast_combine<<<c.batch * n_q_heads, HD, 0, st>>>(p.ws_m, p.ws_l, p.ws_o, pl.tp, pl.npu, pl.grid, pl.smax,

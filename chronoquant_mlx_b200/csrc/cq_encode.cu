@@ -72,6 +72,7 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) append_kernel(EncodeArgs A)
       int d = lane + 32 * i;
       if (d < D) kf_row[d] = __float2half_rn(xv[i]);
     }
+    if (c.stok && lane == 0) const_cast<__half *>(c.scales)[(pg * cv.H + h) * c.srow + tl] = __float2half_rn(0.f);
     return;
   }
 
@@ -146,7 +147,7 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) append_kernel(EncodeArgs A)
   if (lane < W) code_row[lane] = sw[lane];
   if (lane == 0) {
     // scale.astype(float16) (codec.py:65, cache.py:116)
-    const_cast<__half *>(c.scales)[(pg * cv.H + h) * c.srow + pf] = __float2half_rn(scale);
+    const_cast<__half *>(c.scales)[(pg * cv.H + h) * c.srow + (c.stok ? tl : pf)] = __float2half_rn(scale);
   }
 }
 

@@ -46,6 +46,10 @@ extern "C" {
 #define CQ_BF16 1
 #define CQ_F32 2
 
+/* Scale indexing within a (page, head) row */
+#define CQ_SCALE_BY_PFRAME 0 /* slot = P-frame ordinal (the reference layout, cache.py:116) */
+#define CQ_SCALE_BY_TOKEN 1  /* slot = page-local token position, 0 at I-frames */
+
 /* V-code nibble orders (the cache's own storage; the reference layout is order 0) */
 #define CQ_ORDER_NATURAL 0 /* word w holds dims 8w..8w+7, LSB first (kernels.py:15-19) */
 #define CQ_ORDER_MMA 1     /* word 2g+q, nibble j holds dim g + 64q + 8j (head_dim 128) */
@@ -54,11 +58,13 @@ extern "C" {
  * One compressed component (K or V) of a paged cache.  Per page and head:
  *   keyframes fp16  [anchors_per_page][head_dim]
  *   codes     u32   [pframes_per_page][head_dim/8]
- *   scales    fp16  [scale_row]            (scale_row >= pframes_per_page, multiple of 8)
+ *   scales    fp16  [scale_row]            (indexed per scale_index; multiple of 8)
  * Arrays are [n_pages][kv_heads][...] contiguous.  Token t of sequence b lives
  * in page block_table[b*max_pages + t/page_tokens] at tl = t % page_tokens;
  * it is an I-frame iff tl % stride == 0 (anchor slot tl/stride), else a
- * P-frame in slot tl - tl/stride - 1 anchored on slot tl/stride.
+ * P-frame in code row tl - tl/stride - 1 anchored on slot tl/stride; its
+ * scale sits at that row index (CQ_SCALE_BY_PFRAME) or at tl
+ * (CQ_SCALE_BY_TOKEN, whose I-frame slots hold 0).
  */
 typedef struct cq_component {
   int32_t stride;           /* I-frame period (cache.py:100) */
@@ -68,7 +74,7 @@ typedef struct cq_component {
   int32_t pframes_per_page; /* page_tokens - anchors_per_page */
   int32_t scale_row;        /* padded scales per (page, head) */
   int32_t code_order;       /* CQ_ORDER_* */
-  int32_t _pad;
+  int32_t scale_index;      /* CQ_SCALE_BY_* */
   void *keyframes;          /* fp16 */
   uint32_t *codes;
   void *scales;             /* fp16 */

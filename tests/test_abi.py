@@ -52,8 +52,9 @@ def _desc(**over):
         c.stride, c.bits, c.dead_zone = s, 4, 0.0
         c.anchors_per_page = 256 // s
         c.pframes_per_page = 256 - 256 // s
-        c.scale_row = ((c.pframes_per_page + 7) // 8) * 8
+        c.scale_row = 256
         c.code_order = 0
+        c.scale_index = 1
         c.keyframes, c.codes, c.scales = 0x2000, 0x3000, 0x4000
     for k, v in over.items():
         setattr(d, k, v)
