@@ -23,12 +23,13 @@ CQ_ERR_WORKSPACE = -4
 CQ_F16, CQ_BF16, CQ_F32 = 0, 1, 2
 CQ_ORDER_NATURAL, CQ_ORDER_MMA = 0, 1
 CQ_SCALE_BY_PFRAME, CQ_SCALE_BY_TOKEN = 0, 1
+CQ_STATIC_SCRATCH_BYTES = 8 << 20  # cq_attention_static_scratch's fixed per-device scratch
 
 EXPORTED = [
     "cq_abi_version", "cq_last_error", "cq_device_error", "cq_append", "cq_attention", "cq_attention_workspace",
     "cq_attention_masked", "cq_lse_merge", "cq_reconstruct", "cq_export_state", "cq_import_state", "cq_quantize_delta",
     "cq_dequantize_delta", "cq_pack_int4", "cq_unpack_int4", "cq_sdpa_reference_layout",
-    "cq_sdpa_reference_layout_workspace",
+    "cq_sdpa_reference_layout_workspace", "cq_attention_static_scratch",
 ]
 
 
@@ -83,6 +84,8 @@ def _declare(lib):
         "cq_sdpa_reference_layout": [P, I32, I32, P, I32, P, P, I32, P, I32, P, P, I32, I32, I64, I32, I32, P, P,
                                      SZ, P],
         "cq_sdpa_reference_layout_workspace": [I32, I32, I64, ctypes.POINTER(SZ)],
+        "cq_attention_static_scratch": [C, I64, P, ctypes.c_int, I32, I32, I32, I64, I64, I64, F, P, ctypes.c_int,
+                                        P, I32, P],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)

@@ -187,6 +187,28 @@ int cq_sdpa_reference_layout(const float *q, int32_t n_q_heads, int32_t dim, con
                              float *out, void *workspace, size_t workspace_bytes, void *stream);
 int cq_sdpa_reference_layout_workspace(int32_t n_q_heads, int32_t dim, int64_t seq_len, size_t *bytes);
 
+/* cq_attention without a workspace argument, for callers that cannot
+ * allocate device memory at decode time (a runtime whose memory pool is owned
+ * elsewhere, a thread that must not take an allocator's lock mid-step, a
+ * binding that holds only plain pointers).  No reference counterpart: the
+ * reference's attention (attention.py:23-74) allocates through MLX.
+ *
+ * The split-KV partials live in one fixed device array of
+ * CQ_STATIC_SCRATCH_BYTES bytes per device inside the library; the call
+ * allocates nothing.  A shape whose partials need more (cq_attention_workspace
+ * reports the size) is rejected with CQ_ERR_WORKSPACE.  The first call on a
+ * device, with that device current, looks up the array's address; make it
+ * before any stream capture.  Nothing in the array needs to start at zero.
+ * All calls on one device share the array: calls that overlap on the device
+ * (other streams, other host threads) race and can corrupt each other's
+ * results, so serialise them on one stream.  Arguments and results are those
+ * of cq_attention. */
+#define CQ_STATIC_SCRATCH_BYTES (8u << 20)
+int cq_attention_static_scratch(const cq_paged_cache *cache, int64_t T, const void *q, int q_dtype,
+                                int32_t n_q_heads, int32_t q_len, int32_t causal, int64_t q_sb, int64_t q_sh,
+                                int64_t q_sq, float scale, void *out, int out_dtype, float *lse_out,
+                                int32_t num_splits, void *stream);
+
 #ifdef __cplusplus
 }
 #endif
