@@ -29,7 +29,7 @@ EXPORTED = [
     "cq_abi_version", "cq_last_error", "cq_device_error", "cq_append", "cq_attention", "cq_attention_workspace",
     "cq_attention_masked", "cq_lse_merge", "cq_reconstruct", "cq_export_state", "cq_import_state", "cq_quantize_delta",
     "cq_dequantize_delta", "cq_pack_int4", "cq_unpack_int4", "cq_sdpa_reference_layout",
-    "cq_sdpa_reference_layout_workspace", "cq_attention_static_scratch",
+    "cq_sdpa_reference_layout_workspace", "cq_attention_static_scratch", "cq_decode_chunk_tokens",
 ]
 
 
@@ -39,6 +39,10 @@ class CqComponent(ctypes.Structure):
         ("anchors_per_page", ctypes.c_int32), ("pframes_per_page", ctypes.c_int32),
         ("scale_row", ctypes.c_int32), ("code_order", ctypes.c_int32), ("scale_index", ctypes.c_int32),
         ("keyframes", ctypes.c_void_p), ("codes", ctypes.c_void_p), ("scales", ctypes.c_void_p),
+        ("keyframe_head_stride", ctypes.c_int64), ("code_head_stride", ctypes.c_int64),
+        ("scale_head_stride", ctypes.c_int64), ("chunk_tokens", ctypes.c_int32), ("reserved", ctypes.c_int32),
+        ("keyframe_chunk_stride", ctypes.c_int64), ("code_chunk_stride", ctypes.c_int64),
+        ("scale_chunk_stride", ctypes.c_int64),
     ]
 
 
@@ -84,6 +88,7 @@ def _declare(lib):
         "cq_sdpa_reference_layout": [P, I32, I32, P, I32, P, P, I32, P, I32, P, P, I32, I32, I64, I32, I32, P, P,
                                      SZ, P],
         "cq_sdpa_reference_layout_workspace": [I32, I32, I64, ctypes.POINTER(SZ)],
+        "cq_decode_chunk_tokens": [I32, I32, I32, I32],
         "cq_attention_static_scratch": [C, I64, P, ctypes.c_int, I32, I32, I32, I64, I64, I64, F, P, ctypes.c_int,
                                         P, I32, P],
     }

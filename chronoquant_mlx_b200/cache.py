@@ -7,13 +7,15 @@ constructor, attributes, cache protocol (``update_and_fetch``, ``offset``,
 
 Storage differs from the reference's growing concatenated arrays
 (cache.py:118-129): tokens live in fixed-size pages of ``page_tokens`` tokens
-(a multiple of lcm(stride_k, stride_v), so every page owns its anchors).  Per
-page and kv-head, each component keeps fp16 anchors, uint32 code rows and
-fp16 scales -- exactly the reference's per-token bytes, so ``nbytes`` (the
-active-byte accounting of cache.py:274-287) is unchanged.  V code rows use
-the decode kernel's nibble order when head_dim is 128; ``state`` converts to
-the reference layout.  Appending never copies history except when the page
-pool grows (geometrically, or never with ``max_tokens``).
+(a multiple of lcm(stride_k, stride_v), so every page owns its anchors), each
+cut into chunk blocks that hold both components' fp16 anchors, uint32 code
+rows and fp16 scales (``PagedStore``).  The anchors and code rows are exactly
+the reference's per-token bytes, so ``nbytes`` (the active-byte accounting of
+cache.py:274-287) is unchanged; scales are stored per token (2 bytes more per
+I-frame).  V code rows use the decode kernel's nibble order when head_dim is
+128; ``state`` converts to the reference layout.  Appending never copies
+history except when the page pool grows (geometrically, or never with
+``max_tokens``).
 """
 
 from __future__ import annotations
@@ -63,14 +65,28 @@ class _Component:
         self.dead_zone = float(dead_zone)
         self.apg = page_tokens // stride
         self.ppg = page_tokens - self.apg
-        self.srow = max(8, ((page_tokens + 7) // 8) * 8)  # scales indexed by token position
+        self.srow = page_tokens  # scales indexed by token position
         self.order = order
-        self.kf = self.codes = self.scales = None
+        self.off_kf = self.off_cd = self.off_sc = 0  # byte offsets within a chunk block
+
+
+def _up16(n: int) -> int:
+    return (n + 15) & ~15
 
 
 class PagedStore:
-    """Device storage of one cache: page pools for K and V plus the block table.
+    """Device storage of one cache: one byte buffer of chunk blocks plus the
+    block table.
 
+    Pages hold ``P`` tokens, cut into chunks of ``chunk`` tokens (the decode
+    kernel's chunk when it takes this configuration, else the whole page).
+    Every (page, kv-head, chunk) is one contiguous block
+
+        [K anchors][K code rows][K scales][V anchors][V code rows][V scales]
+
+    (anchors fp16 [chunk/stride][D], code rows uint32 [chunk - chunk/stride]
+    [D/8] in P-frame order, scales fp16 [chunk] by token), each segment
+    16-byte aligned, so a decode step fetches a chunk with one bulk copy.
     Physical page of (sequence b, logical page p) is ``p * batch + b``; the
     pool grows by reallocating and copying the prefix of pages."""
 
@@ -79,8 +95,22 @@ class PagedStore:
         self.W = (head_dim + 7) // 8
         self.comps = comps  # [k, v] _Component
         self.device = device
+        c = int(_lib.lib().cq_decode_chunk_tokens(comps[0].stride, comps[1].stride, page_tokens, head_dim))
+        self.chunk = c if c > 0 else page_tokens
+        off = 0
+        for comp in comps:
+            a = self.chunk // comp.stride
+            comp.off_kf = off
+            off = _up16(off + a * head_dim * 2)
+            comp.off_cd = off
+            off = _up16(off + (self.chunk - a) * self.W * 4)
+            comp.off_sc = off
+            off = _up16(off + self.chunk * 2)
+        self.chunk_bytes = off
+        self.head_bytes = (page_tokens // self.chunk) * self.chunk_bytes
         self.max_pages = 0
         self.block_table = None
+        self.buf = None
         self._desc = None
 
     @property
@@ -104,17 +134,12 @@ class PagedStore:
     def _grow(self, max_pages: int) -> None:
         old_n = self.n_pages
         n = max_pages * self.B
-        dev = self.device
-        for c in self.comps:
-            kf = torch.zeros((n, self.H, c.apg, self.D), dtype=torch.float16, device=dev)
-            codes = torch.zeros((n, self.H, max(c.ppg, 1), self.W), dtype=torch.int32, device=dev)
-            scales = torch.zeros((n, self.H, c.srow), dtype=torch.float16, device=dev)
-            if old_n:
-                kf[:old_n].copy_(c.kf)
-                codes[:old_n].copy_(c.codes)
-                scales[:old_n].copy_(c.scales)
-            c.kf, c.codes, c.scales = kf, codes, scales
+        buf = torch.zeros((n, self.H, self.head_bytes), dtype=torch.uint8, device=self.device)
+        if old_n:
+            buf[:old_n].copy_(self.buf)
+        self.buf = buf
         self.max_pages = max_pages
+        dev = self.device
         pages = torch.arange(max_pages, dtype=torch.int32, device=dev)
         self.block_table = (pages[None, :] * self.B + torch.arange(self.B, dtype=torch.int32, device=dev)[:, None]
                             ).contiguous()
@@ -126,18 +151,24 @@ class PagedStore:
             d.batch, d.kv_heads, d.head_dim, d.page_tokens = self.B, self.H, self.D, self.P
             d.max_pages, d.n_pages = self.max_pages, self.n_pages
             d.block_table = self.block_table.data_ptr()
+            base = self.buf.data_ptr()
             for name, c in zip(("k", "v"), self.comps):
                 cc = getattr(d, name)
                 cc.stride, cc.bits, cc.dead_zone = c.stride, c.bits, c.dead_zone
                 cc.anchors_per_page, cc.pframes_per_page, cc.scale_row = c.apg, c.ppg, c.srow
                 cc.code_order = c.order
                 cc.scale_index = _lib.CQ_SCALE_BY_TOKEN
-                cc.keyframes, cc.codes, cc.scales = c.kf.data_ptr(), c.codes.data_ptr(), c.scales.data_ptr()
+                cc.keyframes, cc.codes, cc.scales = base + c.off_kf, base + c.off_cd, base + c.off_sc
+                cc.keyframe_head_stride, cc.code_head_stride = self.head_bytes // 2, self.head_bytes // 4
+                cc.scale_head_stride = self.head_bytes // 2
+                cc.chunk_tokens = self.chunk
+                cc.keyframe_chunk_stride, cc.code_chunk_stride = self.chunk_bytes // 2, self.chunk_bytes // 4
+                cc.scale_chunk_stride = self.chunk_bytes // 2
             self._desc = d
         return self._desc
 
     def pool_bytes(self) -> int:
-        return sum(t.numel() * t.element_size() for c in self.comps for t in (c.kf, c.codes, c.scales))
+        return self.buf.numel()
 
 
 class ChronoQuantCache:

@@ -351,6 +351,14 @@ extern "C" int cq_sdpa_reference_layout(const float *q, int32_t n_q_heads, int32
     cv.c[i].stok = 0;
     cv.c[i].bits = 4;
     cv.c[i].dead_zone = 0.f;
+    // one chunk spanning the whole view
+    cv.c[i].ac = nkf[i] > 0 ? nkf[i] : 1;
+    cv.c[i].pc = npf[i] > 0 ? npf[i] : 1;
+    cv.c[i].scn = cv.c[i].pc;
+    cv.c[i].kf_hs = (int64_t)nkf[i] * dim;
+    cv.c[i].cd_hs = (int64_t)npf[i] * ((dim + 7) / 8);
+    cv.c[i].sc_hs = npf[i];
+    cv.c[i].kf_cs = cv.c[i].cd_cs = cv.c[i].sc_cs = 0;
   }
   CQ_REQUIRE(cv.P >= seq_len, CQ_ERR_UNSUPPORTED, "cq_sdpa_reference_layout: sequence too long");
   // padded code rows: words = ceil(dim/8)

@@ -34,6 +34,14 @@ static int validate_component(const cq_paged_cache *c, const cq_component &k, co
   CQ_REQUIRE(k.bits >= 2 && k.bits <= 8, CQ_ERR_INVALID, n + ": bits must be in [2, 8]");
   CQ_REQUIRE(k.code_order == CQ_ORDER_NATURAL || (k.code_order == CQ_ORDER_MMA && c->head_dim % 64 == 0),
              CQ_ERR_INVALID, n + ": code_order MMA needs head_dim % 64 == 0");
+  if (k.chunk_tokens > 0 && k.chunk_tokens != c->page_tokens) {
+    CQ_REQUIRE(c->page_tokens % k.chunk_tokens == 0 && k.chunk_tokens % k.stride == 0, CQ_ERR_INVALID,
+               n + ": chunk_tokens must divide page_tokens and be a multiple of the stride");
+    CQ_REQUIRE(k.keyframe_chunk_stride > 0 && k.code_chunk_stride > 0 && k.scale_chunk_stride > 0, CQ_ERR_INVALID,
+               n + ": chunk strides must be positive with several chunks per page");
+  }
+  CQ_REQUIRE(k.keyframe_head_stride >= 0 && k.code_head_stride >= 0 && k.scale_head_stride >= 0, CQ_ERR_INVALID,
+             n + ": negative head stride");
   CQ_REQUIRE(k.keyframes != nullptr, CQ_ERR_INVALID, n + ": keyframes is null");
   CQ_REQUIRE(k.pframes_per_page == 0 || (k.codes != nullptr && k.scales != nullptr), CQ_ERR_INVALID,
              n + ": codes/scales null");

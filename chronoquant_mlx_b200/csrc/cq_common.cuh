@@ -33,11 +33,15 @@ struct CompView {
   int stride;
   int apg;    // anchors per page
   int ppg;    // P-frames per page
-  int srow;   // scale row length
+  int srow;   // scale slots per (page, head)
   int order;  // CQ_ORDER_*
   int stok;   // scales indexed by token position (CQ_SCALE_BY_TOKEN)
   int bits;
   float dead_zone;
+  // addressing (elements): per (page, head) block, per chunk, slots per chunk
+  int64_t kf_hs, cd_hs, sc_hs;
+  int64_t kf_cs, cd_cs, sc_cs;
+  int ac, pc, scn;  // anchors, code rows, scale slots per chunk
 };
 
 struct CacheView {
@@ -68,8 +72,37 @@ inline CacheView make_view(const cq_paged_cache &c) {
     v.c[i].stok = src[i]->scale_index == CQ_SCALE_BY_TOKEN;
     v.c[i].bits = src[i]->bits;
     v.c[i].dead_zone = src[i]->dead_zone;
+    const cq_component &k = *src[i];
+    const int W = (c.head_dim + 7) >> 3;
+    const int ct = k.chunk_tokens > 0 ? k.chunk_tokens : c.page_tokens;
+    v.c[i].ac = ct / k.stride;
+    v.c[i].pc = ct - v.c[i].ac;
+    v.c[i].scn = k.scale_index == CQ_SCALE_BY_TOKEN ? ct : v.c[i].pc;
+    const bool one = ct == c.page_tokens;
+    v.c[i].kf_hs = k.keyframe_head_stride ? k.keyframe_head_stride : (int64_t)k.anchors_per_page * c.head_dim;
+    v.c[i].cd_hs = k.code_head_stride ? k.code_head_stride : (int64_t)k.pframes_per_page * W;
+    v.c[i].sc_hs = k.scale_head_stride ? k.scale_head_stride : (int64_t)k.scale_row;
+    v.c[i].kf_cs = one ? 0 : k.keyframe_chunk_stride;
+    v.c[i].cd_cs = one ? 0 : k.code_chunk_stride;
+    v.c[i].sc_cs = one ? 0 : k.scale_chunk_stride;
+    if (one) v.c[i].scn = k.scale_row;  // one chunk: the scale index never wraps
   }
   return v;
+}
+
+// Element addresses of anchor slot a, code row pf and scale slot si (all
+// page-local) of (physical page pg, head h); see cq_component.
+__host__ __device__ inline int64_t kf_index(const CompView &c, int H, int D, int64_t pg, int h, int a) {
+  const int j = a / c.ac;
+  return (pg * H + h) * c.kf_hs + j * c.kf_cs + (int64_t)(a - j * c.ac) * D;
+}
+__host__ __device__ inline int64_t code_index(const CompView &c, int H, int W, int64_t pg, int h, int pf) {
+  const int j = pf / c.pc;
+  return (pg * H + h) * c.cd_hs + j * c.cd_cs + (int64_t)(pf - j * c.pc) * W;
+}
+__host__ __device__ inline int64_t scale_index(const CompView &c, int H, int64_t pg, int h, int si) {
+  const int j = si / c.scn;
+  return (pg * H + h) * c.sc_hs + j * c.sc_cs + (si - j * c.scn);
 }
 
 int validate_cache(const cq_paged_cache *c);
@@ -110,15 +143,15 @@ __device__ __forceinline__ TokLoc locate(const CacheView &cv, int comp, int b, i
   int64_t pg = page_of(cv, b, lp);
   int a = tl / c.stride;
   TokLoc L;
-  L.anchor = c.kf + ((pg * cv.H + h) * c.apg + a) * (int64_t)cv.D;
+  L.anchor = c.kf + kf_index(c, cv.H, cv.D, pg, h, a);
   L.tl = tl;
   if (tl - a * c.stride == 0) {
     L.codes = nullptr;
     L.scale = 0.f;
   } else {
     int pf = tl - a - 1;
-    L.codes = c.codes + ((pg * cv.H + h) * c.ppg + pf) * (int64_t)words_of(cv.D);
-    L.scale = __half2float(c.scales[(pg * cv.H + h) * c.srow + (c.stok ? tl : pf)]);
+    L.codes = c.codes + code_index(c, cv.H, words_of(cv.D), pg, h, pf);
+    L.scale = __half2float(c.scales[scale_index(c, cv.H, pg, h, c.stok ? tl : pf)]);
   }
   return L;
 }

@@ -7,6 +7,11 @@ namespace cq {
 // True when the fast decode kernel handles this shape (q_len == 1,
 // head_dim 128, GQA group <= 8, pages of <= 256 tokens laid out for it).
 bool fast_decode_supported(const cq_paged_cache &c, int n_q_heads, int q_len);
+// Chunk tokens of the fast kernel for these strides (0: the kernel does not
+// take them); a cache stored in chunk blocks of this size decodes on it.
+namespace fast {
+int fast_chunk_tokens(int stride_k, int stride_v, int page_tokens);
+}
 size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len, int splits_req);
 int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, const void *q, int q_dtype,
                     int n_q_heads, int64_t q_sb, int64_t q_sh, float scale, void *out, int out_dtype,

@@ -35,6 +35,9 @@ __device__ __forceinline__ int quantise_code(float q, float hl, bool zero_scale)
 template <int DTYPE>
 __global__ void __launch_bounds__(kEncodeWarps * 32) append_kernel(EncodeArgs A) {
   __shared__ uint32_t s_words[kEncodeWarps][32];
+  // a programmatically dependent successor (the decode kernel) may be
+  // scheduled now; it waits for this grid's completion before reading
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
   const CacheView &cv = A.cv;
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -65,14 +68,14 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) append_kernel(EncodeArgs A)
     xv[i] = (d < D) ? load_as_float(A.x[comp], xbase + s * A.ss[comp] + d, DTYPE) : 0.f;
   }
 
-  __half *kf_row = const_cast<__half *>(c.kf) + ((pg * cv.H + h) * c.apg + a) * (int64_t)D;
+  __half *kf_row = const_cast<__half *>(c.kf) + kf_index(c, cv.H, D, pg, h, a);
   if (phase == 0) {  // I-frame: token.astype(float16) (cache.py:103-105)
 #pragma unroll
     for (int i = 0; i < kMaxDimsPerLane; ++i) {
       int d = lane + 32 * i;
       if (d < D) kf_row[d] = __float2half_rn(xv[i]);
     }
-    if (c.stok && lane == 0) const_cast<__half *>(c.scales)[(pg * cv.H + h) * c.srow + tl] = __float2half_rn(0.f);
+    if (c.stok && lane == 0) const_cast<__half *>(c.scales)[scale_index(c, cv.H, pg, h, tl)] = __float2half_rn(0.f);
     return;
   }
 
@@ -143,11 +146,11 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) append_kernel(EncodeArgs A)
   }
   __syncwarp();
   const int pf = tl - a - 1;
-  uint32_t *code_row = const_cast<uint32_t *>(c.codes) + ((pg * cv.H + h) * c.ppg + pf) * (int64_t)W;
+  uint32_t *code_row = const_cast<uint32_t *>(c.codes) + code_index(c, cv.H, W, pg, h, pf);
   if (lane < W) code_row[lane] = sw[lane];
   if (lane == 0) {
     // scale.astype(float16) (codec.py:65, cache.py:116)
-    const_cast<__half *>(c.scales)[(pg * cv.H + h) * c.srow + (c.stok ? tl : pf)] = __float2half_rn(scale);
+    const_cast<__half *>(c.scales)[scale_index(c, cv.H, pg, h, c.stok ? tl : pf)] = __float2half_rn(scale);
   }
 }
 

@@ -75,8 +75,8 @@ __global__ void export_kernel(CacheView cv, int comp, int64_t nkf, int64_t npf, 
   const int64_t pg = page_of(cv, b, lp);
   const int a = tl / c.stride;
   const int pf = tl - a - 1;
-  uint32_t *crow = const_cast<uint32_t *>(c.codes) + ((pg * cv.H + h) * c.ppg + pf) * (int64_t)W;
-  __half *cscale = const_cast<__half *>(c.scales) + (pg * cv.H + h) * c.srow + (c.stok ? tl : pf);
+  uint32_t *crow = const_cast<uint32_t *>(c.codes) + code_index(c, cv.H, W, pg, h, pf);
+  __half *cscale = const_cast<__half *>(c.scales) + scale_index(c, cv.H, pg, h, c.stok ? tl : pf);
   uint32_t *rrow = pk_out + (bh * npf + j) * W;
   if (lane < W) {
     // natural word `lane` holds dims 8*lane .. 8*lane+7

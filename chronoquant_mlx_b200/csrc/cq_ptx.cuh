@@ -70,6 +70,29 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t *bar, uint32_t parity
   }
 }
 
+// Orders this thread's earlier generic-proxy accesses of shared memory before
+// later async-proxy (bulk copy) accesses: needed before a bulk copy refills a
+// buffer that plain loads just read.
+__device__ __forceinline__ void fence_proxy_async_smem() {
+  asm volatile("fence.proxy.async.shared::cta;" ::: "memory");
+}
+
+// Programmatic dependent launch: wait until the preceding kernel in the
+// stream has completed and its memory is visible (no-op when the launch has
+// no programmatic dependency), and allow the next kernel to be scheduled.
+__device__ __forceinline__ void grid_dependency_wait() { asm volatile("griddepcontrol.wait;" ::: "memory"); }
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// 1-D bulk copy global -> shared (32-bit shared-memory address), completion
+// counted on `bar` in bytes.  Addresses 16-byte aligned, size a multiple of 16.
+__device__ __forceinline__ void bulk_g2s_a(uint32_t dst_smem, const void *src_gmem, uint32_t bytes, uint64_t *bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(dst_smem),
+               "l"(src_gmem), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+
 // 1-D bulk copy global -> shared, completion counted on `bar` in bytes.
 // Addresses 16-byte aligned, size a multiple of 16.
 __device__ __forceinline__ void bulk_g2s(void *dst_smem, const void *src_gmem, uint32_t bytes, uint64_t *bar) {

@@ -32,7 +32,7 @@
 extern "C" {
 #endif
 
-#define CQ_ABI_VERSION 1
+#define CQ_ABI_VERSION 2
 
 /* status codes */
 #define CQ_OK 0
@@ -55,16 +55,31 @@ extern "C" {
 #define CQ_ORDER_MMA 1     /* word 2g+q, nibble j holds dim g + 64q + 8j (head_dim 128) */
 
 /*
- * One compressed component (K or V) of a paged cache.  Per page and head:
- *   keyframes fp16  [anchors_per_page][head_dim]
- *   codes     u32   [pframes_per_page][head_dim/8]
- *   scales    fp16  [scale_row]            (indexed per scale_index; multiple of 8)
- * Arrays are [n_pages][kv_heads][...] contiguous.  Token t of sequence b lives
- * in page block_table[b*max_pages + t/page_tokens] at tl = t % page_tokens;
- * it is an I-frame iff tl % stride == 0 (anchor slot tl/stride), else a
- * P-frame in code row tl - tl/stride - 1 anchored on slot tl/stride; its
- * scale sits at that row index (CQ_SCALE_BY_PFRAME) or at tl
- * (CQ_SCALE_BY_TOKEN, whose I-frame slots hold 0).
+ * One compressed component (K or V) of a paged cache.  Token t of sequence b
+ * lives in page pg = block_table[b*max_pages + t/page_tokens] at page-local
+ * position tl = t % page_tokens; it is an I-frame iff tl % stride == 0 (anchor
+ * slot tl/stride), else a P-frame in code row tl - tl/stride - 1 anchored on
+ * slot tl/stride; its scale sits at that row index (CQ_SCALE_BY_PFRAME) or
+ * at tl (CQ_SCALE_BY_TOKEN, whose I-frame slots hold 0).
+ *
+ * Addressing.  A page is cut into chunks of chunk_tokens tokens (a multiple
+ * of the stride dividing page_tokens; 0 = the whole page).  A chunk holds
+ * ac = chunk_tokens/stride anchor slots, pc = chunk_tokens - ac code rows and
+ * sc = chunk_tokens (by token) or pc (by P-frame) scale slots; page-local
+ * index i of an array falls in chunk i / (per-chunk count) at offset
+ * i % (per-chunk count):
+ *   keyframes fp16 + (pg*kv_heads + h)*keyframe_head_stride
+ *                  + chunk*keyframe_chunk_stride + offset*head_dim
+ *   codes     u32  + (pg*kv_heads + h)*code_head_stride
+ *                  + chunk*code_chunk_stride + offset*ceil(head_dim/8)
+ *   scales    fp16 + (pg*kv_heads + h)*scale_head_stride
+ *                  + chunk*scale_chunk_stride + offset
+ * Strides are in elements of each array; a head stride of 0 means the
+ * contiguous [n_pages][kv_heads][...] layout (anchors_per_page*head_dim,
+ * pframes_per_page*ceil(head_dim/8), scale_row).  The three arrays of both
+ * components may share one allocation: the cache's own layout stores, per
+ * (page, head, chunk), one block [K anchors][K codes][K scales][V anchors]
+ * [V codes][V scales], which a decode step reads with a single bulk copy.
  */
 typedef struct cq_component {
   int32_t stride;           /* I-frame period (cache.py:100) */
@@ -72,12 +87,16 @@ typedef struct cq_component {
   float dead_zone;          /* dead-zone ratio (codec.py:36-45) */
   int32_t anchors_per_page; /* page_tokens / stride */
   int32_t pframes_per_page; /* page_tokens - anchors_per_page */
-  int32_t scale_row;        /* padded scales per (page, head) */
+  int32_t scale_row;        /* scale slots per (page, head): >= page_tokens (by token) or pframes_per_page */
   int32_t code_order;       /* CQ_ORDER_* */
   int32_t scale_index;      /* CQ_SCALE_BY_* */
   void *keyframes;          /* fp16 */
   uint32_t *codes;
   void *scales;             /* fp16 */
+  int64_t keyframe_head_stride, code_head_stride, scale_head_stride;    /* 0: contiguous */
+  int32_t chunk_tokens;     /* 0: one chunk per page */
+  int32_t reserved;
+  int64_t keyframe_chunk_stride, code_chunk_stride, scale_chunk_stride;  /* unused with one chunk */
 } cq_component;
 
 typedef struct cq_paged_cache {
@@ -94,6 +113,12 @@ typedef struct cq_paged_cache {
 
 int cq_abi_version(void);
 const char *cq_last_error(void);
+
+/* Chunk size (tokens) in which a cache with these strides should store its
+ * pages for the sm_100a decode kernel (one bulk copy per chunk block), or 0
+ * when that kernel does not take these strides or head_dim (store one chunk
+ * per page).  No reference counterpart: the reference stores flat arrays. */
+int cq_decode_chunk_tokens(int32_t stride_k, int32_t stride_v, int32_t page_tokens, int32_t head_dim);
 
 /* Device-side error word: set (non-zero) when a bounded wait inside a kernel
  * gave up (1 = a stage never filled, 2 = a stage was never released); the
@@ -118,7 +143,8 @@ int cq_append(const cq_paged_cache *cache, const void *keys, int64_t k_sb, int64
  * mask anchored at the end (attention.py:8-20; no effect when q_len == 1);
  * causal == 0 lets every query see all T keys (mask=None).  out: [batch][n_q_heads][q_len]
  * [head_dim] contiguous, out_dtype CQ_F16/CQ_BF16/CQ_F32.  workspace: device
- * memory of at least cq_attention_workspace() bytes (split-KV partials);
+ * memory of at least cq_attention_workspace() bytes (split-KV partials and
+ * per-call-stamped completion words; its prior contents are ignored);
  * num_splits <= 0 picks a split count.  lse_out (optional, may be NULL):
  * fp32 [batch][n_q_heads][q_len] log-sum-exp of the scaled scores (natural
  * log), for merging sequence shards. */

@@ -39,7 +39,7 @@ def test_binding_covers_header():
 
 
 def test_abi_version():
-    assert _lib.lib().cq_abi_version() == 1
+    assert _lib.lib().cq_abi_version() == 2
 
 
 def _desc(**over):
