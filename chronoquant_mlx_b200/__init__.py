@@ -16,6 +16,7 @@ from .patch import (
     revert,
 )
 from .attention import chronoquant_sdpa
+from .graph import DecodeGraph
 
 __all__ = [
     "ChronoQuantCache",
@@ -25,4 +26,5 @@ __all__ = [
     "create_chronoquant_caches",
     "create_full_throttle_caches",
     "chronoquant_sdpa",
+    "DecodeGraph",
 ]

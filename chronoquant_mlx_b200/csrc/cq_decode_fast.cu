@@ -58,6 +58,7 @@ constexpr float LOG2E = 1.4426950408889634f;
 constexpr float LN2 = 0.6931471805599453f;
 constexpr long long WAIT_BUDGET = 1LL << 31;  // clock cycles (~1 s) before a wait gives up
 constexpr int ERR_TIMEOUT_FULL = 1;
+constexpr int ERR_LENGTH = 4;  // a device-resident length outside [1, mapped tokens]
 constexpr int kQaBytes = 16 * 8 * 4;  // per-warp q.anchor table: 16 anchors x 8 heads, fp32
 constexpr int kQnBytes = 8 * 32 * 8;  // per-warp natural-order query fragments
 
@@ -68,16 +69,15 @@ struct Params {
   int64_t q_sb, q_sh;
   float scale;
   int gqa;
-  int64_t T;
+  int64_t T;              // cached tokens (used when T_dev is null)
+  const int64_t *T_dev;   // else: read from device memory at launch (graph replays)
   int C;         // tokens per chunk
   int cpp;       // chunks per page
-  int cpu;       // chunks per (sequence, kv-head) unit = ceil(T / C)
-  int64_t tc;    // total chunks = units * cpu
   int nwarps;    // warps with work (<= tc)
   int ns;        // copy slots per warp
   int lsk, lsv;  // log2 of the strides
   // shared memory: [mbarriers][per-warp regions: ns slots + q.anchor table]
-  int off_fin, off_warp, warp_bytes, slot_bytes;
+  int off_fin, off_strad, off_warp, warp_bytes, slot_bytes;
   int o_kf[2], o_cd[2], o_sc[2];  // segment offsets within a slot
   const char *blk;                // chunk blocks: K keyframes base (bytes)
   int64_t phs;                    // bytes per (page, head)
@@ -95,6 +95,30 @@ struct Params {
 
 __device__ __forceinline__ int64_t warp_of_chunk(int64_t x, int64_t tc, int nwarps) {
   return ((x + 1) * nwarps + tc - 1) / tc - 1;
+}
+
+// Length-dependent plan of one launch: cached tokens, chunks per unit, total
+// chunks, and whether the range arithmetic fits 32 bits.  Fixed on the host,
+// or derived at launch from a device-resident length (the grid and workspace
+// are sized for the largest length the caller allows).
+struct Len {
+  int64_t T, tc;
+  int cpu, small;
+};
+
+// Warp owning chunk x, first chunk of warp w, unit of chunk x -- in 32-bit
+// arithmetic when the plan is small enough (the usual case).
+__device__ __forceinline__ int warp_of(const Params &p, const Len &L, int64_t x) {
+  if (L.small) return (int)(((uint32_t)x + 1u) * (uint32_t)p.nwarps + (uint32_t)L.tc - 1u) / (uint32_t)L.tc - 1;
+  return (int)warp_of_chunk(x, L.tc, p.nwarps);
+}
+__device__ __forceinline__ int64_t first_chunk(const Params &p, const Len &L, int w) {
+  if (L.small) return (int64_t)(((uint32_t)w * (uint32_t)L.tc) / (uint32_t)p.nwarps);
+  return (int64_t)w * L.tc / p.nwarps;
+}
+__device__ __forceinline__ int unit_of(const Len &L, int64_t x) {
+  if (L.small) return (int)((uint32_t)x / (uint32_t)L.cpu);
+  return (int)(x / L.cpu);
 }
 
 __device__ int g_fast_error;
@@ -115,9 +139,9 @@ __device__ __forceinline__ float q_scaled(const Params &p, int b, int hq, int d)
 struct Cursor {
   int unit, b, h, cu, lp, j;  // unit, its (sequence, head), chunk in unit, page in unit, chunk in page
   int64_t left;               // chunks left including the current one
-  __device__ void init(const Params &p, int64_t first, int64_t last) {
-    unit = (int)(first / p.cpu);
-    cu = (int)(first - (int64_t)unit * p.cpu);
+  __device__ void init(const Params &p, const Len &L, int64_t first, int64_t last) {
+    unit = (int)(first / L.cpu);
+    cu = (int)(first - (int64_t)unit * L.cpu);
     lp = cu / p.cpp;
     j = cu - lp * p.cpp;
     b = unit / p.cv.H;
@@ -125,14 +149,16 @@ struct Cursor {
     left = last - first;
   }
   __device__ bool valid() const { return left > 0; }
-  __device__ int nvalid(const Params &p) const { return (int)min((int64_t)p.C, p.T - (int64_t)cu * p.C); }
-  __device__ void next(const Params &p) {
+  __device__ int nvalid(const Params &p, const Len &L) const {
+    return (int)min((int64_t)p.C, L.T - (int64_t)cu * p.C);
+  }
+  __device__ void next(const Params &p, const Len &L) {
     ++cu;
     if (++j == p.cpp) {
       j = 0;
       ++lp;
     }
-    if (cu == p.cpu) {
+    if (cu == L.cpu) {
       cu = lp = j = 0;
       ++unit;
       if (++h == p.cv.H) {
@@ -457,23 +483,32 @@ __device__ __forceinline__ void flush_global(const Params &p, WarpState &st, int
 // Per-warp partial kept in shared memory at the end of the warp's range:
 // [8] max, [8] sum, [8][HD] output (the warp's free copy slots hold it).
 constexpr int kFinFloats = 16 + 8 * HD;
+// Partials of the units a warp leaves inside its range (a unit boundary in
+// the middle of a warp's range; one warp per boundary) stay on chip too, for
+// the first kStrad units of the CTA's range; later ones go to global slots.
+constexpr int kStrad = 2;
+
+__device__ __forceinline__ int cta_first_unit(const Params &p, const Len &L, int cta) {
+  return unit_of(L, first_chunk(p, L, cta * p.nwc));
+}
 
 template <int NT>
-__device__ __forceinline__ void warp_main(const Params &p, unsigned char *smem, uint64_t *bar, int wg, int warp,
-                                          int lane) {
-  const int64_t first = (int64_t)wg * p.tc / p.nwarps;
-  const int64_t last = (int64_t)(wg + 1) * p.tc / p.nwarps;
+__device__ __forceinline__ void warp_main(const Params &p, const Len &L, unsigned char *smem, uint64_t *bar, int wg,
+                                          int warp, int lane) {
+  const int64_t first = first_chunk(p, L, wg);
+  const int64_t last = first_chunk(p, L, wg + 1);
   unsigned char *region = smem + p.off_warp + warp * p.warp_bytes;
   const uint32_t region_a = ptx::smem_u32(region);
+  const int u0 = cta_first_unit(p, L, blockIdx.x);
   float *qa = (float *)(region + p.ns * p.slot_bytes);
 
   Cursor ci, cc;
-  cc.init(p, first, last);
+  cc.init(p, L, first, last);
   ci = cc;
   for (int s = 0; s < p.ns && ci.valid(); ++s) {
     const int64_t pg = p.cv.block_table[(int64_t)ci.b * p.cv.max_pages + ci.lp];
     issue_chunk(p, region_a + s * p.slot_bytes, &bar[s], ci, pg, lane);
-    ci.next(p);
+    ci.next(p, L);
   }
 
   uint2 *qn = (uint2 *)(region + p.ns * p.slot_bytes + kQaBytes);
@@ -485,11 +520,19 @@ __device__ __forceinline__ void warp_main(const Params &p, unsigned char *smem, 
   int cur_unit = -1;
   int s = 0;
   uint32_t ph = 0;
-  for (; cc.valid(); cc.next(p)) {
+  for (; cc.valid(); cc.next(p, L)) {
     // page of the next chunk to issue, loaded early so its latency hides under this chunk
     const int64_t pg_next = ci.valid() ? (int64_t)p.cv.block_table[(int64_t)ci.b * p.cv.max_pages + ci.lp] : 0;
     if (cc.unit != cur_unit) {
-      if (cur_unit >= 0) flush_global(p, st, (int64_t)wg + cur_unit, lane);
+      if (cur_unit >= 0) {
+        const int a = cur_unit - u0;
+        if (a < kStrad) {
+          float *sp = (float *)(smem + p.off_strad) + a * kFinFloats;
+          flush_to(p, st, sp, sp + 8, sp + 16, lane);
+        } else {
+          flush_global(p, st, (int64_t)wg + cur_unit, lane);
+        }
+      }
       cur_unit = cc.unit;
       load_q(p, cc.b, cc.h, lane, f, qn);
       __syncwarp();
@@ -500,7 +543,7 @@ __device__ __forceinline__ void warp_main(const Params &p, unsigned char *smem, 
       return;
     }
     const uint32_t sa = region_a + s * p.slot_bytes;
-    const int nvalid = cc.nvalid(p);
+    const int nvalid = cc.nvalid(p, L);
     const LaneAddr A(p, sa, qa_a, lane);
     // tiles in groups of two (one softmax update per 32 tokens)
     if (nvalid == p.C) {
@@ -518,7 +561,7 @@ __device__ __forceinline__ void warp_main(const Params &p, unsigned char *smem, 
     ptx::fence_proxy_async_smem();
     if (ci.valid()) {
       issue_chunk(p, sa, &bar[s], ci, pg_next, lane);
-      ci.next(p);
+      ci.next(p, L);
     }
     if (++s == p.ns) {
       s = 0;
@@ -545,63 +588,84 @@ __device__ __forceinline__ void fence_acq_rel_gpu() { asm volatile("fence.acq_re
 // The CTA that completes
 // a unit merges the unit's CTA partials into the output rows of its query
 // heads (and their log-sum-exp) while other CTAs may still be working.
-__device__ void finish_units(const Params &p, unsigned char *smem) {
+__device__ void finish_units(const Params &p, const Len &L, unsigned char *smem) {
   __shared__ int s_n;
   __shared__ float s_w[kMaxWarps][8];  // per (warp, head): weight exp2(m_w - M)
   __shared__ float s_ML[8][2];         // per head: M, L
-  __shared__ const float *s_src[kMaxWarps][3];
+  __shared__ int s_glob[kMaxWarps];    // the warp's partial of this unit is in global memory
+  __shared__ int s_src[kMaxWarps];     // else: float offset of its on-chip partial
   const int G = p.gqa;
   const int *fin_unit = (const int *)(smem + p.off_fin);
   const int w0 = blockIdx.x * p.nwc;
   const int w1 = min(w0 + p.nwc, p.nwarps) - 1;
-  const int64_t first = (int64_t)w0 * p.tc / p.nwarps;
-  const int64_t last = (int64_t)(w1 + 1) * p.tc / p.nwarps;
-  const int u0 = (int)(first / p.cpu), nu = (int)((last - 1) / p.cpu) - u0 + 1;
+  const int64_t cfirst = first_chunk(p, L, w0), clast = first_chunk(p, L, w1 + 1);
+  if (clast <= cfirst) return;  // no chunks in this CTA's range (short cache, large grid)
+  const int u0 = unit_of(L, cfirst), nu = unit_of(L, clast - 1) - u0 + 1;
   int *s_list = (int *)(smem + p.off_warp + 8192);  // warp 0's region, past its on-chip partial
+  const int wstride = p.warp_bytes / 4;             // floats between two warps' on-chip partials
+  const float *smf = (const float *)smem;
 
   // ---- CTA merge
   for (int k = 0; k < nu; ++k) {
     const int u = u0 + k;
-    const int lo = (int)warp_of_chunk((int64_t)u * p.cpu, p.tc, p.nwarps);
-    const int hi = (int)warp_of_chunk((int64_t)u * p.cpu + p.cpu - 1, p.tc, p.nwarps);
+    const int lo = warp_of(p, L, (int64_t)u * L.cpu);
+    const int hi = warp_of(p, L, (int64_t)u * L.cpu + L.cpu - 1);
     const int wa = max(lo, w0), nw = min(hi, w1) - wa + 1;
     const bool whole = lo >= w0 && hi <= w1;
-    // sources of the partials of u: on chip (the warp's last unit) or global
+    const int fin0 = p.off_warp / 4 + (wa - w0) * wstride;  // float offset of warp wa's on-chip partial
+    // where each warp's partial of u lives: its on-chip last-unit partial, the
+    // CTA's on-chip boundary partial of u, or a global slot
     if (threadIdx.x < nw) {
-      const int w = wa + threadIdx.x;
-      if (fin_unit[w - w0] == u) {
-        const float *fin = (const float *)(smem + p.off_warp + (w - w0) * p.warp_bytes);
-        s_src[threadIdx.x][0] = fin;
-        s_src[threadIdx.x][1] = fin + 8;
-        s_src[threadIdx.x][2] = fin + 16;
-      } else {
-        const int64_t i = ((int64_t)w + u) * G;
-        s_src[threadIdx.x][0] = p.ws_m + i;
-        s_src[threadIdx.x][1] = p.ws_l + i;
-        s_src[threadIdx.x][2] = p.ws_o + i * HD;
-      }
+      const int j = threadIdx.x, w = wa + j;
+      int src = -1;  // float offset of the on-chip partial: [8] max, [8] sum, [8][HD] output
+      if (fin_unit[w - w0] == u)
+        src = fin0 + j * wstride;
+      else if (k < kStrad)
+        src = p.off_strad / 4 + k * kFinFloats;
+      s_src[j] = src;
+      s_glob[j] = src < 0;
     }
     __syncthreads();
-    if (threadIdx.x < G) {  // per head: M, L and the warps' weights
-      const int hh = threadIdx.x;
-      float M = -INFINITY;
-      for (int j = 0; j < nw; ++j) M = fmaxf(M, s_src[j][0][hh]);
-      float L = 0.f;
-      for (int j = 0; j < nw; ++j) {
-        const float m = s_src[j][0][hh];
-        const float f = (m == -INFINITY) ? 0.f : fast_exp2(m - M);
-        s_w[j][hh] = f;
-        L += s_src[j][1][hh] * f;
+    // per head: 16 lanes, one per warp (shuffle reductions stay inside each half-warp)
+    if (threadIdx.x < ((G * 16 + 31) & ~31)) {  // whole warps: the shuffles use every lane
+      const int hh = threadIdx.x >> 4, j = threadIdx.x & 15;
+      float m = -INFINITY, l = 0.f;
+      if (hh < G && j < nw) {
+        if (s_glob[j]) {
+          const int64_t i = ((int64_t)wa + j + u) * G + hh;
+          m = p.ws_m[i];
+          l = p.ws_l[i];
+        } else {
+          m = smf[s_src[j] + hh];
+          l = smf[s_src[j] + 8 + hh];
+        }
       }
-      s_ML[hh][0] = M;
-      s_ML[hh][1] = L;
+      float M = m;
+#pragma unroll
+      for (int o = 8; o; o >>= 1) M = fmaxf(M, __shfl_xor_sync(0xffffffffu, M, o));
+      const float f = (m == -INFINITY) ? 0.f : fast_exp2(m - M);
+      float L = l * f;
+#pragma unroll
+      for (int o = 8; o; o >>= 1) L += __shfl_xor_sync(0xffffffffu, L, o);
+      if (hh < G) s_w[j][hh] = f;
+      if (hh < G && j == 0) {
+        s_ML[hh][0] = M;
+        s_ML[hh][1] = L;
+      }
     }
     __syncthreads();
     const int b = u / p.cv.H, h = u - b * p.cv.H;
     for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
       const int hh = idx / HD, d = idx - hh * HD;
       float acc = 0.f;
-      for (int j = 0; j < nw; ++j) acc += s_src[j][2][hh * HD + d] * s_w[j][hh];
+#pragma unroll
+      for (int j = 0; j < kMaxWarps; ++j) {  // fixed bound: all loads issue before they are used
+        if (j < nw) {
+          const float o =
+              s_glob[j] ? p.ws_o[(((int64_t)wa + j + u) * G + hh) * HD + d] : smf[s_src[j] + 16 + hh * HD + d];
+          acc += o * s_w[j][hh];
+        }
+      }
       const float M = s_ML[hh][0], L = s_ML[hh][1];
       if (whole) {
         const int64_t row = (int64_t)b * p.Hq + h * G + hh;
@@ -620,15 +684,15 @@ __device__ void finish_units(const Params &p, unsigned char *smem) {
   }
 
   // ---- cross-CTA completion, in rounds of blockDim.x units
-  fence_acq_rel_gpu();  // release this thread's CTA-partial writes
   for (int base = 0; base < nu; base += blockDim.x) {
     if (threadIdx.x == 0) s_n = 0;
-    __syncthreads();
+    __syncthreads();  // the CTA's partial writes happen before the counting threads' release
     const int k = base + threadIdx.x;
     if (k < nu) {
+      fence_acq_rel_gpu();  // release, cumulative over the barrier above
       const int u = u0 + k;
-      const int c_lo = (int)(warp_of_chunk((int64_t)u * p.cpu, p.tc, p.nwarps) / p.nwc);
-      const int c_hi = (int)(warp_of_chunk((int64_t)u * p.cpu + p.cpu - 1, p.tc, p.nwarps) / p.nwc);
+      const int c_lo = warp_of(p, L, (int64_t)u * L.cpu) / p.nwc;
+      const int c_hi = warp_of(p, L, (int64_t)u * L.cpu + L.cpu - 1) / p.nwc;
       if (c_hi > c_lo) {
         // add first (one round trip when the word already carries this call's
         // stamp); a word with another stamp is reset to this call's by CAS,
@@ -650,7 +714,10 @@ __device__ void finish_units(const Params &p, unsigned char *smem) {
             cur = prev;
           }
         }
-        if (cnt == (unsigned long long)(c_hi - c_lo + 1)) s_list[atomicAdd(&s_n, 1)] = u;
+        if (cnt == (unsigned long long)(c_hi - c_lo + 1)) {
+          s_list[atomicAdd(&s_n, 1)] = u;
+          *w = 0ull;  // every CTA of u has counted: reset, so a replay of the same launch starts from zero
+        }
       }
     }
     __syncthreads();
@@ -658,8 +725,8 @@ __device__ void finish_units(const Params &p, unsigned char *smem) {
     if (n) fence_acq_rel_gpu();  // acquire: other CTAs' partials are read after their counts
     for (int e = 0; e < n; ++e) {
       const int u = s_list[e];
-      const int c_lo = (int)(warp_of_chunk((int64_t)u * p.cpu, p.tc, p.nwarps) / p.nwc);
-      const int c_hi = (int)(warp_of_chunk((int64_t)u * p.cpu + p.cpu - 1, p.tc, p.nwarps) / p.nwc);
+      const int c_lo = warp_of(p, L, (int64_t)u * L.cpu) / p.nwc;
+      const int c_hi = warp_of(p, L, (int64_t)u * L.cpu + L.cpu - 1) / p.nwc;
       const int b = u / p.cv.H, h = u - b * p.cv.H;
       const int np = c_hi - c_lo + 1;
       for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
@@ -711,13 +778,28 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const __grid_
     ptx::fence_mbar_init();
     ((int *)(smem + p.off_fin))[warp] = -1;  // warps without work contribute nothing
   }
-  __syncwarp();
-  // inputs (query, block table, cache pages) may come from the preceding kernel
+  // inputs (query, block table, cache pages, the length) may come from the preceding kernel
   ptx::grid_dependency_wait();
-  const int wg = blockIdx.x * nwc + warp;
-  if (wg < p.nwarps) warp_main<NT>(p, smem, bar, wg, warp, lane);
+  __shared__ Len s_len;
+  if (threadIdx.x == 0) {
+    Len L;
+    L.T = p.T_dev ? *p.T_dev : p.T;
+    if (L.T < 1 || L.T > (int64_t)p.cv.max_pages * p.cv.P) {
+      if (blockIdx.x == 0) atomicExch(&g_fast_error, ERR_LENGTH);
+      L.T = 0;
+    }
+    L.cpu = (int)((L.T + p.C - 1) / p.C);
+    L.tc = (int64_t)p.cv.B * p.cv.H * L.cpu;
+    L.small = (uint64_t)L.tc * (uint64_t)(p.nwarps + 1) < (1ull << 32);
+    s_len = L;
+  }
   __syncthreads();
-  finish_units(p, smem);
+  const Len L = s_len;
+  if (L.T == 0) return;  // no length: nothing written (the error word says why)
+  const int wg = blockIdx.x * nwc + warp;
+  if (wg < p.nwarps) warp_main<NT>(p, L, smem, bar, wg, warp, lane);
+  __syncthreads();
+  finish_units(p, L, smem);
 }
 
 // ---------------------------------------------------------------------------
@@ -730,7 +812,7 @@ static int up128(int x) { return (x + 127) & ~127; }
 
 struct Layout {
   int C, ns, nwc, lsk, lsv;
-  int o_kf[2], o_cd[2], o_sc[2], slot_bytes, warp_bytes, off_fin, off_warp, total;
+  int o_kf[2], o_cd[2], o_sc[2], slot_bytes, warp_bytes, off_fin, off_strad, off_warp, total;
   int64_t phs;  // bytes per (page, head)
 };
 
@@ -802,7 +884,8 @@ static bool make_layout(const cq_paged_cache &c, Layout &L) {
   L.warp_bytes = std::max(L.ns * L.slot_bytes, 8192 + 4 * kMaxWarps * 32) + kQaBytes + kQnBytes;
   static_assert(kFinFloats * 4 <= 8192, "on-chip partial must fit below the unit list");
   L.off_fin = kMaxWarps * 4 * 8;  // after the mbarriers [warp][slot]: each warp's last unit
-  L.off_warp = up128(L.off_fin + kMaxWarps * 4);
+  L.off_strad = up128(L.off_fin + kMaxWarps * 4);
+  L.off_warp = up128(L.off_strad + kStrad * kFinFloats * 4);
   L.nwc = std::min(kMaxWarps, (kMaxSmem - L.off_warp) / L.warp_bytes);
   L.total = L.off_warp + L.nwc * L.warp_bytes;
   return L.nwc >= 4;
@@ -864,8 +947,9 @@ size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, 
 
 int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, const void *q, int q_dtype,
                     int n_q_heads, int64_t q_sb, int64_t q_sh, float scale, void *out, int out_dtype, float *lse_out,
-                    void *ws, size_t ws_bytes, int splits_req, cudaStream_t st) {
+                    void *ws, size_t ws_bytes, int splits_req, cudaStream_t st, const int64_t *T_dev) {
   Params p;
+  p.T_dev = T_dev;  // when set, T is the largest length the launch is sized for
   p.cv = cv;
   p.q = q;
   p.q_dtype = q_dtype;
@@ -878,13 +962,12 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
   const Layout &L = pl.L;
   p.C = L.C;
   p.cpp = c.page_tokens / L.C;
-  p.cpu = pl.cpu;
-  p.tc = pl.tc;
   p.nwarps = pl.nwarps;
   p.ns = L.ns;
   p.lsk = L.lsk;
   p.lsv = L.lsv;
   p.off_fin = L.off_fin;
+  p.off_strad = L.off_strad;
   p.off_warp = L.off_warp;
   p.warp_bytes = L.warp_bytes;
   p.slot_bytes = L.slot_bytes;
@@ -959,9 +1042,9 @@ size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, 
 }
 int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, const void *q, int q_dtype, int n_q_heads,
                     int64_t q_sb, int64_t q_sh, float scale, void *out, int out_dtype, float *lse_out, void *ws,
-                    size_t ws_bytes, int splits_req, cudaStream_t st) {
+                    size_t ws_bytes, int splits_req, cudaStream_t st, const int64_t *T_dev) {
   return fast::run_fast_decode(c, cv, T, q, q_dtype, n_q_heads, q_sb, q_sh, scale, out, out_dtype, lse_out, ws,
-                               ws_bytes, splits_req, st);
+                               ws_bytes, splits_req, st, T_dev);
 }
 
 // Read (and optionally clear) the device-side error word the fast kernel sets
@@ -983,9 +1066,14 @@ extern "C" int cq_decode_chunk_tokens(int32_t stride_k, int32_t stride_v, int32_
   return cq::fast::fast_chunk_tokens(stride_k, stride_v, page_tokens);
 }
 
+namespace cq {
+int read_append_error(int clear);
+}
+
 extern "C" int cq_device_error(int *code, int clear) {
   if (!code) return cq::set_error(CQ_ERR_INVALID, "cq_device_error: code is null");
-  *code = cq::read_fast_error(clear);
+  const int a = cq::read_fast_error(clear), b = cq::read_append_error(clear);
+  *code = a ? a : b;
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cq::set_error(CQ_ERR_CUDA, cudaGetErrorString(e));
   return CQ_OK;

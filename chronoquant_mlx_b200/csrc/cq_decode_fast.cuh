@@ -13,8 +13,11 @@ namespace fast {
 int fast_chunk_tokens(int stride_k, int stride_v, int page_tokens);
 }
 size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len, int splits_req);
+// T_dev != nullptr: the length is read from device memory at launch and T is
+// the largest length the launch (grid, workspace) is sized for.
 int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, const void *q, int q_dtype,
                     int n_q_heads, int64_t q_sb, int64_t q_sh, float scale, void *out, int out_dtype,
-                    float *lse_out, void *ws, size_t ws_bytes, int splits_req, cudaStream_t st);
+                    float *lse_out, void *ws, size_t ws_bytes, int splits_req, cudaStream_t st,
+                    const int64_t *T_dev = nullptr);
 
 }  // namespace cq

@@ -21,7 +21,13 @@ struct EncodeArgs {
   int64_t sb[2], sh[2], ss[2];
   int64_t t0;
   int S;
+  // device-resident length (graph replays): t0 = len[0]; the last block to
+  // finish advances len[0] by S and resets the arrival counter len[1]
+  int64_t *len;
 };
+
+__device__ int g_append_error;
+constexpr int ERR_APPEND_RANGE = 5;  // tokens past the mapped pages
 
 // Quantise one residual value (codec.py:48-54).  `q` is the dtype-rounded
 // quotient delta/scale_safe.
@@ -33,11 +39,46 @@ __device__ __forceinline__ int quantise_code(float q, float hl, bool zero_scale)
 }
 
 template <int DTYPE>
+__device__ __forceinline__ void encode_token(const EncodeArgs &A, int64_t t0, uint32_t *sw);
+
+template <int DTYPE>
 __global__ void __launch_bounds__(kEncodeWarps * 32) append_kernel(EncodeArgs A) {
   __shared__ uint32_t s_words[kEncodeWarps][32];
+  __shared__ int64_t s_t0;
   // a programmatically dependent successor (the decode kernel) may be
   // scheduled now; it waits for this grid's completion before reading
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+  if (threadIdx.x == 0) {
+    int64_t t0 = A.t0;
+    if (A.len) {
+      t0 = *(volatile int64_t *)A.len;
+      if (t0 < 0 || (t0 + A.S - 1) / A.cv.P >= A.cv.max_pages) {
+        atomicExch(&g_append_error, ERR_APPEND_RANGE);
+        t0 = -1;
+      }
+    }
+    s_t0 = t0;
+  }
+  __syncthreads();
+  const int64_t t0 = s_t0;
+  if (t0 >= 0) encode_token<DTYPE>(A, t0, s_words[threadIdx.x >> 5]);
+  if (A.len) {
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      unsigned long long *arrive = (unsigned long long *)(A.len + 1);
+      if (atomicAdd(arrive, 1ull) == gridDim.x - 1) {  // every block has read the old length
+        if (t0 >= 0) *(volatile int64_t *)A.len = t0 + A.S;
+        *arrive = 0ull;
+      }
+    }
+  }
+}
+
+// Encode the token of this warp: component, sequence, kv-head and position
+// t0 + s from the warp index.
+template <int DTYPE>
+__device__ __forceinline__ void encode_token(const EncodeArgs &A, int64_t t0, uint32_t *sw) {
   const CacheView &cv = A.cv;
   const int lane = threadIdx.x & 31;
   const int wib = threadIdx.x >> 5;
@@ -53,7 +94,7 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) append_kernel(EncodeArgs A)
   const CompView &c = cv.c[comp];
   const int D = cv.D;
 
-  const int64_t t = A.t0 + s;
+  const int64_t t = t0 + s;
   const int64_t lp = t / cv.P;
   const int tl = (int)(t - lp * cv.P);
   const int64_t pg = page_of(cv, b, lp);
@@ -88,8 +129,8 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) append_kernel(EncodeArgs A)
     int d = lane + 32 * i;
     float v = 0.f;
     if (d < D) {
-      if (ta >= A.t0)
-        v = __half2float(__float2half_rn(load_as_float(A.x[comp], xbase + (ta - A.t0) * A.ss[comp] + d, DTYPE)));
+      if (ta >= t0)
+        v = __half2float(__float2half_rn(load_as_float(A.x[comp], xbase + (ta - t0) * A.ss[comp] + d, DTYPE)));
       else
         v = __half2float(kf_row[d]);
     }
@@ -128,7 +169,6 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) append_kernel(EncodeArgs A)
   const bool zero_scale = scale < tiny;
   const float scale_safe = zero_scale ? 1.f : scale;
 
-  uint32_t *sw = s_words[wib];
   const int W = words_of(D);
   sw[lane] = 0u;
   __syncwarp();
@@ -154,21 +194,19 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) append_kernel(EncodeArgs A)
   }
 }
 
-}  // namespace cq
-
-using namespace cq;
-
-extern "C" int cq_append(const cq_paged_cache *cache, const void *keys, int64_t k_sb, int64_t k_sh, int64_t k_ss,
+static int launch_append(const cq_paged_cache *cache, const void *keys, int64_t k_sb, int64_t k_sh, int64_t k_ss,
                          const void *values, int64_t v_sb, int64_t v_sh, int64_t v_ss, int dtype, int64_t t0,
-                         int32_t S, void *stream) {
+                         int64_t *len, int32_t S, void *stream, const char *who) {
   int r = validate_cache(cache);
   if (r) return r;
-  CQ_REQUIRE(keys && values, CQ_ERR_INVALID, "cq_append: keys/values null");
-  CQ_REQUIRE(dtype == CQ_F16 || dtype == CQ_BF16, CQ_ERR_UNSUPPORTED, "cq_append: dtype must be f16 or bf16");
-  CQ_REQUIRE(S >= 0 && t0 >= 0, CQ_ERR_INVALID, "cq_append: negative S or t0");
+  CQ_REQUIRE(keys && values, CQ_ERR_INVALID, std::string(who) + ": keys/values null");
+  CQ_REQUIRE(dtype == CQ_F16 || dtype == CQ_BF16, CQ_ERR_UNSUPPORTED, std::string(who) + ": dtype must be f16 or bf16");
+  CQ_REQUIRE(S >= 0 && t0 >= 0, CQ_ERR_INVALID, std::string(who) + ": negative S or t0");
   if (S == 0) return CQ_OK;
-  int64_t last_page = (t0 + S - 1) / cache->page_tokens;
-  CQ_REQUIRE(last_page < cache->max_pages, CQ_ERR_INVALID, "cq_append: tokens beyond max_pages*page_tokens");
+  if (!len) {
+    int64_t last_page = (t0 + S - 1) / cache->page_tokens;
+    CQ_REQUIRE(last_page < cache->max_pages, CQ_ERR_INVALID, std::string(who) + ": tokens beyond max_pages*page_tokens");
+  }
   EncodeArgs A;
   A.cv = make_view(*cache);
   A.x[0] = keys;
@@ -177,13 +215,44 @@ extern "C" int cq_append(const cq_paged_cache *cache, const void *keys, int64_t 
   A.sb[1] = v_sb; A.sh[1] = v_sh; A.ss[1] = v_ss;
   A.t0 = t0;
   A.S = S;
+  A.len = len;
   int64_t warps = 2LL * cache->batch * cache->kv_heads * S;
   int64_t blocks = (warps + kEncodeWarps - 1) / kEncodeWarps;
-  CQ_REQUIRE(blocks < (1LL << 31), CQ_ERR_INVALID, "cq_append: too many tokens in one call");
+  CQ_REQUIRE(blocks < (1LL << 31), CQ_ERR_INVALID, std::string(who) + ": too many tokens in one call");
   cudaStream_t st = (cudaStream_t)stream;
   if (dtype == CQ_F16)
     append_kernel<CQ_F16><<<(unsigned)blocks, kEncodeWarps * 32, 0, st>>>(A);
   else
     append_kernel<CQ_BF16><<<(unsigned)blocks, kEncodeWarps * 32, 0, st>>>(A);
-  return check_launch("cq_append");
+  return check_launch(who);
+}
+
+// Read (and optionally clear) the append kernel's device error word.
+int read_append_error(int clear) {
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_append_error, sizeof(int));
+  if (clear) {
+    int z = 0;
+    cudaMemcpyToSymbol(g_append_error, &z, sizeof(int));
+  }
+  return v;
+}
+
+}  // namespace cq
+
+using namespace cq;
+
+extern "C" int cq_append(const cq_paged_cache *cache, const void *keys, int64_t k_sb, int64_t k_sh, int64_t k_ss,
+                         const void *values, int64_t v_sb, int64_t v_sh, int64_t v_ss, int dtype, int64_t t0,
+                         int32_t S, void *stream) {
+  return launch_append(cache, keys, k_sb, k_sh, k_ss, values, v_sb, v_sh, v_ss, dtype, t0, nullptr, S, stream,
+                       "cq_append");
+}
+
+extern "C" int cq_append_at(const cq_paged_cache *cache, const void *keys, int64_t k_sb, int64_t k_sh, int64_t k_ss,
+                            const void *values, int64_t v_sb, int64_t v_sh, int64_t v_ss, int dtype, int64_t *len_dev,
+                            int32_t S, void *stream) {
+  CQ_REQUIRE(len_dev, CQ_ERR_INVALID, "cq_append_at: len_dev is null");
+  return launch_append(cache, keys, k_sb, k_sh, k_ss, values, v_sb, v_sh, v_ss, dtype, 0, len_dev, S, stream,
+                       "cq_append_at");
 }

@@ -120,10 +120,11 @@ const char *cq_last_error(void);
  * per page).  No reference counterpart: the reference stores flat arrays. */
 int cq_decode_chunk_tokens(int32_t stride_k, int32_t stride_v, int32_t page_tokens, int32_t head_dim);
 
-/* Device-side error word: set (non-zero) when a bounded wait inside a kernel
- * gave up (1 = a stage never filled, 2 = a stage was never released); the
- * kernel then returned early instead of hanging.  Synchronises the device;
- * clear != 0 resets the word. */
+/* Device-side error word: set (non-zero) when a kernel gave up instead of
+ * hanging or writing out of range: 1 = a bulk copy never landed (bounded
+ * wait), 4 = a device-resident length outside [1, mapped tokens] (attention
+ * wrote nothing), 5 = a device-resident append past the mapped pages (append
+ * wrote nothing).  Synchronises the device; clear != 0 resets the word. */
 int cq_device_error(int *code, int clear);
 
 /* Encode S new tokens at absolute positions t0..t0+S-1 for K and V in one
@@ -154,6 +155,25 @@ int cq_attention(const cq_paged_cache *cache, int64_t T, const void *q, int q_dt
                  void *stream);
 int cq_attention_workspace(const cq_paged_cache *cache, int64_t T, int32_t n_q_heads, int32_t q_len,
                            int32_t num_splits, size_t *bytes);
+
+/* A decode step that a CUDA graph can replay at any length (no reference
+ * counterpart: the reference steps eagerly from Python, cache.py:198-215 and
+ * attention.py:23-74).  len_dev: device int64[2] = {tokens cached, arrival
+ * counter}, zero-initialised by the caller; neither call reads the length on
+ * the host.  cq_append_at encodes S tokens at positions len_dev[0].. (as
+ * cq_append) and, when its grid completes, advances len_dev[0] by S and leaves
+ * the counter at 0.  cq_attention_at is cq_attention for q_len 1 over
+ * len_dev[0] tokens; its grid and workspace are sized for max_len tokens
+ * (query cq_attention_workspace with T = max_len).  It needs the cache layout
+ * of the sm_100a decode kernel (cq_decode_chunk_tokens) and answers
+ * CQ_ERR_UNSUPPORTED otherwise.  A length outside the mapped pages makes the
+ * kernels write nothing and set cq_device_error. */
+int cq_append_at(const cq_paged_cache *cache, const void *keys, int64_t k_sb, int64_t k_sh, int64_t k_ss,
+                 const void *values, int64_t v_sb, int64_t v_sh, int64_t v_ss, int dtype, int64_t *len_dev,
+                 int32_t S, void *stream);
+int cq_attention_at(const cq_paged_cache *cache, const int64_t *len_dev, int64_t max_len, const void *q, int q_dtype,
+                    int32_t n_q_heads, int64_t q_sb, int64_t q_sh, float scale, void *out, int out_dtype,
+                    float *lse_out, void *workspace, size_t workspace_bytes, void *stream);
 
 /* cq_attention with an explicit mask instead of the implicit causal rule
  * (attention.py:8-20 for array masks): mask_kind 1 = boolean uint8 (nonzero
