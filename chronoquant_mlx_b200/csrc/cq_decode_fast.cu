@@ -6,11 +6,14 @@
 // math.  Here a warp streams chunks (32 or 64 tokens) of one (sequence,
 // kv-head) unit and serves every query head of the GQA group from one read.
 //
-// Every warp runs its own copy pipeline: `ns` private shared-memory slots,
-// each filled by 1-D bulk-async copies (the TMA engine) of one chunk's K/V
-// anchors, code rows and per-token scales, completion counted on the slot's
-// mbarrier.  A warp waits only for its own copies, never for other warps, and
-// refills a slot as soon as it has consumed it.  Per chunk:
+// Every warp runs its own copy pipeline: two private shared-memory slots, each
+// filled by one 1-D bulk-async copy (the TMA engine) of a chunk block -- the
+// chunk's K/V anchors, code rows and per-token scales, stored contiguously by
+// the cache -- completion counted on the slot's mbarrier.  A warp waits only
+// for its own copies, never for other warps, and refills a slot as soon as it
+// has consumed it.  The kernel is instantiated per (stride_k, stride_v) pair,
+// so the chunk geometry and every shared-memory offset are compile-time
+// constants.  Per chunk:
 //
 //   q.anchor  for the chunk's K anchors, one tensor-core MMA tile (rows =
 //             anchors), kept in a small per-warp table;
@@ -34,10 +37,10 @@
 // output rows -- one launch per decode step.
 //
 // Requirements (fast_decode_supported): q_len 1, head_dim 128, GQA group <= 8,
-// a chunk size (lcm of 16 and both strides, at least 32) of at most 64 tokens
-// that divides page_tokens, at most 16 K anchors per chunk, K codes in the
-// natural and V codes in the MMA nibble order, token-indexed scales, 16-byte
-// aligned arrays.
+// power-of-two strides with stride_k in {16, 32, 64} and stride_v in
+// {8, .., 64} (chunk = max(32, strides) tokens dividing page_tokens), the
+// cache's chunk-block layout for that geometry, K codes in the natural and V
+// codes in the MMA nibble order, token-indexed scales.
 #include <algorithm>
 #include <atomic>
 #include <cstdlib>
@@ -61,6 +64,32 @@ constexpr int ERR_TIMEOUT_FULL = 1;
 constexpr int ERR_LENGTH = 4;  // a device-resident length outside [1, mapped tokens]
 constexpr int kQaBytes = 16 * 8 * 4;  // per-warp q.anchor table: 16 anchors x 8 heads, fp32
 constexpr int kQnBytes = 8 * 32 * 8;  // per-warp natural-order query fragments
+constexpr int kNS = 2;                // copy slots per warp
+
+constexpr int cx_log2(int x) { return x <= 1 ? 0 : 1 + cx_log2(x >> 1); }
+constexpr int cx_up16(int x) { return (x + 15) & ~15; }
+constexpr int cx_max(int a, int b) { return a > b ? a : b; }
+
+// Compile-time geometry of one (stride_k, stride_v) pair: chunk tokens, tiles
+// per chunk, anchors per chunk and the byte offsets of a chunk block's six
+// segments [K anchors][K codes][K scales][V anchors][V codes][V scales]
+// (each 16-byte aligned) -- the layout the cache stores and a slot mirrors.
+template <int SK_, int SV_>
+struct Geo {
+  static constexpr int SK = SK_, SV = SV_;
+  static constexpr int LSK = cx_log2(SK), LSV = cx_log2(SV);
+  static constexpr int C = cx_max(32, cx_max(SK, SV));
+  static constexpr int NT = C / 16;
+  static constexpr int AK = C / SK, AV = C / SV;
+  static constexpr int O_KF0 = 0;
+  static constexpr int O_CD0 = cx_up16(O_KF0 + AK * HD * 2);
+  static constexpr int O_SC0 = cx_up16(O_CD0 + (C - AK) * (HD / 2));
+  static constexpr int O_KF1 = cx_up16(O_SC0 + C * 2);
+  static constexpr int O_CD1 = cx_up16(O_KF1 + AV * HD * 2);
+  static constexpr int O_SC1 = cx_up16(O_CD1 + (C - AV) * (HD / 2));
+  static constexpr int SLOT = cx_up16(O_SC1 + C * 2);
+  static_assert(SK >= 16 && SV >= 8 && C <= 64 && AK <= 16, "geometry outside the kernel's range");
+};
 
 struct Params {
   CacheView cv;
@@ -74,14 +103,10 @@ struct Params {
   int C;         // tokens per chunk
   int cpp;       // chunks per page
   int nwarps;    // warps with work (<= tc)
-  int ns;        // copy slots per warp
-  int lsk, lsv;  // log2 of the strides
   // shared memory: [mbarriers][per-warp regions: ns slots + q.anchor table]
-  int off_fin, off_strad, off_warp, warp_bytes, slot_bytes;
-  int o_kf[2], o_cd[2], o_sc[2];  // segment offsets within a slot
+  int off_fin, off_strad, off_warp, warp_bytes;
   const char *blk;                // chunk blocks: K keyframes base (bytes)
   int64_t phs;                    // bytes per (page, head)
-  int cs;                         // bytes per chunk block
   int nwc;                        // warps per CTA
   float *ws_m, *ws_l, *ws_o;      // warp partials: [nwarps + units][gqa], same, [nwarps + units][gqa][HD]
   float *cs_m, *cs_l, *cs_o;      // CTA partials: [grid + units][gqa], same, [grid + units][gqa][HD]
@@ -173,12 +198,13 @@ struct Cursor {
 // One bulk copy of a chunk's block (page `pg`) into `slot`, counted on
 // `bar`, issued by lane 0.  The whole block is copied even for the last,
 // partial chunk of a unit: the bytes past its valid tokens are masked.
+template <class G>
 __device__ __forceinline__ void issue_chunk(const Params &p, uint32_t slot, uint64_t *bar, const Cursor &c,
                                             int64_t pg, int lane) {
   if (lane != 0) return;
-  ptx::mbar_arrive_expect_tx(bar, (uint32_t)p.cs);
-  const char *src = p.blk + (pg * p.cv.H + c.h) * p.phs + (int64_t)c.j * p.cs;
-  ptx::bulk_g2s_a(slot, src, (uint32_t)p.cs, bar);
+  ptx::mbar_arrive_expect_tx(bar, (uint32_t)G::SLOT);
+  const char *src = p.blk + (pg * p.cv.H + c.h) * p.phs + (int64_t)c.j * G::SLOT;
+  ptx::bulk_g2s_a(slot, src, (uint32_t)G::SLOT, bar);
 }
 
 struct QFrag {
@@ -273,15 +299,16 @@ struct LaneAddr {
   uint32_t kfV0;  // V anchor row 0, same column half
   uint32_t qa;    // q.anchor table, heads 2t, 2t+1
   int dv8;        // V rows between tokens 2t and 2t+8
-  __device__ __forceinline__ LaneAddr(const Params &p, uint32_t sa, uint32_t qa_base, int lane) {
+  template <class G>
+  __device__ __forceinline__ LaneAddr(G, uint32_t sa, uint32_t qa_base, int lane) {
     const int g = lane >> 2, t = lane & 3, mi = lane >> 3;
-    const bool v8 = p.lsv == 3;
-    cdK = sa + p.o_cd[0] + (g - 1) * 64 + t * 16;
-    cdV = sa + p.o_cd[1] + (2 * t - 1) * 64 + g * 8;
+    constexpr bool v8 = G::LSV == 3;
+    cdK = sa + G::O_CD0 + (g - 1) * 64 + t * 16;
+    cdV = sa + G::O_CD1 + (2 * t - 1) * 64 + g * 8;
     dv8 = v8 ? 7 : 8;
-    scK = sa + p.o_sc[0] + g * 2;
-    scV = sa + p.o_sc[1] + g * 2;
-    kfV0 = sa + p.o_kf[1] + ((mi & 1) ? 16 : 0);
+    scK = sa + G::O_SC0 + g * 2;
+    scV = sa + G::O_SC1 + g * 2;
+    kfV0 = sa + G::O_KF1 + ((mi & 1) ? 16 : 0);
     kfV = kfV0 + ((v8 ? (mi >> 1) : 0) * (HD * 2));
     qa = qa_base + t * 8;
   }
@@ -294,9 +321,10 @@ __device__ __forceinline__ float lds_half_as_float(uint32_t a) {
 }
 
 // Two 16-token tiles starting at chunk-local token t0.
-template <bool MASK>
-__device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, const QFrag &f, int t0, int lsk,
-                                              int lsv, int nvalid, int lane) {
+template <class G, bool MASK>
+__device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, const QFrag &f, int t0, int nvalid,
+                                              int lane) {
+  constexpr int lsk = G::LSK, lsv = G::LSV;
   constexpr int NT = 2;
   const int g = lane >> 2;
   float s[NT][4];
@@ -492,7 +520,7 @@ __device__ __forceinline__ int cta_first_unit(const Params &p, const Len &L, int
   return unit_of(L, first_chunk(p, L, cta * p.nwc));
 }
 
-template <int NT>
+template <class G>
 __device__ __forceinline__ void warp_main(const Params &p, const Len &L, unsigned char *smem, uint64_t *bar, int wg,
                                           int warp, int lane) {
   const int64_t first = first_chunk(p, L, wg);
@@ -500,18 +528,18 @@ __device__ __forceinline__ void warp_main(const Params &p, const Len &L, unsigne
   unsigned char *region = smem + p.off_warp + warp * p.warp_bytes;
   const uint32_t region_a = ptx::smem_u32(region);
   const int u0 = cta_first_unit(p, L, blockIdx.x);
-  float *qa = (float *)(region + p.ns * p.slot_bytes);
+  float *qa = (float *)(region + kNS * G::SLOT);
 
   Cursor ci, cc;
   cc.init(p, L, first, last);
   ci = cc;
-  for (int s = 0; s < p.ns && ci.valid(); ++s) {
+  for (int s = 0; s < kNS && ci.valid(); ++s) {
     const int64_t pg = p.cv.block_table[(int64_t)ci.b * p.cv.max_pages + ci.lp];
-    issue_chunk(p, region_a + s * p.slot_bytes, &bar[s], ci, pg, lane);
+    issue_chunk<G>(p, region_a + s * G::SLOT, &bar[s], ci, pg, lane);
     ci.next(p, L);
   }
 
-  uint2 *qn = (uint2 *)(region + p.ns * p.slot_bytes + kQaBytes);
+  uint2 *qn = (uint2 *)(region + kNS * G::SLOT + kQaBytes);
   const uint32_t qa_a = ptx::smem_u32(qa);
 
   WarpState st;
@@ -542,28 +570,28 @@ __device__ __forceinline__ void warp_main(const Params &p, const Len &L, unsigne
       atomicExch(&g_fast_error, ERR_TIMEOUT_FULL);
       return;
     }
-    const uint32_t sa = region_a + s * p.slot_bytes;
+    const uint32_t sa = region_a + s * G::SLOT;
     const int nvalid = cc.nvalid(p, L);
-    const LaneAddr A(p, sa, qa_a, lane);
+    const LaneAddr A(G(), sa, qa_a, lane);
     // tiles in groups of two (one softmax update per 32 tokens)
-    if (nvalid == p.C) {
-      compute_qa(sa + p.o_kf[0], qa, NT * 16 >> p.lsk, qn, lane);
+    if (nvalid == G::C) {
+      compute_qa(sa + G::O_KF0, qa, G::AK, qn, lane);
       __syncwarp();
 #pragma unroll
-      for (int grp = 0; grp < NT / 2; ++grp) process_group<false>(st, A, f, grp * 32, p.lsk, p.lsv, nvalid, lane);
+      for (int grp = 0; grp < G::NT / 2; ++grp) process_group<G, false>(st, A, f, grp * 32, nvalid, lane);
     } else {
-      compute_qa(sa + p.o_kf[0], qa, ((nvalid - 1) >> p.lsk) + 1, qn, lane);
+      compute_qa(sa + G::O_KF0, qa, ((nvalid - 1) >> G::LSK) + 1, qn, lane);
       __syncwarp();
-      for (int grp = 0; grp * 32 < nvalid; ++grp) process_group<true>(st, A, f, grp * 32, p.lsk, p.lsv, nvalid, lane);
+      for (int grp = 0; grp * 32 < nvalid; ++grp) process_group<G, true>(st, A, f, grp * 32, nvalid, lane);
     }
     // every lane's reads of this slot are done before the refill is issued
     __syncwarp();
     ptx::fence_proxy_async_smem();
     if (ci.valid()) {
-      issue_chunk(p, sa, &bar[s], ci, pg_next, lane);
+      issue_chunk<G>(p, sa, &bar[s], ci, pg_next, lane);
       ci.next(p, L);
     }
-    if (++s == p.ns) {
+    if (++s == kNS) {
       s = 0;
       ph ^= 1u;
     }
@@ -767,14 +795,14 @@ __device__ void finish_units(const Params &p, const Len &L, unsigned char *smem)
   }
 }
 
-template <int NT>
+template <class G>
 __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const __grid_constant__ Params p) {
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwc = blockDim.x >> 5;
-  uint64_t *bar = (uint64_t *)smem + warp * p.ns;
+  uint64_t *bar = (uint64_t *)smem + warp * kNS;
   if (lane == 0) {
-    for (int s = 0; s < p.ns; ++s) ptx::mbar_init(&bar[s], 1);
+    for (int s = 0; s < kNS; ++s) ptx::mbar_init(&bar[s], 1);
     ptx::fence_mbar_init();
     ((int *)(smem + p.off_fin))[warp] = -1;  // warps without work contribute nothing
   }
@@ -797,7 +825,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const __grid_
   const Len L = s_len;
   if (L.T == 0) return;  // no length: nothing written (the error word says why)
   const int wg = blockIdx.x * nwc + warp;
-  if (wg < p.nwarps) warp_main<NT>(p, L, smem, bar, wg, warp, lane);
+  if (wg < p.nwarps) warp_main<G>(p, L, smem, bar, wg, warp, lane);
   __syncthreads();
   finish_units(p, L, smem);
 }
@@ -810,78 +838,78 @@ static constexpr int kMaxSmem = 227 * 1024 - 1024;  // dynamic shared memory; th
 static bool aligned16(const void *p) { return ((uintptr_t)p & 15) == 0; }
 static int up128(int x) { return (x + 127) & ~127; }
 
+using KernelFn = void (*)(Params);
+
+// One supported (stride_k, stride_v) pair: its geometry and kernel.
+struct GeoInfo {
+  int sk, sv, C, slot;
+  int off[6];  // K anchors, K codes, K scales, V anchors, V codes, V scales
+  KernelFn fn;
+};
+
+template <int SK, int SV>
+static GeoInfo geo_info() {
+  using G = Geo<SK, SV>;
+  return GeoInfo{SK, SV, G::C, G::SLOT, {G::O_KF0, G::O_CD0, G::O_SC0, G::O_KF1, G::O_CD1, G::O_SC1},
+                 decode_kernel<G>};
+}
+
+// Every pair the kernel takes: power-of-two strides, stride_k in {16, 32, 64}
+// (one K anchor per 16-token tile), stride_v in {8, .., 64}.
+static const GeoInfo *find_geo(int sk, int sv, int *index = nullptr) {
+  static const GeoInfo table[] = {
+      geo_info<16, 8>(),  geo_info<16, 16>(), geo_info<16, 32>(), geo_info<16, 64>(),
+      geo_info<32, 8>(),  geo_info<32, 16>(), geo_info<32, 32>(), geo_info<32, 64>(),
+      geo_info<64, 8>(),  geo_info<64, 16>(), geo_info<64, 32>(), geo_info<64, 64>(),
+  };
+  for (int i = 0; i < (int)(sizeof(table) / sizeof(table[0])); ++i)
+    if (table[i].sk == sk && table[i].sv == sv) {
+      if (index) *index = i;
+      return &table[i];
+    }
+  return nullptr;
+}
+
+// Chunk size of the fast kernel for these strides (0: not taken).
+int fast_chunk_tokens(int stride_k, int stride_v, int page_tokens) {
+  const GeoInfo *g = find_geo(stride_k, stride_v);
+  if (!g || page_tokens % g->C) return 0;
+  return g->C;
+}
+
 struct Layout {
-  int C, ns, nwc, lsk, lsv;
-  int o_kf[2], o_cd[2], o_sc[2], slot_bytes, warp_bytes, off_fin, off_strad, off_warp, total;
+  const GeoInfo *geo;
+  int gi;  // index in the geometry table
+  int C, nwc, warp_bytes, off_fin, off_strad, off_warp, total;
   int64_t phs;  // bytes per (page, head)
 };
 
-static int log2_exact(int x) {
-  if (x <= 0 || (x & (x - 1))) return -1;
-  int l = 0;
-  while ((1 << l) < x) ++l;
-  return l;
-}
-
-// Chunk size of the fast kernel: max(32, stride_k, stride_v) for power-of-two
-// strides (stride_k >= 16: one K anchor per 16-token tile; stride_v >= 8), at
-// most 64 tokens; 0 when the fast kernel does not take these strides.
-int fast_chunk_tokens(int stride_k, int stride_v, int page_tokens) {
-  const int lk = log2_exact(stride_k), lv = log2_exact(stride_v);
-  if (lk < 4 || lv < 3) return 0;
-  const int L = std::max(32, std::max(stride_k, stride_v));
-  if (L > 64 || page_tokens % L) return 0;
-  return L;
-}
-
-// Copy slots per warp: CQ_DECODE_SLOTS (2..4) overrides; default 2.
-static int pick_ns() {
-  static int ns = 0;
-  if (!ns) {
-    const char *e = getenv("CQ_DECODE_SLOTS");
-    const int v = e ? atoi(e) : 0;
-    ns = (v >= 2 && v <= 4) ? v : 2;
-  }
-  return ns;
-}
-
 // The fast kernel reads the chunk-block layout: per (page, head, chunk) one
 // block [K anchors][K codes][K scales][V anchors][V codes][V scales] of the
-// same size, the six arrays' base pointers pointing into the first block.  A
-// slot is a byte image of one block; the segment offsets come from the
-// pointer differences.
+// kernel's geometry, the six arrays' base pointers pointing into the first
+// block.  A slot is a byte image of one block.
 static bool make_layout(const cq_paged_cache &c, Layout &L) {
-  L.C = fast_chunk_tokens(c.k.stride, c.v.stride, c.page_tokens);
-  if (!L.C || c.k.chunk_tokens != L.C || c.v.chunk_tokens != L.C) return false;
-  L.ns = pick_ns();
-  L.lsk = log2_exact(c.k.stride);
-  L.lsv = log2_exact(c.v.stride);
+  L.geo = find_geo(c.k.stride, c.v.stride, &L.gi);
+  if (!L.geo) return false;
+  L.C = L.geo->C;
+  if (c.page_tokens % L.C || c.k.chunk_tokens != L.C || c.v.chunk_tokens != L.C) return false;
   const cq_component *cc[2] = {&c.k, &c.v};
   const char *base = (const char *)c.k.keyframes;
-  const int64_t cs = c.k.keyframe_chunk_stride * 2;
+  const int64_t cs = L.geo->slot;
   L.phs = c.k.keyframe_head_stride * 2;
-  int prev_end = 0;
   for (int i = 0; i < 2; ++i) {
     const cq_component &k = *cc[i];
     if (k.keyframe_chunk_stride * 2 != cs || k.code_chunk_stride * 4 != cs || k.scale_chunk_stride * 2 != cs)
       return false;
     if (k.keyframe_head_stride * 2 != L.phs || k.code_head_stride * 4 != L.phs || k.scale_head_stride * 2 != L.phs)
       return false;
-    const int a = L.C / k.stride;
-    const int64_t ok = (const char *)k.keyframes - base, oc = (const char *)k.codes - base,
-                  os = (const char *)k.scales - base;
-    // in block order, 16-byte aligned, each segment large enough, code rows
-    // preceded by at least one row of other data (row -1 of an I-frame)
-    if (ok != prev_end || oc < ok + a * HD * 2 || os < oc + (L.C - a) * (HD / 2) || ((ok | oc | os) & 15)) return false;
-    prev_end = (int)(((os + L.C * 2) + 15) & ~15ll);
-    L.o_kf[i] = (int)ok;
-    L.o_cd[i] = (int)oc;
-    L.o_sc[i] = (int)os;
+    if ((const char *)k.keyframes - base != L.geo->off[3 * i] || (const char *)k.codes - base != L.geo->off[3 * i + 1] ||
+        (const char *)k.scales - base != L.geo->off[3 * i + 2])
+      return false;
   }
-  if (prev_end > cs || (cs & 15) || (L.phs & 15) || L.phs < cs * (c.page_tokens / L.C)) return false;
-  L.slot_bytes = (int)cs;
+  if ((L.phs & 15) || L.phs < cs * (c.page_tokens / L.C)) return false;
   // a warp's copy slots later hold its on-chip partial; warp 0's also the unit list
-  L.warp_bytes = std::max(L.ns * L.slot_bytes, 8192 + 4 * kMaxWarps * 32) + kQaBytes + kQnBytes;
+  L.warp_bytes = std::max(kNS * (int)cs, 8192 + 4 * kMaxWarps * 32) + kQaBytes + kQnBytes;
   static_assert(kFinFloats * 4 <= 8192, "on-chip partial must fit below the unit list");
   L.off_fin = kMaxWarps * 4 * 8;  // after the mbarriers [warp][slot]: each warp's last unit
   L.off_strad = up128(L.off_fin + kMaxWarps * 4);
@@ -963,22 +991,12 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
   p.C = L.C;
   p.cpp = c.page_tokens / L.C;
   p.nwarps = pl.nwarps;
-  p.ns = L.ns;
-  p.lsk = L.lsk;
-  p.lsv = L.lsv;
   p.off_fin = L.off_fin;
   p.off_strad = L.off_strad;
   p.off_warp = L.off_warp;
   p.warp_bytes = L.warp_bytes;
-  p.slot_bytes = L.slot_bytes;
-  for (int i = 0; i < 2; ++i) {
-    p.o_kf[i] = L.o_kf[i];
-    p.o_cd[i] = L.o_cd[i];
-    p.o_sc[i] = L.o_sc[i];
-  }
   p.blk = (const char *)c.k.keyframes;
   p.phs = L.phs;
-  p.cs = L.slot_bytes;
   p.nwc = L.nwc;
   const size_t slots = (size_t)(pl.nwarps + pl.units) * p.gqa;  // warp partials
   const size_t cslots = (size_t)(pl.grid + pl.units) * p.gqa;   // CTA partials
@@ -1000,15 +1018,14 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
   p.lse_out = lse_out;
 
   static std::mutex mu;
-  static bool attr_set[64][2] = {};
-  const int v = L.C == 32 ? 0 : 1;
+  static bool attr_set[64][16] = {};
+  const int v = L.gi;
   {
     int dev = 0;
     cudaGetDevice(&dev);
     std::lock_guard<std::mutex> lk(mu);
     if (dev < 0 || dev >= 64 || !attr_set[dev][v]) {
-      cudaError_t e = v == 0 ? cudaFuncSetAttribute(decode_kernel<2>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem)
-                             : cudaFuncSetAttribute(decode_kernel<4>, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
+      cudaError_t e = cudaFuncSetAttribute(L.geo->fn, cudaFuncAttributeMaxDynamicSharedMemorySize, kMaxSmem);
       if (e != cudaSuccess)
         return set_error(CQ_ERR_CUDA, std::string("cudaFuncSetAttribute: ") + cudaGetErrorString(e));
       if (dev >= 0 && dev < 64) attr_set[dev][v] = true;
@@ -1027,7 +1044,7 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
   cfg.stream = st;
   cfg.attrs = attr;
   cfg.numAttrs = 1;
-  cudaError_t e = v == 0 ? cudaLaunchKernelEx(&cfg, decode_kernel<2>, p) : cudaLaunchKernelEx(&cfg, decode_kernel<4>, p);
+  cudaError_t e = cudaLaunchKernelEx(&cfg, L.geo->fn, p);
   if (e != cudaSuccess) return set_error(CQ_ERR_CUDA, std::string("decode_kernel: ") + cudaGetErrorString(e));
   return check_launch("decode_kernel");
 }
