@@ -314,6 +314,34 @@ extern "C" int cq_attention_at(const cq_paged_cache *cache, const int64_t *len_d
                          out_dtype, lse_out, workspace, workspace_bytes, 0, (cudaStream_t)stream, len_dev);
 }
 
+extern "C" int cq_decode_step_at(const cq_paged_cache *cache, const void *keys, int64_t k_sb, int64_t k_sh,
+                                 const void *values, int64_t v_sb, int64_t v_sh, int kv_dtype, int64_t *len_dev,
+                                 int64_t max_len, const void *q, int q_dtype, int32_t n_q_heads, int64_t q_sb,
+                                 int64_t q_sh, float scale, void *out, int out_dtype, float *lse_out, void *workspace,
+                                 size_t workspace_bytes, void *stream) {
+  int r = attention_common_checks(cache, max_len, n_q_heads, 1);
+  if (r) return r;
+  CQ_REQUIRE(keys && values && len_dev && q && out, CQ_ERR_INVALID, "cq_decode_step_at: null pointer");
+  CQ_REQUIRE(kv_dtype == CQ_F16 || kv_dtype == CQ_BF16, CQ_ERR_UNSUPPORTED,
+             "cq_decode_step_at: key/value dtype must be f16/bf16");
+  CQ_REQUIRE(q_dtype == CQ_F16 || q_dtype == CQ_BF16, CQ_ERR_UNSUPPORTED, "cq_decode_step_at: q dtype must be f16/bf16");
+  CQ_REQUIRE(out_dtype == CQ_F16 || out_dtype == CQ_BF16 || out_dtype == CQ_F32, CQ_ERR_UNSUPPORTED,
+             "cq_decode_step_at: bad out dtype");
+  CQ_REQUIRE(fast_decode_supported(*cache, n_q_heads, 1), CQ_ERR_UNSUPPORTED,
+             "cq_decode_step_at: this cache layout or shape does not take the sm_100a decode kernel");
+  StepInputs in;
+  in.x[0] = keys;
+  in.x[1] = values;
+  in.sb[0] = k_sb;
+  in.sh[0] = k_sh;
+  in.sb[1] = v_sb;
+  in.sh[1] = v_sh;
+  in.dtype = kv_dtype;
+  in.len = len_dev;
+  return run_fast_decode(*cache, make_view(*cache), max_len, q, q_dtype, n_q_heads, q_sb, q_sh, scale, out,
+                         out_dtype, lse_out, workspace, workspace_bytes, 0, (cudaStream_t)stream, nullptr, &in);
+}
+
 extern "C" int cq_lse_merge(const float *lse, const float *o, int32_t n_parts, int64_t rows, int32_t dim, void *out,
                             int out_dtype, void *stream) {
   CQ_REQUIRE(lse && o && out, CQ_ERR_INVALID, "cq_lse_merge: null pointer");

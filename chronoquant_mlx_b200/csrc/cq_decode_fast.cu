@@ -49,6 +49,7 @@
 #include <string>
 
 #include "cq_decode_fast.cuh"
+#include "cq_encode.cuh"
 #include "cq_ptx.cuh"
 
 namespace cq {
@@ -116,6 +117,15 @@ struct Params {
   void *out;
   int out_dtype;
   float *lse_out;
+  // in-step encode (graph decode steps): the kernel first stores token
+  // *T_dev of every unit (inputs x[comp] at b*x_sb + h*x_sh, dtype x_dtype),
+  // attends over *T_dev + 1 tokens and, when its grid ends, sets *len_rw to
+  // that length (arrival counter len_rw[1], left at 0)
+  int fuse;
+  const void *x[2];
+  int64_t x_sb[2], x_sh[2];
+  int x_dtype;
+  int64_t *len_rw;
 };
 
 __device__ __forceinline__ int64_t warp_of_chunk(int64_t x, int64_t tc, int nwarps) {
@@ -520,6 +530,60 @@ __device__ __forceinline__ int cta_first_unit(const Params &p, const Len &L, int
   return unit_of(L, first_chunk(p, L, cta * p.nwc));
 }
 
+// In-step encode of token tnew of unit (b, h) by one warp, into the chunk's
+// slot (already holding the block copied from the cache) and into the cache
+// block itself (physical page pg).  The same codec as the append kernel.
+template <class G, int DTYPE>
+__device__ void encode_new_token(const Params &p, unsigned char *slot, int64_t pg, int b, int h, int64_t tnew,
+                                 uint32_t *sw, int lane) {
+  const int tl = (int)(tnew % p.cv.P);
+  const int x = tl % G::C, j = tl / G::C;
+  unsigned char *blk = const_cast<unsigned char *>((const unsigned char *)p.blk) + (pg * p.cv.H + h) * p.phs +
+                       (int64_t)j * G::SLOT;
+#pragma unroll
+  for (int comp = 0; comp < 2; ++comp) {
+    const CompView &c = p.cv.c[comp];
+    const int s = comp ? G::SV : G::SK;
+    const int okf = comp ? G::O_KF1 : G::O_KF0, ocd = comp ? G::O_CD1 : G::O_CD0, osc = comp ? G::O_SC1 : G::O_SC0;
+    const int a = x / s, phase = x - a * s;
+    const int64_t xb = b * p.x_sb[comp] + h * p.x_sh[comp];
+    float xv[kMaxDimsPerLane];
+#pragma unroll
+    for (int i = 0; i < kMaxDimsPerLane; ++i) {
+      const int d = lane + 32 * i;
+      xv[i] = (d < HD) ? load_as_float(p.x[comp], xb + d, DTYPE) : 0.f;
+    }
+    __half *arow_s = (__half *)(slot + okf + a * HD * 2), *arow_g = (__half *)(blk + okf + a * HD * 2);
+    if (phase == 0) {  // I-frame: token.astype(float16) (cache.py:103-105), scale slot 0
+#pragma unroll
+      for (int i = 0; i < HD / 32; ++i) {
+        const __half v = __float2half_rn(xv[i]);
+        arow_s[lane + 32 * i] = v;
+        arow_g[lane + 32 * i] = v;
+      }
+      if (lane == 0) {
+        *(__half *)(slot + osc + x * 2) = __float2half_rn(0.f);
+        *(__half *)(blk + osc + x * 2) = __float2half_rn(0.f);
+      }
+    } else {
+      float av[kMaxDimsPerLane];
+#pragma unroll
+      for (int i = 0; i < kMaxDimsPerLane; ++i) av[i] = (i < HD / 32) ? __half2float(arow_s[lane + 32 * i]) : 0.f;
+      const float scale = encode_residual<DTYPE>(xv, av, HD, c.bits, c.dead_zone, c.order, sw, lane);
+      const int pf = x - a - 1;
+      if (lane < HD / 8) {
+        ((uint32_t *)(slot + ocd + pf * (HD / 2)))[lane] = sw[lane];
+        ((uint32_t *)(blk + ocd + pf * (HD / 2)))[lane] = sw[lane];
+      }
+      if (lane == 0) {
+        *(__half *)(slot + osc + x * 2) = __float2half_rn(scale);
+        *(__half *)(blk + osc + x * 2) = __float2half_rn(scale);
+      }
+    }
+    __syncwarp();
+  }
+}
+
 template <class G>
 __device__ __forceinline__ void warp_main(const Params &p, const Len &L, unsigned char *smem, uint64_t *bar, int wg,
                                           int warp, int lane) {
@@ -572,6 +636,14 @@ __device__ __forceinline__ void warp_main(const Params &p, const Len &L, unsigne
     }
     const uint32_t sa = region_a + s * G::SLOT;
     const int nvalid = cc.nvalid(p, L);
+    if (p.fuse && cc.cu == L.cpu - 1) {  // this step's new token lies in the unit's last chunk
+      const int64_t pg = p.cv.block_table[(int64_t)cc.b * p.cv.max_pages + cc.lp];
+      unsigned char *slot = region + s * G::SLOT;
+      if (p.x_dtype == CQ_BF16)
+        encode_new_token<G, CQ_BF16>(p, slot, pg, cc.b, cc.h, L.T - 1, (uint32_t *)qa, lane);
+      else
+        encode_new_token<G, CQ_F16>(p, slot, pg, cc.b, cc.h, L.T - 1, (uint32_t *)qa, lane);
+    }
     const LaneAddr A(G(), sa, qa_a, lane);
     // tiles in groups of two (one softmax update per 32 tokens)
     if (nvalid == G::C) {
@@ -811,7 +883,7 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const __grid_
   __shared__ Len s_len;
   if (threadIdx.x == 0) {
     Len L;
-    L.T = p.T_dev ? *p.T_dev : p.T;
+    L.T = (p.T_dev ? *p.T_dev : p.T) + (p.fuse ? 1 : 0);
     if (L.T < 1 || L.T > (int64_t)p.cv.max_pages * p.cv.P) {
       if (blockIdx.x == 0) atomicExch(&g_fast_error, ERR_LENGTH);
       L.T = 0;
@@ -828,6 +900,17 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const __grid_
   if (wg < p.nwarps) warp_main<G>(p, L, smem, bar, wg, warp, lane);
   __syncthreads();
   finish_units(p, L, smem);
+  if (p.len_rw) {  // every CTA has read the old length: the last one to finish advances it
+    __syncthreads();
+    if (threadIdx.x == 0) {
+      __threadfence();
+      unsigned long long *arrive = (unsigned long long *)(p.len_rw + 1);
+      if (atomicAdd(arrive, 1ull) == gridDim.x - 1) {
+        *(volatile int64_t *)p.len_rw = L.T;
+        *arrive = 0ull;
+      }
+    }
+  }
 }
 
 // ---------------------------------------------------------------------------
@@ -975,9 +1058,18 @@ size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, 
 
 int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, const void *q, int q_dtype,
                     int n_q_heads, int64_t q_sb, int64_t q_sh, float scale, void *out, int out_dtype, float *lse_out,
-                    void *ws, size_t ws_bytes, int splits_req, cudaStream_t st, const int64_t *T_dev) {
+                    void *ws, size_t ws_bytes, int splits_req, cudaStream_t st, const int64_t *T_dev,
+                    const StepInputs *in) {
   Params p;
-  p.T_dev = T_dev;  // when set, T is the largest length the launch is sized for
+  p.T_dev = in ? in->len : T_dev;  // when set, T is the largest length the launch is sized for
+  p.fuse = in != nullptr;
+  p.len_rw = in ? in->len : nullptr;
+  for (int i = 0; i < 2; ++i) {
+    p.x[i] = in ? in->x[i] : nullptr;
+    p.x_sb[i] = in ? in->sb[i] : 0;
+    p.x_sh[i] = in ? in->sh[i] : 0;
+  }
+  p.x_dtype = in ? in->dtype : CQ_F16;
   p.cv = cv;
   p.q = q;
   p.q_dtype = q_dtype;
@@ -1059,9 +1151,9 @@ size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, 
 }
 int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, const void *q, int q_dtype, int n_q_heads,
                     int64_t q_sb, int64_t q_sh, float scale, void *out, int out_dtype, float *lse_out, void *ws,
-                    size_t ws_bytes, int splits_req, cudaStream_t st, const int64_t *T_dev) {
+                    size_t ws_bytes, int splits_req, cudaStream_t st, const int64_t *T_dev, const StepInputs *in) {
   return fast::run_fast_decode(c, cv, T, q, q_dtype, n_q_heads, q_sb, q_sh, scale, out, out_dtype, lse_out, ws,
-                               ws_bytes, splits_req, st, T_dev);
+                               ws_bytes, splits_req, st, T_dev, in);
 }
 
 // Read (and optionally clear) the device-side error word the fast kernel sets

@@ -8,12 +8,11 @@
 // rounds to the token dtype exactly as the reference's fp16 (or bf16) MLX
 // arithmetic does: fp32 arithmetic on dtype values followed by one rounding is
 // the correctly rounded dtype result for + - * /.
-#include "cq_common.cuh"
+#include "cq_encode.cuh"
 
 namespace cq {
 
 constexpr int kEncodeWarps = 8;
-constexpr int kMaxDimsPerLane = 8;  // head_dim <= 256
 
 struct EncodeArgs {
   CacheView cv;
@@ -28,15 +27,6 @@ struct EncodeArgs {
 
 __device__ int g_append_error;
 constexpr int ERR_APPEND_RANGE = 5;  // tokens past the mapped pages
-
-// Quantise one residual value (codec.py:48-54).  `q` is the dtype-rounded
-// quotient delta/scale_safe.
-__device__ __forceinline__ int quantise_code(float q, float hl, bool zero_scale) {
-  if (zero_scale || isnan(q)) return 0;  // NaN (0/0) is undefined in the reference; defined as 0
-  float r = rintf(q);                    // mx.round: half to even
-  r = fminf(fmaxf(r, -hl), hl - 1.f);
-  return (int)r;
-}
 
 template <int DTYPE>
 __device__ __forceinline__ void encode_token(const EncodeArgs &A, int64_t t0, uint32_t *sw);
@@ -137,54 +127,8 @@ __device__ __forceinline__ void encode_token(const EncodeArgs &A, int64_t t0, ui
     av[i] = v;
   }
 
-  // delta = token - anchor.astype(token.dtype), in the token dtype (cache.py:113)
-  float dv[kMaxDimsPerLane];
-  float amax = 0.f;
-#pragma unroll
-  for (int i = 0; i < kMaxDimsPerLane; ++i) {
-    float an = (DTYPE == CQ_BF16) ? round_dt(av[i], CQ_BF16) : av[i];
-    dv[i] = round_dt(xv[i] - an, DTYPE);
-    amax = fmaxf(amax, fabsf(dv[i]));
-  }
-  amax = warp_max(amax);
-
-  const int hl_i = (1 << c.bits) / 2;
-  const float hl = (float)hl_i;
-  const float hlm1 = (float)(hl_i - 1);
-  const float tiny = round_dt(1e-10f, DTYPE);  // 0 in fp16
-  float scale = round_dt(__fdiv_rn(amax, hlm1), DTYPE);
-  if (c.dead_zone > 0.f) {  // codec.py:36-45
-    const float ratio = round_dt(c.dead_zone, DTYPE);
-    const float thr = round_dt(amax * ratio, DTYPE);
-    float amax_c = 0.f;
-#pragma unroll
-    for (int i = 0; i < kMaxDimsPerLane; ++i) {
-      if (fabsf(dv[i]) < thr) dv[i] = 0.f;
-      amax_c = fmaxf(amax_c, fabsf(dv[i]));
-    }
-    amax_c = warp_max(amax_c);
-    const float amax_safe = (amax_c < tiny) ? amax : amax_c;
-    scale = round_dt(__fdiv_rn(amax_safe, hlm1), DTYPE);
-  }
-  const bool zero_scale = scale < tiny;
-  const float scale_safe = zero_scale ? 1.f : scale;
-
+  const float scale = encode_residual<DTYPE>(xv, av, D, c.bits, c.dead_zone, c.order, sw, lane);
   const int W = words_of(D);
-  sw[lane] = 0u;
-  __syncwarp();
-#pragma unroll
-  for (int i = 0; i < kMaxDimsPerLane; ++i) {
-    int d = lane + 32 * i;
-    if (d < D) {
-      float q = round_dt(__fdiv_rn(dv[i], scale_safe), DTYPE);
-      int code = quantise_code(q, hl, zero_scale);
-      uint32_t nib = (uint32_t)min(max(code + 8, 0), 15);  // kernels.py:40
-      int w, sh;
-      nibble_pos(d, D, c.order, w, sh);
-      atomicOr(&sw[w], nib << sh);
-    }
-  }
-  __syncwarp();
   const int pf = tl - a - 1;
   uint32_t *code_row = const_cast<uint32_t *>(c.codes) + code_index(c, cv.H, W, pg, h, pf);
   if (lane < W) code_row[lane] = sw[lane];

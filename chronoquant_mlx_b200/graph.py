@@ -4,10 +4,13 @@ The reference steps eagerly from Python: each token costs an
 ``update_and_fetch`` (cache.py:198-215) and a ``chronoquant_sdpa``
 (attention.py:23-74).  Here the same two operations -- encode the new K/V
 token(s) into the paged cache, then attend a one-token query over everything
-cached -- run as one CUDA graph whose kernels read the cache length from
-device memory (``cq_append_at`` / ``cq_attention_at``), so the host issues one
-graph launch per token instead of two Python-side kernel launches, and the
-same graph serves every length up to ``max_len``.
+cached -- run as one CUDA graph whose kernel reads the cache length from
+device memory, so the host issues one graph launch per token instead of two
+Python-side kernel launches, and the same graph serves every length up to
+``max_len``.  With one token per step the graph is a single kernel
+(``cq_decode_step_at``: the decode kernel encodes each unit's new token into
+the chunk it is about to read); with more, ``cq_append_at`` then
+``cq_attention_at``.
 
 Usage::
 
@@ -17,7 +20,9 @@ Usage::
         out = g.step(k_new, v_new, q)     # [B, Hq, 1, D], in q_dtype
 
 ``step`` copies its inputs into the graph's static buffers (callers may also
-write ``g.keys`` / ``g.values`` / ``g.queries`` in place and call ``replay``),
+write ``g.keys`` / ``g.values`` / ``g.queries`` in place -- views of one flat
+byte buffer ``g.inputs``, so a producer can fill all three with one copy --
+and call ``replay``),
 replays the graph and advances ``cache.offset`` like ``update_and_fetch``.
 The returned tensor is the graph's output buffer: it is overwritten by the
 next step.
@@ -55,9 +60,13 @@ class DecodeGraph:
         self.len = torch.zeros(2, dtype=torch.int64, device=dev)  # {tokens cached, arrival counter}
         self.len[0] = cache.offset
         self._synced = cache.offset
-        self.keys = torch.zeros((B, H, self.S, D), dtype=kv_dtype, device=dev)
-        self.values = torch.zeros((B, H, self.S, D), dtype=kv_dtype, device=dev)
-        self.queries = torch.zeros((B, self.Hq, 1, D), dtype=q_dtype, device=dev)
+        # the step's inputs live in one flat buffer (one copy fills all three)
+        nk = B * H * self.S * D * torch.empty((), dtype=kv_dtype).element_size()
+        nq = B * self.Hq * D * torch.empty((), dtype=q_dtype).element_size()
+        self.inputs = torch.zeros(2 * nk + nq, dtype=torch.uint8, device=dev)
+        self.keys = self.inputs[:nk].view(kv_dtype).view(B, H, self.S, D)
+        self.values = self.inputs[nk:2 * nk].view(kv_dtype).view(B, H, self.S, D)
+        self.queries = self.inputs[2 * nk:].view(q_dtype).view(B, self.Hq, 1, D)
         self.out = torch.empty((B, self.Hq, 1, D), dtype=out_dtype or q_dtype, device=dev)
         self._desc = st.descriptor()
         L = _lib.lib()
@@ -71,8 +80,11 @@ class DecodeGraph:
         torch.cuda.synchronize(dev)
         self.graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(self.graph):
-            self._append()
-            self._attend()
+            if self.S == 1:
+                self._step_fused()  # one kernel: encode each unit's token, then attend
+            else:
+                self._append()
+                self._attend()
         torch.cuda.synchronize(dev)
 
     def _append(self):
@@ -81,6 +93,16 @@ class DecodeGraph:
         _lib.check(_lib.lib().cq_append_at(ctypes.byref(self._desc), k.data_ptr(), ks[0], ks[1], ks[2], v.data_ptr(),
                                            vs[0], vs[1], vs[2], cq_dtype(k), self.len.data_ptr(), self.S,
                                            stream_ptr(k.device)), "DecodeGraph")
+
+    def _step_fused(self):
+        k, v, q = self.keys, self.values, self.queries
+        ks, vs, qs = k.stride(), v.stride(), q.stride()
+        _lib.check(_lib.lib().cq_decode_step_at(ctypes.byref(self._desc), k.data_ptr(), ks[0], ks[1], v.data_ptr(),
+                                                vs[0], vs[1], cq_dtype(k), self.len.data_ptr(), self.max_len,
+                                                q.data_ptr(), cq_dtype(q), self.Hq, qs[0], qs[1], self.scale,
+                                                self.out.data_ptr(), cq_dtype(self.out), None,
+                                                self.workspace.data_ptr(), self.workspace.numel() * 4,
+                                                stream_ptr(q.device)), "DecodeGraph")
 
     def _attend(self):
         q = self.queries

@@ -175,6 +175,20 @@ int cq_attention_at(const cq_paged_cache *cache, const int64_t *len_dev, int64_t
                     int32_t n_q_heads, int64_t q_sb, int64_t q_sh, float scale, void *out, int out_dtype,
                     float *lse_out, void *workspace, size_t workspace_bytes, void *stream);
 
+/* cq_append_at of one token per (sequence, kv-head) followed by
+ * cq_attention_at, as one kernel launch: the warp that reads each unit's last
+ * chunk first encodes the unit's new token (keys/values [batch][kv_heads][1]
+ * [head_dim] at b*sb + h*sh, unit dim stride, kv_dtype f16/bf16) into the
+ * cache and into its on-chip copy, the attention covers len_dev[0] + 1
+ * tokens, and the grid's last CTA advances len_dev[0] by one (leaving the
+ * arrival counter len_dev[1] at 0).  The cache bytes written equal
+ * cq_append's.  Same requirements as cq_attention_at.  No reference
+ * counterpart (the reference appends and attends in separate eager calls). */
+int cq_decode_step_at(const cq_paged_cache *cache, const void *keys, int64_t k_sb, int64_t k_sh, const void *values,
+                      int64_t v_sb, int64_t v_sh, int kv_dtype, int64_t *len_dev, int64_t max_len, const void *q,
+                      int q_dtype, int32_t n_q_heads, int64_t q_sb, int64_t q_sh, float scale, void *out,
+                      int out_dtype, float *lse_out, void *workspace, size_t workspace_bytes, void *stream);
+
 /* cq_attention with an explicit mask instead of the implicit causal rule
  * (attention.py:8-20 for array masks): mask_kind 1 = boolean uint8 (nonzero
  * keeps the key; masked scores become finfo(score dtype).min as
