@@ -14,6 +14,7 @@
 
 #include "cq_common.cuh"
 #include "cq_decode_fast.cuh"
+#include "cq_prefill.cuh"
 
 namespace cq {
 
@@ -276,7 +277,8 @@ extern "C" int cq_attention_workspace(const cq_paged_cache *cache, int64_t T, in
   const int64_t rows = (int64_t)cache->batch * n_q_heads * q_len;
   size_t need = generic_workspace(rows, pick_splits(rows, T, num_splits), cache->head_dim);
   size_t fast = fast_decode_workspace(*cache, T, n_q_heads, q_len, num_splits);
-  *bytes = std::max(need, fast);
+  size_t chunk = prefill_workspace(*cache, T, n_q_heads, q_len);
+  *bytes = std::max(need, std::max(fast, chunk));
   return CQ_OK;
 }
 
@@ -295,6 +297,9 @@ extern "C" int cq_attention(const cq_paged_cache *cache, int64_t T, const void *
   if (fast_decode_supported(*cache, n_q_heads, q_len))
     return run_fast_decode(*cache, cv, T, q, q_dtype, n_q_heads, q_sb, q_sh, scale, out, out_dtype, lse_out,
                            workspace, workspace_bytes, num_splits, st);
+  if (prefill_supported(*cache, n_q_heads, q_len))
+    return run_prefill(*cache, cv, T, q, q_dtype, n_q_heads, q_len, q_sb, q_sh, q_sq, scale, out, out_dtype, lse_out,
+                       workspace, workspace_bytes, causal != 0, st);
   return run_generic(cv, T, q, q_dtype, n_q_heads, q_len, q_sb, q_sh, q_sq, scale, out, out_dtype, lse_out,
                      workspace, workspace_bytes, num_splits, st, MaskSpec(), causal != 0);
 }

@@ -49,6 +49,7 @@
 #include <string>
 
 #include "cq_decode_fast.cuh"
+#include "cq_prefill.cuh"
 #include "cq_encode.cuh"
 #include "cq_ptx.cuh"
 
@@ -1181,8 +1182,8 @@ int read_append_error(int clear);
 
 extern "C" int cq_device_error(int *code, int clear) {
   if (!code) return cq::set_error(CQ_ERR_INVALID, "cq_device_error: code is null");
-  const int a = cq::read_fast_error(clear), b = cq::read_append_error(clear);
-  *code = a ? a : b;
+  const int a = cq::read_fast_error(clear), b = cq::read_append_error(clear), c = cq::read_prefill_error(clear);
+  *code = a ? a : (b ? b : c);
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cq::set_error(CQ_ERR_CUDA, cudaGetErrorString(e));
   return CQ_OK;

@@ -1,0 +1,17 @@
+// cq_prefill.cuh -- host entry points of the tensor-core query-chunk path (cq_prefill.cu).
+#pragma once
+
+#include "cq_common.cuh"
+
+namespace cq {
+
+// head_dim 128, at least 16 query tokens, GQA group a power of two <= 16
+bool prefill_supported(const cq_paged_cache &c, int n_q_heads, int q_len);
+// workspace bytes (0 when unsupported): K and V^T tile images of every key, query tile images
+size_t prefill_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len);
+int run_prefill(const cq_paged_cache &cache, const CacheView &cv, int64_t T, const void *q, int q_dtype, int Hq,
+                int q_len, int64_t q_sb, int64_t q_sh, int64_t q_sq, float scale, void *out, int out_dtype,
+                float *lse_out, void *ws, size_t ws_bytes, bool causal, cudaStream_t st);
+int read_prefill_error(int clear);
+
+}  // namespace cq

@@ -124,7 +124,9 @@ int cq_decode_chunk_tokens(int32_t stride_k, int32_t stride_v, int32_t page_toke
  * hanging or writing out of range: 1 = a bulk copy never landed (bounded
  * wait), 4 = a device-resident length outside [1, mapped tokens] (attention
  * wrote nothing), 5 = a device-resident append past the mapped pages (append
- * wrote nothing).  Synchronises the device; clear != 0 resets the word. */
+ * wrote nothing), 6 = the tensor-core query-chunk kernel gave up on a bounded
+ * wait (its output is incomplete).  Synchronises the device; clear != 0
+ * resets the word. */
 int cq_device_error(int *code, int clear);
 
 /* Encode S new tokens at absolute positions t0..t0+S-1 for K and V in one
@@ -146,7 +148,11 @@ int cq_append(const cq_paged_cache *cache, const void *keys, int64_t k_sb, int64
  * [head_dim] contiguous, out_dtype CQ_F16/CQ_BF16/CQ_F32.  workspace: device
  * memory of at least cq_attention_workspace() bytes (split-KV partials and
  * per-call-stamped completion words; its prior contents are ignored);
- * num_splits <= 0 picks a split count.  lse_out (optional, may be NULL):
+ * num_splits <= 0 picks a split count.  Query chunks (q_len >= 16, head_dim
+ * 128, a GQA group that is a power of two <= 16) run on the tensor cores: the
+ * history is reconstructed in fp16 (as cache.py:131-160) into the workspace
+ * (16-byte aligned, as is out), whose size then covers 2*T*head_dim*2 bytes
+ * per (sequence, kv-head) plus the query tiles.  lse_out (optional, may be NULL):
  * fp32 [batch][n_q_heads][q_len] log-sum-exp of the scaled scores (natural
  * log), for merging sequence shards. */
 int cq_attention(const cq_paged_cache *cache, int64_t T, const void *q, int q_dtype, int32_t n_q_heads,
