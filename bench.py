@@ -1,6 +1,6 @@
 """Benchmark: ChronoQuant compressed-cache decode step on B200.
 
-    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3] [--impl ours|reference]
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4] [--impl ours|reference]
 
 Workload (BASELINE config 2 by default): one attention layer, B=8 sequences,
 32 query / 8 KV heads, head_dim 128, a compressed context of T=16384 tokens
@@ -49,7 +49,10 @@ CONFIGS = {
             bits_k=4, bits_v=4, dz_k=0.0, dz_v=0.0, rho_k=0.95, rho_v=0.8),
     3: dict(name="cfg3-ftv3-decode", B=16, Hq=32, Hkv=8, D=128, T=32768, stride_k=64, stride_v=32,
             bits_k=4, bits_v=3, dz_k=0.0, dz_v=0.05, rho_k=0.97, rho_v=0.85),
+    4: dict(name="cfg4-standard-prefill", B=1, Hq=32, Hkv=8, D=128, T=65536, chunk=2048, stride_k=32,
+            stride_v=8, bits_k=4, bits_v=4, dz_k=0.0, dz_v=0.0, rho_k=0.95, rho_v=0.8),
 }
+PREFILL_METRIC = "chunked prefill attention TFLOP/s over the compressed cache (config 4)"
 
 
 def active_bytes(B, H, T, D, sk, sv):
@@ -77,6 +80,18 @@ def step_bytes(cfg, T):
         else:
             enc += B * H * (D * 2 + D * 2 + (D // 8) * 4 + 2)
     return attn, enc
+
+
+def prefill_flops(cfg, rows=None, kv_heads=None):
+    """Algorithmic FLOPs of one query chunk: 4*Hq*Tq*Tctx*D for the cached
+    context plus 4*Hq*Tq^2*D/2 for the causal chunk itself (QK^T and PV, 2
+    FLOPs per multiply-add).  ``rows``/``kv_heads`` restrict it to a sample."""
+    Tq, Tc, D = cfg["chunk"], cfg["T"], cfg["D"]
+    hq = cfg["Hq"] if kv_heads is None else kv_heads * (cfg["Hq"] // cfg["Hkv"])
+    if rows is None:
+        return 4 * hq * Tq * Tc * D + 4 * hq * Tq * Tq * D / 2
+    # rows = the last `rows` tokens of the chunk: each sees the context plus its causal prefix
+    return sum(4 * hq * (Tc + Tq - rows + i + 1) * D for i in range(rows))
 
 
 def ar1_host(B, H, T, D, rho_k, rho_v, seed):
@@ -353,7 +368,7 @@ def run_ours(args, cfg):
                          "algorithmic_bytes_per_launch": round(mean_attn_bytes),
                          "launch_ms": round(mean_attn_ms, 5), "launch_timing": "graph replays back to back"},
             "clocks": clk.summary(),
-            "gpu_launches": args.steps * 2,
+            "gpu_launches": args.steps,  # one fused encode+decode kernel per graph replay
         }
         if not args.no_cpu_baseline and world == 1:
             res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
@@ -361,6 +376,246 @@ def run_ours(args, cfg):
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()
+
+
+def run_prefill(args, cfg):
+    """Config 4: one step = encode a 2048-token chunk into the compressed cache
+    (context 65536 tokens) and attend its 2048 causal queries over all 67584
+    tokens on the tensor-core path (cq_append + cq_attention)."""
+    import ctypes
+
+    import torch
+    import torch.distributed as dist
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    sys.path.insert(0, HERE)
+    from chronoquant_mlx_b200 import ChronoQuantCache, _lib
+
+    B, H, Hq, D, ctx, S = cfg["B"], cfg["Hkv"], cfg["Hq"], cfg["D"], cfg["T"], cfg["chunk"]
+    T = ctx + S
+    K, V = ar1_host(B, H, T, D, cfg["rho_k"], cfg["rho_v"], seed=2000 + rank)
+    cache = ChronoQuantCache(stride_k=cfg["stride_k"], stride_v=cfg["stride_v"], delta_bits_k=cfg["bits_k"],
+                             delta_bits_v=cfg["bits_v"], dead_zone_k=cfg["dz_k"], dead_zone_v=cfg["dz_v"],
+                             max_tokens=T)
+    for t in range(0, T, 4096):
+        n = min(4096, T - t)
+        cache.update_and_fetch(torch.from_numpy(K[:, :, t:t + n]).to(device),
+                               torch.from_numpy(V[:, :, t:t + n]).to(device))
+    kc = torch.from_numpy(np.ascontiguousarray(K[:, :, ctx:])).to(device)
+    vc = torch.from_numpy(np.ascontiguousarray(V[:, :, ctx:])).to(device)
+    del K, V
+    g = torch.Generator(device="cpu").manual_seed(11 + rank)
+    q = (torch.randn((B, Hq, S, D), generator=g) / math.sqrt(D)).to(torch.bfloat16).to(device)
+    out = torch.empty_like(q)
+    scale = 1.0 / math.sqrt(D)
+    L = _lib.lib()
+    desc = cache.store.descriptor()
+    need = ctypes.c_size_t(0)
+    _lib.check(L.cq_attention_workspace(ctypes.byref(desc), T, Hq, S, 0, ctypes.byref(need)), "bench")
+    ws = torch.empty((need.value + 3) // 4, dtype=torch.float32, device=device)
+    ws_bytes = ws.numel() * 4
+    stream = torch.cuda.current_stream()
+    sp = stream.cuda_stream
+    ks, vs, qs = kc.stride(), vc.stride(), q.stride()
+
+    def append(kk, vv):
+        _lib.check(L.cq_append(ctypes.byref(desc), kk.data_ptr(), ks[0], ks[1], ks[2], vv.data_ptr(), vs[0], vs[1],
+                               vs[2], _lib.CQ_F16, ctx, S, sp), "bench append")
+
+    def prepare(qq):
+        _lib.check(L.cq_prefill_prepare(ctypes.byref(desc), T, qq.data_ptr(), _lib.CQ_BF16, Hq, S, qs[0], qs[1],
+                                        qs[2], scale, ws.data_ptr(), ws_bytes, sp), "bench prepare")
+
+    def attend(oo):
+        _lib.check(L.cq_prefill_attend(ctypes.byref(desc), T, Hq, S, 1, oo.data_ptr(), _lib.CQ_BF16, None,
+                                       ws.data_ptr(), ws_bytes, sp), "bench attend")
+
+    def step(kk, vv, qq, oo):  # the public path: encode the chunk, then cq_attention (prepare + attend)
+        append(kk, vv)
+        _lib.check(L.cq_attention(ctypes.byref(desc), T, qq.data_ptr(), _lib.CQ_BF16, Hq, S, 1, qs[0], qs[1],
+                                  qs[2], scale, oo.data_ptr(), _lib.CQ_BF16, None, ws.data_ptr(), ws_bytes, 0, sp),
+                   "bench attention")
+
+    def timed(fn, reps):
+        fn()
+        torch.cuda.synchronize()
+        e0 = torch.cuda.Event(enable_timing=True)
+        e1 = torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for _ in range(reps):
+            fn()
+        e1.record(stream)
+        torch.cuda.synchronize()
+        return e0.elapsed_time(e1) / reps
+
+    for _ in range(args.warmup):
+        step(kc, vc, q, out)
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step(kc, vc, q, out)
+        t1.record(stream)
+        torch.cuda.synchronize()
+    elapsed_ms = t0.elapsed_time(t1)
+    if world > 1:
+        tt = torch.tensor([elapsed_ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(tt.item())
+    ms_per_step = elapsed_ms / args.steps
+    flops = prefill_flops(cfg) * B
+    value = world * flops / (ms_per_step * 1e-3) / 1e12
+    # the stages apart: encode of the chunk, tile images (history + queries), tensor-core attention
+    reps = max(5, min(args.steps, 20))
+    append_ms = timed(lambda: append(kc, vc), reps)
+    prepare_ms = timed(lambda: prepare(q), reps)
+    attend_ms = timed(lambda: attend(out), reps)
+
+    # e2e: the chunk's K/V and the queries from pinned host memory, the output back, every step
+    hk, hv, hq = kc.cpu().pin_memory(), vc.cpu().pin_memory(), q.cpu().pin_memory()
+    ho = torch.empty_like(hq).pin_memory()
+    dk, dv, dq = torch.empty_like(kc), torch.empty_like(vc), torch.empty_like(q)
+    e_steps = max(3, min(args.steps, 10))
+    torch.cuda.synchronize()
+    if world > 1:
+        dist.barrier()
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(e_steps):
+        dk.copy_(hk, non_blocking=True)
+        dv.copy_(hv, non_blocking=True)
+        dq.copy_(hq, non_blocking=True)
+        step(dk, dv, dq, out)
+        ho.copy_(out, non_blocking=True)
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e_ms = e0.elapsed_time(e1)
+    if world > 1:
+        tt = torch.tensor([e_ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_ms = float(tt.item())
+    e2e_value = world * flops * e_steps / (e_ms * 1e-3) / 1e12
+
+    peaks = {}
+    try:
+        with open(os.path.join(HERE, "MEASURED_PEAKS.json")) as f:
+            peaks = json.load(f)
+        peak, peak_kind = float(peaks["bf16_tflops"]), "measured (burst, cuBLAS bf16)"
+    except Exception:
+        peak, peak_kind = 1590.0, "fallback"
+    achieved = flops / (attend_ms * 1e-3) / 1e12
+    if rank == 0:
+        res = {
+            "metric": PREFILL_METRIC, "value": round(value, 2), "unit": "TFLOP/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step, 4),
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "int4-residual/f16-anchor cache; fp16 tensor-core operands, f32 accumulate, bf16 q/out",
+            "data": "synthetic AR(1) K/V (seeded), random bf16 queries",
+            "config": {"workload": cfg["name"], "batch": B, "q_heads": Hq, "kv_heads": H, "head_dim": D,
+                       "context_tokens": ctx, "chunk_tokens": S, "stride_k": cfg["stride_k"],
+                       "stride_v": cfg["stride_v"], "causal": True,
+                       "step": "encode the chunk (cq_append) + cq_attention (tile images + tcgen05 attention)",
+                       "l2": "fp16 tile images %.0f MB > 126 MB L2; no flush" % (2 * B * H * T * D * 2 / 1e6),
+                       "parallelism": f"dp{world} (independent chunks per rank, no collective)"},
+            "stages_ms": {"append": round(append_ms, 4), "prepare": round(prepare_ms, 4),
+                          "attend": round(attend_ms, 4)},
+            "e2e": {"value": round(e2e_value, 2), "unit": "TFLOP/s", "steps": e_steps,
+                    "h2d_bytes_per_step": (kc.numel() + vc.numel() + q.numel()) * 2,
+                    "d2h_bytes_per_step": out.numel() * 2},
+            "roofline": {"bound": "tensor", "kernel": "attn_kernel (tcgen05 flash attention)",
+                         "achieved": round(achieved, 1), "peak": peak, "unit": "TFLOP/s",
+                         "frac": round(achieved / peak, 4), "peak_source": peak_kind, "traffic": None,
+                         "algorithmic_flops_per_launch": flops, "launch_ms": round(attend_ms, 4)},
+            "clocks": clk.summary(),
+            "gpu_launches": args.steps * 4,  # append, unpack, query tiles, attention
+        }
+        if not args.no_cpu_baseline and world == 1:
+            res["cpu_baseline"] = cpu_baseline_prefill(cfg, rows=args.cpu_rows)
+        print(json.dumps(res))
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _prefill_unit(cfg, seed, rows):
+    """One kv-head of config 4 on the reference's CPU path (oracle port):
+    encode the chunk onto the cached context (cache.py:87-129), reconstruct
+    the fp16 history (cache.py:131-160), fallback SDPA (attention.py:61-74)
+    for the last ``rows`` queries of the chunk.  Returns (seconds, flops)."""
+    from oracle import cq_oracle as O
+    ctx, S, D = cfg["T"], cfg["chunk"], cfg["D"]
+    rep = cfg["Hq"] // cfg["Hkv"]
+    K, V = ar1_host(1, 1, ctx + S, D, cfg["rho_k"], cfg["rho_v"], seed)
+    c = O.OracleCache(stride_k=cfg["stride_k"], stride_v=cfg["stride_v"], delta_bits_k=cfg["bits_k"],
+                      delta_bits_v=cfg["bits_v"], dead_zone_k=cfg["dz_k"], dead_zone_v=cfg["dz_v"])
+    c.update_and_fetch(K[:, :, :ctx], V[:, :, :ctx])
+    q = (np.random.default_rng(seed).standard_normal((1, rep, rows, D)) / math.sqrt(D)).astype(np.float32)
+    q = O.round_bf16(q)
+    t0 = time.perf_counter()
+    c.update_and_fetch(K[:, :, ctx:], V[:, :, ctx:])
+    fk, fv = c.reconstruct_history()
+    mask = O.causal_mask(S, ctx + S)[S - rows:]
+    O.fallback_sdpa(q, "bf16", fk, fv, 1.0 / math.sqrt(D), mask)
+    return time.perf_counter() - t0, prefill_flops(cfg, rows=rows, kv_heads=1)
+
+
+def _prefill_worker(a):
+    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    return _prefill_unit(*a)
+
+
+def cpu_baseline_prefill(cfg, rows=128):
+    sys.path.insert(0, HERE)
+    sec, fl = _prefill_unit(cfg, 0, rows)
+    return {"value": round(fl / sec / 1e12, 6), "unit": "TFLOP/s", "cores": 1, "kind": "port",
+            "sample": f"1 of {cfg['Hkv']} kv-heads, the last {rows} of {cfg['chunk']} queries: oracle chunk encode "
+                      f"+ fp16 reconstruct of {cfg['T'] + cfg['chunk']} tokens + fallback SDPA (numpy)",
+            "seconds": round(sec, 2), "host_cpus": os.cpu_count()}
+
+
+def run_reference_prefill(args, cfg):
+    rank = int(os.environ.get("RANK", "0"))
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    if rank != 0:
+        return
+    import multiprocessing as mp
+    workers = max(1, min(os.cpu_count() or 1, cfg["Hkv"]))
+    ctx = mp.get_context("spawn")
+    t0 = time.perf_counter()
+    with ctx.Pool(workers) as pool:
+        res = pool.map(_prefill_worker, [(cfg, 300 + i, args.cpu_rows) for i in range(workers)])
+    wall = time.perf_counter() - t0
+    sec = max(r[0] for r in res)
+    fl = sum(r[1] for r in res)
+    value = fl / sec / 1e12
+    out = {
+        "impl": "reference", "metric": PREFILL_METRIC, "value": round(value, 6), "unit": "TFLOP/s",
+        "n_gpus": world, "steps": 1, "warmup": 0, "ms_per_step": round(prefill_flops(cfg) / (value * 1e12) * 1e3, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+        "dtype": "fp16 reconstruct, fp32 scores (bf16 q x fp16 K), numpy", "data": "synthetic AR(1) K/V (seeded)",
+        "config": {"workload": cfg["name"], "batch": cfg["B"], "q_heads": cfg["Hq"], "kv_heads": cfg["Hkv"],
+                   "head_dim": cfg["D"], "context_tokens": cfg["T"], "chunk_tokens": cfg["chunk"],
+                   "parallelism": f"{workers} host processes"},
+        "cpu_baseline": {"value": round(value, 6), "unit": "TFLOP/s", "cores": workers, "kind": "port",
+                         "sample": f"{workers} kv-heads x the last {args.cpu_rows} queries each (oracle restatement of "
+                                   "the reference's encode + fp16 reconstruct + fallback SDPA); wall %.1f s" % wall},
+        "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out))
 
 
 # ----------------------------------------------------------------------------- CPU reference arm
@@ -483,10 +738,17 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--page-tokens", type=int, default=None, help="cache page size (default: the cache's choice)")
+    ap.add_argument("--cpu-rows", type=int, default=128, help="config 4 CPU sample: query rows per kv-head")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     cfg = CONFIGS[args.config]
+    if args.config == 4:
+        if args.impl == "reference":
+            run_reference_prefill(args, cfg)
+        else:
+            run_prefill(args, cfg)
+        return
     if args.impl == "reference":
         run_reference(args, cfg)
     else:

@@ -30,7 +30,7 @@ EXPORTED = [
     "cq_attention_masked", "cq_lse_merge", "cq_reconstruct", "cq_export_state", "cq_import_state", "cq_quantize_delta",
     "cq_dequantize_delta", "cq_pack_int4", "cq_unpack_int4", "cq_sdpa_reference_layout",
     "cq_sdpa_reference_layout_workspace", "cq_attention_static_scratch", "cq_decode_chunk_tokens",
-    "cq_append_at", "cq_attention_at", "cq_decode_step_at",
+    "cq_append_at", "cq_attention_at", "cq_decode_step_at", "cq_prefill_prepare", "cq_prefill_attend",
 ]
 
 
@@ -94,6 +94,8 @@ def _declare(lib):
         "cq_attention_at": [C, P, I64, P, ctypes.c_int, I32, I64, I64, F, P, ctypes.c_int, P, P, SZ, P],
         "cq_decode_step_at": [C, P, I64, I64, P, I64, I64, ctypes.c_int, P, I64, P, ctypes.c_int, I32, I64, I64, F, P,
                               ctypes.c_int, P, P, SZ, P],
+        "cq_prefill_prepare": [C, I64, P, ctypes.c_int, I32, I32, I64, I64, I64, F, P, SZ, P],
+        "cq_prefill_attend": [C, I64, I32, I32, I32, P, ctypes.c_int, P, P, SZ, P],
         "cq_attention_static_scratch": [C, I64, P, ctypes.c_int, I32, I32, I32, I64, I64, I64, F, P, ctypes.c_int,
                                         P, I32, P],
     }

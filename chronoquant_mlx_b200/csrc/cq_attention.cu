@@ -282,6 +282,29 @@ extern "C" int cq_attention_workspace(const cq_paged_cache *cache, int64_t T, in
   return CQ_OK;
 }
 
+extern "C" int cq_prefill_prepare(const cq_paged_cache *cache, int64_t T, const void *q, int q_dtype,
+                                  int32_t n_q_heads, int32_t q_len, int64_t q_sb, int64_t q_sh, int64_t q_sq,
+                                  float scale, void *workspace, size_t workspace_bytes, void *stream) {
+  int r = attention_common_checks(cache, T, n_q_heads, q_len);
+  if (r) return r;
+  CQ_REQUIRE(q, CQ_ERR_INVALID, "cq_prefill_prepare: q null");
+  CQ_REQUIRE(q_dtype == CQ_F16 || q_dtype == CQ_BF16, CQ_ERR_UNSUPPORTED, "cq_prefill_prepare: q dtype must be f16/bf16");
+  return prefill_prepare(*cache, make_view(*cache), T, q, q_dtype, n_q_heads, q_len, q_sb, q_sh, q_sq, scale,
+                         workspace, workspace_bytes, (cudaStream_t)stream);
+}
+
+extern "C" int cq_prefill_attend(const cq_paged_cache *cache, int64_t T, int32_t n_q_heads, int32_t q_len,
+                                 int32_t causal, void *out, int out_dtype, float *lse_out, void *workspace,
+                                 size_t workspace_bytes, void *stream) {
+  int r = attention_common_checks(cache, T, n_q_heads, q_len);
+  if (r) return r;
+  CQ_REQUIRE(out, CQ_ERR_INVALID, "cq_prefill_attend: out null");
+  CQ_REQUIRE(out_dtype == CQ_F16 || out_dtype == CQ_BF16 || out_dtype == CQ_F32, CQ_ERR_UNSUPPORTED,
+             "cq_prefill_attend: bad out dtype");
+  return prefill_attend(*cache, T, n_q_heads, q_len, causal != 0, out, out_dtype, lse_out, workspace, workspace_bytes,
+                        (cudaStream_t)stream);
+}
+
 extern "C" int cq_attention(const cq_paged_cache *cache, int64_t T, const void *q, int q_dtype, int32_t n_q_heads,
                             int32_t q_len, int32_t causal, int64_t q_sb, int64_t q_sh, int64_t q_sq, float scale, void *out,
                             int out_dtype, float *lse_out, void *workspace, size_t workspace_bytes,

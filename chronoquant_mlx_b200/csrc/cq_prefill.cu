@@ -490,29 +490,40 @@ size_t prefill_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int 
   return units * (2 * (size_t)n_kt + (size_t)n_qt) * kImgBytes;
 }
 
-int run_prefill(const cq_paged_cache &cache, const CacheView &cv, int64_t T, const void *q, int q_dtype, int Hq,
-                int q_len, int64_t q_sb, int64_t q_sh, int64_t q_sq, float scale, void *out, int out_dtype,
-                float *lse_out, void *ws, size_t ws_bytes, bool causal, cudaStream_t st) {
-  int n_kt, TQ, n_qt;
-  prefill_shape(cache, T, Hq, q_len, n_kt, TQ, n_qt);
+struct Plan {
+  int n_kt, TQ, n_qt, units;
+  uint8_t *kimg, *vimg, *qimg;
+};
+
+static int make_plan(const cq_paged_cache &cache, int64_t T, int Hq, int q_len, void *ws, size_t ws_bytes, Plan &pl) {
+  CQ_REQUIRE(prefill_supported(cache, Hq, q_len), CQ_ERR_UNSUPPORTED,
+             "query-chunk path: needs head_dim 128, q_len >= 16 and a GQA group that is a power of two <= 16");
+  prefill_shape(cache, T, Hq, q_len, pl.n_kt, pl.TQ, pl.n_qt);
   const size_t need = prefill_workspace(cache, T, Hq, q_len);
   CQ_REQUIRE(ws && ws_bytes >= need, CQ_ERR_WORKSPACE, "cq_attention: workspace too small");
-  CQ_REQUIRE(((uintptr_t)ws & 15) == 0 && ((uintptr_t)out & 15) == 0, CQ_ERR_INVALID,
-             "cq_attention: workspace and out must be 16-byte aligned for query chunks");
-  const int units = cache.batch * cache.kv_heads;
-  CQ_REQUIRE((int64_t)units * n_qt < (1LL << 31), CQ_ERR_INVALID, "cq_attention: grid too large");
-  uint8_t *kimg = (uint8_t *)ws;
-  uint8_t *vimg = kimg + (size_t)units * n_kt * kImgBytes;
-  uint8_t *qimg = vimg + (size_t)units * n_kt * kImgBytes;
+  CQ_REQUIRE(((uintptr_t)ws & 15) == 0, CQ_ERR_INVALID, "cq_attention: workspace must be 16-byte aligned for query chunks");
+  pl.units = cache.batch * cache.kv_heads;
+  CQ_REQUIRE((int64_t)pl.units * pl.n_qt < (1LL << 31), CQ_ERR_INVALID, "cq_attention: grid too large");
+  pl.kimg = (uint8_t *)ws;
+  pl.vimg = pl.kimg + (size_t)pl.units * pl.n_kt * kImgBytes;
+  pl.qimg = pl.vimg + (size_t)pl.units * pl.n_kt * kImgBytes;
+  return CQ_OK;
+}
 
+int prefill_prepare(const cq_paged_cache &cache, const CacheView &cv, int64_t T, const void *q, int q_dtype, int Hq,
+                    int q_len, int64_t q_sb, int64_t q_sh, int64_t q_sq, float scale, void *ws, size_t ws_bytes,
+                    cudaStream_t st) {
+  Plan pl;
+  int r = make_plan(cache, T, Hq, q_len, ws, ws_bytes, pl);
+  if (r) return r;
   UnpackArgs U;
   U.cv = cv;
   U.T = T;
-  U.n_kt = n_kt;
-  U.img[0] = kimg;
-  U.img[1] = vimg;
-  unpack_kernel<<<dim3((unsigned)n_kt, (unsigned)units, 2), 256, 0, st>>>(U);
-  int r = check_launch("prefill unpack_kernel");
+  U.n_kt = pl.n_kt;
+  U.img[0] = pl.kimg;
+  U.img[1] = pl.vimg;
+  unpack_kernel<<<dim3((unsigned)pl.n_kt, (unsigned)pl.units, 2), 256, 0, st>>>(U);
+  r = check_launch("prefill unpack_kernel");
   if (r) return r;
 
   QArgs Q;
@@ -523,26 +534,32 @@ int run_prefill(const cq_paged_cache &cache, const CacheView &cv, int64_t T, con
   Q.sq = q_sq;
   Q.Hkv = cache.kv_heads;
   Q.G = Hq / cache.kv_heads;
-  Q.TQ = TQ;
+  Q.TQ = pl.TQ;
   Q.q_len = q_len;
-  Q.n_qt = n_qt;
+  Q.n_qt = pl.n_qt;
   // the scale is a weakly typed Python float: it multiplies in the query dtype
   Q.scale = (q_dtype == CQ_BF16) ? __bfloat162float(__float2bfloat16_rn(scale)) : __half2float(__float2half_rn(scale));
-  Q.img = qimg;
-  q_image_kernel<<<dim3((unsigned)n_qt, (unsigned)units), 256, 0, st>>>(Q);
-  r = check_launch("prefill q_image_kernel");
-  if (r) return r;
+  Q.img = pl.qimg;
+  q_image_kernel<<<dim3((unsigned)pl.n_qt, (unsigned)pl.units), 256, 0, st>>>(Q);
+  return check_launch("prefill q_image_kernel");
+}
 
+int prefill_attend(const cq_paged_cache &cache, int64_t T, int Hq, int q_len, bool causal, void *out, int out_dtype,
+                   float *lse_out, void *ws, size_t ws_bytes, cudaStream_t st) {
+  Plan pl;
+  int r = make_plan(cache, T, Hq, q_len, ws, ws_bytes, pl);
+  if (r) return r;
+  CQ_REQUIRE(((uintptr_t)out & 15) == 0, CQ_ERR_INVALID, "cq_attention: out must be 16-byte aligned for query chunks");
   AttnParams P;
-  P.kimg = kimg;
-  P.vimg = vimg;
-  P.qimg = qimg;
-  P.n_kt = n_kt;
+  P.kimg = pl.kimg;
+  P.vimg = pl.vimg;
+  P.qimg = pl.qimg;
+  P.n_kt = pl.n_kt;
   P.T = T;
   P.q_len = q_len;
-  P.G = Q.G;
-  P.TQ = TQ;
-  P.n_qt = n_qt;
+  P.G = Hq / cache.kv_heads;
+  P.TQ = pl.TQ;
+  P.n_qt = pl.n_qt;
   P.Hkv = cache.kv_heads;
   P.Hq = Hq;
   P.causal = causal ? 1 : 0;
@@ -551,8 +568,16 @@ int run_prefill(const cq_paged_cache &cache, const CacheView &cv, int64_t T, con
   P.lse = lse_out;
   cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return set_error(CQ_ERR_CUDA, std::string("prefill attn_kernel smem: ") + cudaGetErrorString(e));
-  attn_kernel<<<(unsigned)(units * n_qt), kThreads, kSmemBytes, st>>>(P);
+  attn_kernel<<<(unsigned)(pl.units * pl.n_qt), kThreads, kSmemBytes, st>>>(P);
   return check_launch("prefill attn_kernel");
+}
+
+int run_prefill(const cq_paged_cache &cache, const CacheView &cv, int64_t T, const void *q, int q_dtype, int Hq,
+                int q_len, int64_t q_sb, int64_t q_sh, int64_t q_sq, float scale, void *out, int out_dtype,
+                float *lse_out, void *ws, size_t ws_bytes, bool causal, cudaStream_t st) {
+  int r = prefill_prepare(cache, cv, T, q, q_dtype, Hq, q_len, q_sb, q_sh, q_sq, scale, ws, ws_bytes, st);
+  if (r) return r;
+  return prefill_attend(cache, T, Hq, q_len, causal, out, out_dtype, lse_out, ws, ws_bytes, st);
 }
 
 int read_prefill_error(int clear) {

@@ -12,6 +12,12 @@ size_t prefill_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int 
 int run_prefill(const cq_paged_cache &cache, const CacheView &cv, int64_t T, const void *q, int q_dtype, int Hq,
                 int q_len, int64_t q_sb, int64_t q_sh, int64_t q_sq, float scale, void *out, int out_dtype,
                 float *lse_out, void *ws, size_t ws_bytes, bool causal, cudaStream_t st);
+// the two halves of run_prefill: tile images of the history and the queries, then the attention
+int prefill_prepare(const cq_paged_cache &cache, const CacheView &cv, int64_t T, const void *q, int q_dtype, int Hq,
+                    int q_len, int64_t q_sb, int64_t q_sh, int64_t q_sq, float scale, void *ws, size_t ws_bytes,
+                    cudaStream_t st);
+int prefill_attend(const cq_paged_cache &cache, int64_t T, int Hq, int q_len, bool causal, void *out, int out_dtype,
+                   float *lse_out, void *ws, size_t ws_bytes, cudaStream_t st);
 int read_prefill_error(int clear);
 
 }  // namespace cq

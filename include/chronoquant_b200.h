@@ -20,6 +20,7 @@
  *   kernels.py:248-279 chronoquant_sdpa_kernel (+ Metal kernels.py:79-228)
  *                                                          -> cq_sdpa_reference_layout
  *   attention.py:23-74 chronoquant_sdpa (fused + fallback) -> cq_attention
+ *   attention.py:61-74 fallback branch (query chunks)     -> cq_prefill_prepare / cq_prefill_attend
  *   (no reference counterpart) seq-split partial merge     -> cq_lse_merge
  */
 #ifndef CHRONOQUANT_B200_H
@@ -161,6 +162,22 @@ int cq_attention(const cq_paged_cache *cache, int64_t T, const void *q, int q_dt
                  void *stream);
 int cq_attention_workspace(const cq_paged_cache *cache, int64_t T, int32_t n_q_heads, int32_t q_len,
                            int32_t num_splits, size_t *bytes);
+
+/* The two halves of cq_attention's tensor-core query-chunk path, for callers
+ * that schedule or time them apart (no reference counterpart; together they
+ * are the fallback branch of attention.py:61-74).  cq_prefill_prepare
+ * reconstructs the first T cached tokens in fp16 (cache.py:131-160) into the
+ * workspace as tensor-core tile images and packs q*scale (rounded to the
+ * query dtype, attention.py:65) into query tiles; cq_prefill_attend runs the
+ * attention over those images.  Arguments and workspace as cq_attention;
+ * CQ_ERR_UNSUPPORTED for shapes that do not take this path (head_dim != 128,
+ * q_len < 16, GQA group not a power of two <= 16). */
+int cq_prefill_prepare(const cq_paged_cache *cache, int64_t T, const void *q, int q_dtype, int32_t n_q_heads,
+                       int32_t q_len, int64_t q_sb, int64_t q_sh, int64_t q_sq, float scale, void *workspace,
+                       size_t workspace_bytes, void *stream);
+int cq_prefill_attend(const cq_paged_cache *cache, int64_t T, int32_t n_q_heads, int32_t q_len, int32_t causal,
+                      void *out, int out_dtype, float *lse_out, void *workspace, size_t workspace_bytes,
+                      void *stream);
 
 /* A decode step that a CUDA graph can replay at any length (no reference
  * counterpart: the reference steps eagerly from Python, cache.py:198-215 and
