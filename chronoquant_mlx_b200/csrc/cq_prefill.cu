@@ -78,47 +78,80 @@ struct UnpackArgs {
 };
 
 __global__ void __launch_bounds__(256) unpack_kernel(UnpackArgs A) {
-  __shared__ __align__(16) __half tile[kTile][kTile + 8];  // [key][dim], padded rows
+  // K: tile[key][dim]; V: tile[dim][key] (transposed while decoding); padded
+  // rows (68 words) keep both the decode stores and the image reads spread
+  // over the banks
+  __shared__ __align__(16) __half tile[kTile][kTile + 8];
+  __shared__ const __half *s_anchor[kTile];
+  __shared__ const uint32_t *s_codes[kTile];
+  __shared__ float s_scale[kTile];
   const int kt = blockIdx.x, bh = blockIdx.y, comp = blockIdx.z;
   const CacheView &cv = A.cv;
   const int b = bh / cv.H, h = bh - b * cv.H;
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const CompView &c = cv.c[comp];
-  for (int r = warp; r < kTile; r += 8) {
+  if (threadIdx.x < kTile) {
+    const int r = threadIdx.x;
     const int64_t t = (int64_t)kt * kTile + r;
+    const __half *an = nullptr;
+    const uint32_t *cd = nullptr;
+    float sc = 0.f;
     if (t < A.T) {
       const TokLoc L = locate(cv, comp, b, h, t);
-      const __half s = __float2half_rn(L.scale);
+      an = L.anchor;
+      cd = L.codes;
+      sc = L.scale;
+    }
+    s_anchor[r] = an;
+    s_codes[r] = cd;
+    s_scale[r] = sc;
+  }
+  __syncthreads();
+  const bool natural = c.order != CQ_ORDER_MMA;
+  // one item = (token, code word): the 8 dims whose nibbles share a u32
+  for (int it = threadIdx.x; it < kTile * 16; it += 256) {
+    const int r = it >> 4, w = it & 15;
+    const __half *an = s_anchor[r];
+    int dim[8];
 #pragma unroll
-      for (int i = 0; i < 4; ++i) {
-        const int d = lane + 32 * i;
-        const __half a = L.anchor[d];
-        // reconstruct_history (cache.py:141-156): fp16(code) * scale in fp16, then anchor + that
-        // in fp16; I-frames add +0 (where(is_pframe, delta, 0)), turning -0.0 into +0.0
-        __half v = __hadd_rn(a, __float2half_rn(0.f));
-        if (L.codes) v = __hadd_rn(a, __hmul_rn(__int2half_rn(nibble_at(L.codes, d, kTile, c.order) - 8), s));
-        tile[r][d] = v;
+    for (int j = 0; j < 8; ++j) dim[j] = natural ? 8 * w + j : (w >> 1) + 64 * (w & 1) + 8 * j;
+    __half v[8];
+    if (an) {
+      // reconstruct_history (cache.py:141-156): fp16(code) * scale in fp16, then anchor + that
+      // in fp16.  I-frames read as code 0 with scale 0: anchor + (+0), which turns -0.0 into
+      // +0.0 exactly as the reference's where(is_pframe, delta, 0) sum does.
+      const uint32_t word = s_codes[r] ? s_codes[r][w] : 0x88888888u;
+      const __half sh = __float2half_rn(s_scale[r]);
+      __half a[8];
+      if (natural && ((uintptr_t)(an + 8 * w) & 15) == 0) {
+        *reinterpret_cast<uint4 *>(a) = *reinterpret_cast<const uint4 *>(an + 8 * w);
+      } else {
+#pragma unroll
+        for (int j = 0; j < 8; ++j) a[j] = an[dim[j]];
       }
+#pragma unroll
+      for (int j = 0; j < 8; ++j)
+        v[j] = __hadd_rn(a[j], __hmul_rn(__int2half_rn((int)((word >> (4 * j)) & 0xFu) - 8), sh));
     } else {
 #pragma unroll
-      for (int i = 0; i < 4; ++i) tile[r][lane + 32 * i] = __float2half_rn(0.f);
+      for (int j = 0; j < 8; ++j) v[j] = __float2half_rn(0.f);
+    }
+    if (comp == 0 && natural) {
+      *reinterpret_cast<uint4 *>(&tile[r][8 * w]) = *reinterpret_cast<const uint4 *>(v);
+    } else if (comp == 0) {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) tile[r][dim[j]] = v[j];
+    } else {
+#pragma unroll
+      for (int j = 0; j < 8; ++j) tile[dim[j]][r] = v[j];
     }
   }
   __syncthreads();
+  // the image: chunk `ch` holds row `row`, columns col0..col0+7 (row = key for K, head dim for V)
   uint8_t *dst = A.img[comp] + ((int64_t)bh * A.n_kt + kt) * kImgBytes;
   for (int ch = threadIdx.x; ch < kImgBytes / 16; ch += 256) {
     const int half = ch >> 10, row = (ch >> 3) & 127, pos = ch & 7;
-    const int col0 = half * 64 + ((pos ^ (row & 7)) << 3);  // first column of the chunk stored here
-    uint4 v;
-    if (comp == 0) {  // K: image row = key, column = head dim
-      v = *reinterpret_cast<const uint4 *>(&tile[row][col0]);
-    } else {          // V^T: image row = head dim, column = key
-      __half e[8];
-#pragma unroll
-      for (int j = 0; j < 8; ++j) e[j] = tile[col0 + j][row];
-      v = *reinterpret_cast<const uint4 *>(e);
-    }
-    *reinterpret_cast<uint4 *>(dst + (int64_t)ch * 16) = v;
+    const int col0 = half * 64 + ((pos ^ (row & 7)) << 3);
+    *reinterpret_cast<uint4 *>(dst + (int64_t)ch * 16) = *reinterpret_cast<const uint4 *>(&tile[row][col0]);
   }
 }
 
@@ -146,9 +179,20 @@ __global__ void __launch_bounds__(256) q_image_kernel(QArgs A) {
     __half e[8];
     if (tok < A.q_len) {
       const int64_t base = (int64_t)b * A.sb + (int64_t)(h * A.G + g) * A.sh + (int64_t)tok * A.sq + d0;
+      const uint16_t *src = (const uint16_t *)A.q + base;
+      uint16_t raw[8];
+      if (((uintptr_t)src & 15) == 0) {
+        *reinterpret_cast<uint4 *>(raw) = *reinterpret_cast<const uint4 *>(src);
+      } else {
 #pragma unroll
-      for (int j = 0; j < 8; ++j)  // q_scaled = queries * scale in the query dtype (attention.py:65), then fp16
-        e[j] = __float2half_rn(round_dt(load_as_float(A.q, base + j, A.q_dtype) * A.scale, A.q_dtype));
+        for (int j = 0; j < 8; ++j) raw[j] = src[j];
+      }
+#pragma unroll
+      for (int j = 0; j < 8; ++j) {  // q_scaled = queries * scale in the query dtype (attention.py:65), then fp16
+        const float x = A.q_dtype == CQ_BF16 ? __bfloat162float(__ushort_as_bfloat16(raw[j]))
+                                             : __half2float(__ushort_as_half(raw[j]));
+        e[j] = __float2half_rn(round_dt(x * A.scale, A.q_dtype));
+      }
     } else {
 #pragma unroll
       for (int j = 0; j < 8; ++j) e[j] = __float2half_rn(0.f);
