@@ -400,10 +400,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
         for (int c = 0; c < 128; ++c)
           if (k0 + c >= lim) v[c >> 5][c & 31] = __float_as_uint(-INFINITY);
       }
-      float mx = -INFINITY;
+      // row max as a tree over 8 independent partial maxima (one thread owns the row)
+      float pm[8];
 #pragma unroll
-      for (int c = 0; c < 128; ++c) mx = fmaxf(mx, __uint_as_float(v[c >> 5][c & 31]));
-      mx *= kLog2e;
+      for (int t = 0; t < 8; ++t) pm[t] = __uint_as_float(v[0][t]);
+#pragma unroll
+      for (int c = 8; c < 128; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(v[c >> 5][c & 31]));
+      const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
+                             fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * kLog2e;
       if (mx > m + kRescaleThreshold) {
         const float f = ptx_exp2(m - mx);  // 0 while m = -inf
         if (j > 0) {
@@ -434,6 +438,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
         break;
       }
       const uint32_t prow = sP(s) + (uint32_t)r * 128;
+      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 independent partial row sums
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
 #pragma unroll
@@ -443,12 +448,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
           for (int t = 0; t < 8; ++t) {
             const int c = hf * 64 + kc * 8 + t;
             e[t] = ptx_exp2(fmaf(__uint_as_float(v[c >> 5][c & 31]), kLog2e, -m));
-            l += e[t];
+            ps[t] += e[t];
           }
           sts_u128(prow + (uint32_t)hf * kHalfBytes + (uint32_t)((kc ^ (r & 7)) << 4), pack_h2(e[0], e[1]),
                    pack_h2(e[2], e[3]), pack_h2(e[4], e[5]), pack_h2(e[6], e[7]));
         }
       }
+      l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
       ptx::fence_proxy_async_smem();
       tc::fence_before();
       ptx::mbar_arrive(&bars[BPF + s]);
