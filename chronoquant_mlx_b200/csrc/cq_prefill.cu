@@ -18,15 +18,18 @@
 //      one K/V tile serves every head of the group.
 //   3. attn_kernel     -- flash attention over the images: tcgen05.mma computes
 //      S = Q K^T and O += P V into tensor memory (fp16 operands, fp32
-//      accumulation), one CTA per query tile, warp-specialised:
-//        warps 0-3  softmax: one query row per thread (tensor-memory lane),
-//                   base-2 online softmax with a lazy rescale of O, P as fp16
-//                   into shared memory;
-//        warp 4     copies: one bulk copy per 32 KB tile image into a 2-stage
-//                   ring per operand (no multicast);
-//        warp 5     MMA issue (one thread) and tensor-memory allocation.
-//      S is double-buffered in tensor memory so the softmax of tile j overlaps
-//      the MMAs of tiles j+1 (S) and j-1 (P V).
+//      accumulation).  One CTA takes a pair of query tiles (a, b) that read
+//      the same K/V tiles, warp-specialised:
+//        warps 0-3, 4-7  softmax of tile a, tile b: one query row per thread
+//                   (tensor-memory lane), base-2 online softmax with a lazy
+//                   rescale of O; P as fp16 into tensor memory over its own
+//                   S columns, read there by the PV MMA;
+//        warp 8     copies: one bulk copy per 32 KB tile image into a 5-slot
+//                   K/V ring (no multicast);
+//        warp 9     MMA issue (one thread) and tensor-memory allocation.
+//      The MMAs alternate between the tiles (PV_a, S_a, PV_b, S_b per key
+//      tile), so one tile's softmax runs while the tensor core works for the
+//      other, and each scheduler holds two softmax warps.
 //
 // An operand tile image is two 16 KB halves (64 columns each) of 128 rows x
 // 128 bytes; the 16-byte chunk c of row r sits at position c ^ (r % 8) -- the
@@ -49,10 +52,11 @@ namespace prefill {
 constexpr int kTile = 128;          // keys per tile, query rows per tile, head_dim
 constexpr int kImgBytes = 32768;    // one 128 x 128 fp16 tile image
 constexpr int kHalfBytes = 16384;   // 64 columns x 128 rows
-constexpr int kThreads = 192;       // 4 softmax warps, 1 copy warp, 1 MMA warp
+constexpr int kThreads = 320;       // 2 x 4 softmax warps, 1 copy warp, 1 MMA warp
 constexpr int kMinRows = 16;        // shorter query chunks stay on the general kernel
-constexpr uint32_t kTmemCols = 512; // S[0], S[1], O (128 columns each), rounded to a power of two
-constexpr int kSmemTiles = 7 * kImgBytes;  // Q, K[2], V[2], P[2]
+constexpr uint32_t kTmemCols = 512; // S_a, S_b, O_a, O_b (128 columns each)
+constexpr int kRing = 5;            // K/V tile ring slots
+constexpr int kSmemTiles = (2 + kRing) * kImgBytes;  // Q_a, Q_b, ring
 constexpr int kSmemBytes = kSmemTiles + 256 + 1024;  // + barriers, + alignment slack
 constexpr long long kWaitBudget = 2000000000LL;      // clock cycles (about a second)
 constexpr float kLog2e = 1.4426950408889634f;
@@ -66,6 +70,7 @@ __device__ __forceinline__ float ptx_exp2(float x) {
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
   return y;
 }
+
 
 // ---------------------------------------------------------------------------
 // 1. unpack: grid (key tiles, B*H, 2 components), 256 threads
@@ -216,18 +221,16 @@ struct AttnParams {
 
 // barrier slots
 enum {
-  BQ = 0,
-  BKF = 1,   // [2] K tile landed
-  BKE = 3,   // [2] K slot free (S MMA done)
-  BVF = 5,   // [2] V tile landed
-  BVE = 7,   // [2] V slot free (PV MMA done)
-  BSF = 9,   // [2] S ready in tensor memory
-  BSE = 11,  // [2] S read by all softmax threads
-  BPF = 13,  // [2] P written by all softmax threads
-  BPV = 15,  // [2] PV MMA of the tile done (O stable, P slot free)
-  BDR = 17,  // drain: every MMA of the CTA done
-  NBARS = 18
+  BQ = 0,                // both query tiles landed
+  BFULL = 1,             // [kRing] ring slot landed
+  BEMPTY = BFULL + kRing,  // [kRing] ring slot free (every MMA reading it done)
+  BSF = BEMPTY + kRing,  // [2] S of query tile t ready in tensor memory
+  BPF = BSF + 2,         // [2] P of query tile t written (over S_t) by its 128 softmax threads
+  BPV = BPF + 2,         // [2] PV MMA of query tile t done (O_t stable)
+  BDR = BPV + 2,         // drain: every MMA of the CTA done
+  NBARS = BDR + 1
 };
+static_assert(NBARS * 8 + 8 <= 256, "barriers, tensor-memory slot and abort flag fit in front of the tiles");
 
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
@@ -251,10 +254,6 @@ __device__ __forceinline__ bool wait_rows(uint64_t *bar, uint32_t parity, volati
   return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_flag));
 }
 
-__device__ __forceinline__ void sts_u128(uint32_t addr, uint32_t a, uint32_t b, uint32_t c, uint32_t d) {
-  asm volatile("st.shared.v4.b32 [%0], {%1,%2,%3,%4};" ::"r"(addr), "r"(a), "r"(b), "r"(c), "r"(d) : "memory");
-}
-
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
   __half2 v = __floats2half2_rn(lo, hi);
   return *reinterpret_cast<uint32_t *>(&v);
@@ -267,30 +266,30 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
   volatile int *abort_flag = reinterpret_cast<volatile int *>(smem_raw + NBARS * 8 + 4);
   const uint32_t raw = ptx::smem_u32(smem_raw);
   const uint32_t sbase = (raw + 256 + 1023) & ~1023u;  // 1024-byte aligned tile images
-  const uint32_t sQ = sbase;
-  auto sK = [&](int s) { return sbase + (uint32_t)(1 + s) * kImgBytes; };
-  auto sV = [&](int s) { return sbase + (uint32_t)(3 + s) * kImgBytes; };
-  auto sP = [&](int s) { return sbase + (uint32_t)(5 + s) * kImgBytes; };
+  auto sQ = [&](int t) { return sbase + (uint32_t)t * kImgBytes; };        // query tiles a, b
+  auto sR = [&](int L) { return sbase + (uint32_t)(2 + L % kRing) * kImgBytes; };  // ring slot of load L
 
+  // one CTA = a pair of query tiles (2*TQ tokens) of one (sequence, kv-head):
+  // both read the same K/V tiles
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-  const int qt = blockIdx.x % p.n_qt;
-  const int bh = blockIdx.x / p.n_qt;
+  const int n_pairs = p.n_qt >> 1;
+  const int pr = blockIdx.x % n_pairs;
+  const int bh = blockIdx.x / n_pairs;
   const int b = bh / p.Hkv, h = bh - b * p.Hkv;
-  const int q0 = qt * p.TQ;
-  const int qlast = min(q0 + p.TQ, p.q_len) - 1;
+  const int q0 = pr * 2 * p.TQ;  // first query token of tile a; tile b starts at q0 + TQ
+  const int qlast = min(q0 + 2 * p.TQ, p.q_len) - 1;
   const int64_t off = p.T - p.q_len;  // absolute position of query token 0
   const int64_t kend = p.causal ? (off + qlast + 1) : p.T;
   const int n = (int)((kend + kTile - 1) / kTile);
+  // loads in ring order: K_j is load 2j, V_j is load 2j+1
+  auto full_parity = [](int L) { return (uint32_t)((L / kRing) & 1); };
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NBARS; ++i) {
-      const bool by_rows = (i == BSE || i == BSE + 1 || i == BPF || i == BPF + 1);
-      ptx::mbar_init(&bars[i], by_rows ? 128u : 1u);
-    }
+    for (int i = 0; i < NBARS; ++i) ptx::mbar_init(&bars[i], (i == BPF || i == BPF + 1) ? 128u : 1u);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
-  if (warp == 5) {
+  if (warp == 9) {
     tc::tmem_alloc(tmem_slot, kTmemCols);
     tc::tmem_relinquish();
   }
@@ -298,72 +297,84 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
   __syncthreads();
   tc::fence_after();
   const uint32_t tbase = *tmem_slot;
-  const uint32_t tS0 = tbase, tO = tbase + 256;
+  auto tS = [&](int t) { return tbase + (uint32_t)t * 128; };
+  auto tO = [&](int t) { return tbase + 256 + (uint32_t)t * 128; };
 
-  if (warp == 4) {
+  if (warp == 8) {
     // ---------------------------------------------------------------- copies
     if (lane == 0) {
       const uint8_t *kimg = p.kimg + (int64_t)bh * p.n_kt * kImgBytes;
       const uint8_t *vimg = p.vimg + (int64_t)bh * p.n_kt * kImgBytes;
-      ptx::mbar_arrive_expect_tx(&bars[BQ], kImgBytes);
-      ptx::bulk_g2s_a(sQ, p.qimg + ((int64_t)bh * p.n_qt + qt) * kImgBytes, kImgBytes, &bars[BQ]);
-      int nk = 0, nv = 0;
-      for (int j = 0; j < n; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (j >= 2 && !wait_bar(&bars[BKE + s], ph ^ 1, abort_flag)) break;
-        ptx::mbar_arrive_expect_tx(&bars[BKF + s], kImgBytes);
-        ptx::bulk_g2s_a(sK(s), kimg + (int64_t)j * kImgBytes, kImgBytes, &bars[BKF + s]);
-        ++nk;
-        if (j >= 2 && !wait_bar(&bars[BVE + s], ph ^ 1, abort_flag)) break;
-        ptx::mbar_arrive_expect_tx(&bars[BVF + s], kImgBytes);
-        ptx::bulk_g2s_a(sV(s), vimg + (int64_t)j * kImgBytes, kImgBytes, &bars[BVF + s]);
-        ++nv;
+      ptx::mbar_arrive_expect_tx(&bars[BQ], 2 * kImgBytes);  // the pair's two query tiles are adjacent
+      ptx::bulk_g2s_a(sQ(0), p.qimg + ((int64_t)bh * p.n_qt + 2 * pr) * kImgBytes, 2 * kImgBytes, &bars[BQ]);
+      int issued = 0;
+      for (int L = 0; L < 2 * n; ++L) {
+        const int slot = L % kRing;
+        if (L >= kRing && !wait_bar(&bars[BEMPTY + slot], full_parity(L - kRing), abort_flag)) break;
+        ptx::mbar_arrive_expect_tx(&bars[BFULL + slot], kImgBytes);
+        ptx::bulk_g2s_a(sR(L), ((L & 1) ? vimg : kimg) + (int64_t)(L >> 1) * kImgBytes, kImgBytes,
+                        &bars[BFULL + slot]);
+        ++issued;
       }
       // copies still in flight must land before the CTA's shared memory is released
       ptx::mbar_wait_bounded(&bars[BQ], 0, kWaitBudget);
-      for (int i = std::max(0, nk - 2); i < nk; ++i) ptx::mbar_wait_bounded(&bars[BKF + (i & 1)], (i >> 1) & 1, kWaitBudget);
-      for (int i = std::max(0, nv - 2); i < nv; ++i) ptx::mbar_wait_bounded(&bars[BVF + (i & 1)], (i >> 1) & 1, kWaitBudget);
+      for (int L = std::max(0, issued - kRing); L < issued; ++L)
+        ptx::mbar_wait_bounded(&bars[BFULL + L % kRing], full_parity(L), kWaitBudget);
     }
-  } else if (warp == 5) {
+  } else if (warp == 9) {
     // ---------------------------------------------------------------- MMA issue
+    // order: S_a(0) S_b(0) | PV_a(j) S_a(j+1) PV_b(j) S_b(j+1) | ... so that the
+    // softmax of one tile runs while the tensor core works on the other's
     if (lane == 0) {
       constexpr uint32_t idesc = tc::idesc_f16_f32(128, 128);
-      bool ok = wait_bar(&bars[BQ], 0, abort_flag);
-      auto pv = [&](int i) -> bool {
-        const int s = i & 1;
-        const uint32_t ph = (i >> 1) & 1;
-        if (!wait_bar(&bars[BPF + s], ph, abort_flag)) return false;
-        if (!wait_bar(&bars[BVF + s], ph, abort_flag)) return false;
-        tc::fence_after();
+      auto landed = [&](int L) { return wait_bar(&bars[BFULL + L % kRing], full_parity(L), abort_flag); };
+      auto mma_s = [&](int t, int L) {
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t ko = (uint32_t)(k >> 2) * kHalfBytes + (uint32_t)(k & 3) * 32;
-          tc::mma_f16_ss(tO, tc::desc_sw128(sP(s) + ko), tc::desc_sw128(sV(s) + ko), idesc, (i > 0 || k > 0) ? 1u : 0u);
+          tc::mma_f16_ss(tS(t), tc::desc_sw128(sQ(t) + ko), tc::desc_sw128(sR(L) + ko), idesc, k > 0 ? 1u : 0u);
         }
-        tc::commit(&bars[BPV + s]);
-        tc::commit(&bars[BVE + s]);
-        return true;
       };
-      for (int j = 0; ok && j < n; ++j) {
-        const int s = j & 1;
-        const uint32_t ph = (j >> 1) & 1;
-        if (!wait_bar(&bars[BKF + s], ph, abort_flag)) break;
-        if (j >= 2 && !wait_bar(&bars[BSE + s], ph ^ 1, abort_flag)) break;
-        tc::fence_after();
+      auto mma_pv = [&](int t, int j, int L) {  // P_t from tensor memory (columns 0-63 of S_t)
 #pragma unroll
         for (int k = 0; k < 8; ++k) {
           const uint32_t ko = (uint32_t)(k >> 2) * kHalfBytes + (uint32_t)(k & 3) * 32;
-          tc::mma_f16_ss(tS0 + (uint32_t)s * 128, tc::desc_sw128(sQ + ko), tc::desc_sw128(sK(s) + ko), idesc,
-                         k > 0 ? 1u : 0u);
+          tc::mma_f16_ts(tO(t), tS(t) + (uint32_t)k * 8, tc::desc_sw128(sR(L) + ko), idesc,
+                         (j > 0 || k > 0) ? 1u : 0u);
         }
-        tc::commit(&bars[BSF + s]);
-        tc::commit(&bars[BKE + s]);
-        if (j >= 1 && !pv(j - 1)) {
-          ok = false;
-          break;
+      };
+      bool ok = wait_bar(&bars[BQ], 0, abort_flag) && landed(0);
+      if (ok) {
+        tc::fence_after();
+        mma_s(0, 0);
+        tc::commit(&bars[BSF + 0]);
+        mma_s(1, 0);
+        tc::commit(&bars[BSF + 1]);
+        tc::commit(&bars[BEMPTY + 0]);
+      }
+      for (int j = 0; ok && j < n; ++j) {
+        const int Lv = 2 * j + 1, Lk = 2 * j + 2;
+        const bool more = j + 1 < n;
+        if (!wait_bar(&bars[BPF + 0], j & 1, abort_flag) || !landed(Lv)) break;
+        tc::fence_after();
+        mma_pv(0, j, Lv);
+        tc::commit(&bars[BPV + 0]);
+        if (more) {
+          if (!landed(Lk)) break;
+          tc::fence_after();
+          mma_s(0, Lk);
+          tc::commit(&bars[BSF + 0]);
         }
-        if (j == n - 1) ok = pv(j);
+        if (!wait_bar(&bars[BPF + 1], j & 1, abort_flag)) break;
+        tc::fence_after();
+        mma_pv(1, j, Lv);
+        tc::commit(&bars[BPV + 1]);
+        tc::commit(&bars[BEMPTY + Lv % kRing]);
+        if (more) {
+          mma_s(1, Lk);
+          tc::commit(&bars[BSF + 1]);
+          tc::commit(&bars[BEMPTY + Lk % kRing]);
+        }
       }
       // every MMA issued by this thread completes before tensor memory and shared memory are released
       tc::commit(&bars[BDR]);
@@ -371,28 +382,26 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
     }
   } else {
     // ---------------------------------------------------------------- softmax (one row per thread)
-    const int r = threadIdx.x;  // 0..127 = tensor-memory lane = query row of the tile
+    const int t = warp >> 2;            // query tile: warps 0-3 -> a, 4-7 -> b
+    const int r = threadIdx.x & 127;    // tensor-memory lane = query row of the tile
     const int g = r / p.TQ, i = r - g * p.TQ;
-    const int64_t lim = p.causal ? std::min(off + q0 + i + 1, p.T) : p.T;  // keys < lim are visible
-    const uint32_t trow = (uint32_t)(warp * 32) << 16;
+    const int tok = q0 + t * p.TQ + i;  // query token of the row
+    const int64_t lim = p.causal ? std::min(off + tok + 1, p.T) : p.T;  // keys < lim are visible
+    const uint32_t trow = (uint32_t)((warp & 3) * 32) << 16;
     float m = -INFINITY, l = 0.f;
     bool ok = true;
     for (int j = 0; j < n; ++j) {
-      const int s = j & 1;
-      const uint32_t ph = (j >> 1) & 1;
-      if (!wait_rows(&bars[BSF + s], ph, abort_flag)) {
+      if (!wait_rows(&bars[BSF + t], j & 1, abort_flag)) {
         ok = false;
         break;
       }
       tc::fence_after();
       uint32_t v[4][32];
 #pragma unroll
-      for (int c = 0; c < 4; ++c) tc::ld_32x32b_x32(tS0 + trow + (uint32_t)(s * 128 + c * 32), v[c]);
+      for (int c = 0; c < 4; ++c) tc::ld_32x32b_x32(tS(t) + trow + (uint32_t)(c * 32), v[c]);
       tc::wait_ld();
 #pragma unroll
       for (int c = 0; c < 4; ++c) tc::after_wait(v[c]);
-      tc::fence_before();
-      ptx::mbar_arrive(&bars[BSE + s]);
 
       const int64_t k0 = (int64_t)j * kTile;
       if (k0 + kTile > lim) {  // causal edge or keys past T
@@ -403,7 +412,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
       // row max as a tree over 8 independent partial maxima (one thread owns the row)
       float pm[8];
 #pragma unroll
-      for (int t = 0; t < 8; ++t) pm[t] = __uint_as_float(v[0][t]);
+      for (int u = 0; u < 8; ++u) pm[u] = __uint_as_float(v[0][u]);
 #pragma unroll
       for (int c = 8; c < 128; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(v[c >> 5][c & 31]));
       const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
@@ -412,7 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
         const float f = ptx_exp2(m - mx);  // 0 while m = -inf
         if (j > 0) {
           // O holds tiles 0..j-1 at the old base: wait for the last PV, rescale in place
-          if (!wait_rows(&bars[BPV + ((j - 1) & 1)], ((j - 1) >> 1) & 1, abort_flag)) {
+          if (!wait_rows(&bars[BPV + t], (j - 1) & 1, abort_flag)) {
             ok = false;
             break;
           }
@@ -420,49 +429,45 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
 #pragma unroll 1
           for (int c = 0; c < 4; ++c) {
             uint32_t o[32];
-            tc::ld_32x32b_x32(tO + trow + (uint32_t)(c * 32), o);
+            tc::ld_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
             tc::wait_ld();
             tc::after_wait(o);
 #pragma unroll
             for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-            tc::st_32x32b_x32(tO + trow + (uint32_t)(c * 32), o);
+            tc::st_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
           }
           tc::wait_st();
         }
         l *= f;
         m = mx;
       }
-      // P slot s is free once the PV MMA of tile j-2 is done
-      if (j >= 2 && !wait_rows(&bars[BPV + s], ph ^ 1, abort_flag)) {
-        ok = false;
-        break;
-      }
-      const uint32_t prow = sP(s) + (uint32_t)r * 128;
+      // P_t (fp16 pairs) goes over columns 0-63 of S_t, whose values are all in
+      // registers.  The PV MMA of key tile j-1 read the previous P_t there before
+      // S_t(j) overwrote it: MMAs complete in issue order.
+      const uint32_t tP = tS(t) + trow;
       float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 independent partial row sums
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
+        uint32_t w[32];
 #pragma unroll
-        for (int kc = 0; kc < 8; ++kc) {
-          float e[8];
-#pragma unroll
-          for (int t = 0; t < 8; ++t) {
-            const int c = hf * 64 + kc * 8 + t;
-            e[t] = ptx_exp2(fmaf(__uint_as_float(v[c >> 5][c & 31]), kLog2e, -m));
-            ps[t] += e[t];
-          }
-          sts_u128(prow + (uint32_t)hf * kHalfBytes + (uint32_t)((kc ^ (r & 7)) << 4), pack_h2(e[0], e[1]),
-                   pack_h2(e[2], e[3]), pack_h2(e[4], e[5]), pack_h2(e[6], e[7]));
+        for (int q = 0; q < 32; ++q) {
+          const int c = hf * 64 + 2 * q;
+          const float e0 = ptx_exp2(fmaf(__uint_as_float(v[c >> 5][c & 31]), kLog2e, -m));
+          const float e1 = ptx_exp2(fmaf(__uint_as_float(v[(c + 1) >> 5][(c + 1) & 31]), kLog2e, -m));
+          ps[(2 * q) & 7] += e0;
+          ps[(2 * q + 1) & 7] += e1;
+          w[q] = pack_h2(e0, e1);
         }
+        tc::st_32x32b_x32(tP + (uint32_t)(hf * 32), w);
       }
       l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
-      ptx::fence_proxy_async_smem();
+      tc::wait_st();
       tc::fence_before();
-      ptx::mbar_arrive(&bars[BPF + s]);
+      ptx::mbar_arrive(&bars[BPF + t]);
     }
     // ---------------------------------------------------------------- epilogue
-    if (ok && wait_rows(&bars[BPV + ((n - 1) & 1)], ((n - 1) >> 1) & 1, abort_flag)) {
+    if (ok && wait_rows(&bars[BPV + t], (n - 1) & 1, abort_flag)) {
       tc::fence_after();
-      const int tok = q0 + i;
       const bool live = tok < p.q_len;
       const int hq = h * p.G + g;
       const int64_t row = ((int64_t)b * p.Hq + hq) * p.q_len + tok;
@@ -470,7 +475,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
         uint32_t o[32];
-        tc::ld_32x32b_x32(tO + trow + (uint32_t)(c * 32), o);
+        tc::ld_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
         tc::wait_ld();
         tc::after_wait(o);
         if (live) {
@@ -505,13 +510,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
 
   tc::fence_before();
   __syncthreads();
-  if (warp == 5) {
+  if (warp == 9) {
     tc::fence_after();
     tc::tmem_dealloc(tbase, kTmemCols);
   }
 }
 
 }  // namespace prefill
+
 
 // ---------------------------------------------------------------------------
 // host side
@@ -529,7 +535,7 @@ static void prefill_shape(const cq_paged_cache &c, int64_t T, int n_q_heads, int
   const int G = n_q_heads / c.kv_heads;
   n_kt = (int)((T + kTile - 1) / kTile);
   TQ = kTile / G;
-  n_qt = (q_len + TQ - 1) / TQ;
+  n_qt = ((q_len + TQ - 1) / TQ + 1) & ~1;  // whole pairs: the tail tile of an odd count is all padding
 }
 
 size_t prefill_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len) {
@@ -618,7 +624,7 @@ int prefill_attend(const cq_paged_cache &cache, int64_t T, int Hq, int q_len, bo
   P.lse = lse_out;
   cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return set_error(CQ_ERR_CUDA, std::string("prefill attn_kernel smem: ") + cudaGetErrorString(e));
-  attn_kernel<<<(unsigned)(pl.units * pl.n_qt), kThreads, kSmemBytes, st>>>(P);
+  attn_kernel<<<(unsigned)(pl.units * (pl.n_qt / 2)), kThreads, kSmemBytes, st>>>(P);
   return check_launch("prefill attn_kernel");
 }
 

@@ -72,6 +72,19 @@ __device__ __forceinline__ void mma_f16_ss(uint32_t d_tmem, uint64_t a_desc, uin
       : "memory");
 }
 
+// D[tmem] (+)= A[tmem] * B[smem]^T, issued by one thread.  A (K-major) sits in
+// tensor memory: lane i = row i, each 32-bit column two consecutive K elements
+// (the lower K index in the low half), so a K = 16 step reads 8 columns.
+__device__ __forceinline__ void mma_f16_ts(uint32_t d_tmem, uint32_t a_tmem, uint64_t b_desc, uint32_t idesc,
+                                           uint32_t accumulate) {
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "setp.ne.b32 p, %4, 0;\n\t"
+      "tcgen05.mma.cta_group::1.kind::f16 [%0], [%1], %2, %3, p;\n\t}"
+      ::"r"(d_tmem), "r"(a_tmem), "l"(b_desc), "r"(idesc), "r"(accumulate)
+      : "memory");
+}
+
 // ---------------------------------------------------------------- tensor-memory loads / stores
 // 32 lanes x 32 consecutive 32-bit columns: thread t of the warp gets lane
 // (warp % 4) * 32 + t, columns col .. col+31 into v[0..31].
