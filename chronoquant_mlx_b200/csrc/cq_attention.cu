@@ -253,6 +253,13 @@ int run_generic(const CacheView &cv, int64_t T, const void *q, int q_dtype, int 
   return check_launch("combine_kernel");
 }
 
+int launch_split_combine(const float *ws_m, const float *ws_l, const float *ws_o, int64_t rows, int splits, int D,
+                         void *out, int out_dtype, float *lse_out, cudaStream_t st) {
+  const int64_t cblocks = (rows * 32 + 255) / 256;
+  combine_kernel<<<(unsigned)cblocks, 256, 0, st>>>(ws_m, ws_l, ws_o, rows, splits, D, out, out_dtype, lse_out);
+  return check_launch("combine_kernel");
+}
+
 }  // namespace cq
 
 using namespace cq;

@@ -43,6 +43,7 @@
 #include <algorithm>
 
 #include "cq_common.cuh"
+#include "cq_prefill.cuh"
 #include "cq_ptx.cuh"
 #include "cq_tcgen05.cuh"
 
@@ -217,6 +218,10 @@ struct AttnParams {
   void *out;
   int out_dtype;
   float *lse;
+  // key-range splits of each pair (whole waves of CTAs): with splits > 1 each
+  // CTA writes its partial (m natural-log, l, unnormalised O) per row and split
+  int splits;
+  float *ws_m, *ws_l, *ws_o;
 };
 
 // barrier slots
@@ -232,13 +237,15 @@ enum {
 };
 static_assert(NBARS * 8 + 8 <= 256, "barriers, tensor-memory slot and abort flag fit in front of the tiles");
 
+// Polls with try_wait (no suspend-time hint: a hinted wait woke hundreds of
+// cycles after the phase completed, on the critical path of every key tile).
 __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
   if (ptx::mbar_try_wait(bar, parity)) return true;
   const long long t0 = clock64();
   for (;;) {
 #pragma unroll 1
-    for (int i = 0; i < 8; ++i)
-      if (ptx::mbar_try_wait_sleep(bar, parity, 1000u)) return true;
+    for (int i = 0; i < 32; ++i)
+      if (ptx::mbar_try_wait(bar, parity)) return true;
     if (*abort_flag) return false;
     if (clock64() - t0 > kWaitBudget) {
       *abort_flag = 1;
@@ -252,6 +259,27 @@ __device__ __forceinline__ bool wait_bar(uint64_t *bar, uint32_t parity, volatil
 // warp-collective tensor-memory loads and stores stay convergent
 __device__ __forceinline__ bool wait_rows(uint64_t *bar, uint32_t parity, volatile int *abort_flag) {
   return __all_sync(0xffffffffu, wait_bar(bar, parity, abort_flag));
+}
+
+// Packed fp32 pairs (sm_100 f32x2 arithmetic): one instruction for two lanes
+// of a softmax row.
+__device__ __forceinline__ uint64_t f2_pack(float lo, float hi) {
+  uint64_t r;
+  asm("mov.b64 %0, {%1, %2};" : "=l"(r) : "f"(lo), "f"(hi));
+  return r;
+}
+__device__ __forceinline__ void f2_unpack(uint64_t v, float &lo, float &hi) {
+  asm("mov.b64 {%0, %1}, %2;" : "=f"(lo), "=f"(hi) : "l"(v));
+}
+__device__ __forceinline__ uint64_t f2_fma(uint64_t a, uint64_t b, uint64_t c) {
+  uint64_t d;
+  asm("fma.rn.f32x2 %0, %1, %2, %3;" : "=l"(d) : "l"(a), "l"(b), "l"(c));
+  return d;
+}
+__device__ __forceinline__ uint64_t f2_add(uint64_t a, uint64_t b) {
+  uint64_t d;
+  asm("add.rn.f32x2 %0, %1, %2;" : "=l"(d) : "l"(a), "l"(b));
+  return d;
 }
 
 __device__ __forceinline__ uint32_t pack_h2(float lo, float hi) {
@@ -273,14 +301,17 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
   // both read the same K/V tiles
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_pairs = p.n_qt >> 1;
-  const int pr = blockIdx.x % n_pairs;
-  const int bh = blockIdx.x / n_pairs;
+  const int split = blockIdx.x % p.splits;
+  const int pr = (blockIdx.x / p.splits) % n_pairs;
+  const int bh = blockIdx.x / p.splits / n_pairs;
   const int b = bh / p.Hkv, h = bh - b * p.Hkv;
   const int q0 = pr * 2 * p.TQ;  // first query token of tile a; tile b starts at q0 + TQ
   const int qlast = min(q0 + 2 * p.TQ, p.q_len) - 1;
   const int64_t off = p.T - p.q_len;  // absolute position of query token 0
   const int64_t kend = p.causal ? (off + qlast + 1) : p.T;
-  const int n = (int)((kend + kTile - 1) / kTile);
+  const int n_all = (int)((kend + kTile - 1) / kTile);
+  const int j0 = (int)((int64_t)split * n_all / p.splits);  // this CTA's key tiles: j0 .. j0+n-1
+  const int n = (int)((int64_t)(split + 1) * n_all / p.splits) - j0;
   // loads in ring order: K_j is load 2j, V_j is load 2j+1
   auto full_parity = [](int L) { return (uint32_t)((L / kRing) & 1); };
 
@@ -302,9 +333,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
 
   if (warp == 8) {
     // ---------------------------------------------------------------- copies
-    if (lane == 0) {
-      const uint8_t *kimg = p.kimg + (int64_t)bh * p.n_kt * kImgBytes;
-      const uint8_t *vimg = p.vimg + (int64_t)bh * p.n_kt * kImgBytes;
+    if (lane == 0 && n > 0) {
+      const uint8_t *kimg = p.kimg + ((int64_t)bh * p.n_kt + j0) * kImgBytes;
+      const uint8_t *vimg = p.vimg + ((int64_t)bh * p.n_kt + j0) * kImgBytes;
       ptx::mbar_arrive_expect_tx(&bars[BQ], 2 * kImgBytes);  // the pair's two query tiles are adjacent
       ptx::bulk_g2s_a(sQ(0), p.qimg + ((int64_t)bh * p.n_qt + 2 * pr) * kImgBytes, 2 * kImgBytes, &bars[BQ]);
       int issued = 0;
@@ -325,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
     // ---------------------------------------------------------------- MMA issue
     // order: S_a(0) S_b(0) | PV_a(j) S_a(j+1) PV_b(j) S_b(j+1) | ... so that the
     // softmax of one tile runs while the tensor core works on the other's
-    if (lane == 0) {
+    if (lane == 0 && n > 0) {
       constexpr uint32_t idesc = tc::idesc_f16_f32(128, 128);
       auto landed = [&](int L) { return wait_bar(&bars[BFULL + L % kRing], full_parity(L), abort_flag); };
       auto mma_s = [&](int t, int L) {
@@ -403,7 +434,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
 #pragma unroll
       for (int c = 0; c < 4; ++c) tc::after_wait(v[c]);
 
-      const int64_t k0 = (int64_t)j * kTile;
+      const int64_t k0 = (int64_t)(j0 + j) * kTile;
       if (k0 + kTile > lim) {  // causal edge or keys past T
 #pragma unroll
         for (int c = 0; c < 128; ++c)
@@ -445,32 +476,47 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
       // registers.  The PV MMA of key tile j-1 read the previous P_t there before
       // S_t(j) overwrote it: MMAs complete in issue order.
       const uint32_t tP = tS(t) + trow;
-      float ps[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};  // 8 independent partial row sums
+      // exponent arguments and row sums as packed fp32 pairs: (s * log2 e - m) for
+      // two keys per instruction, 4 independent pair partial sums
+      // while no key of the row has been visible (m = -inf), every score is -inf and P is 0
+      const float nm = (m == -INFINITY) ? 0.f : -m;
+      const uint64_t l2e2 = f2_pack(kLog2e, kLog2e), nm2 = f2_pack(nm, nm);
+      uint64_t ps[4] = {0ull, 0ull, 0ull, 0ull};
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         uint32_t w[32];
 #pragma unroll
         for (int q = 0; q < 32; ++q) {
           const int c = hf * 64 + 2 * q;
-          const float e0 = ptx_exp2(fmaf(__uint_as_float(v[c >> 5][c & 31]), kLog2e, -m));
-          const float e1 = ptx_exp2(fmaf(__uint_as_float(v[(c + 1) >> 5][(c + 1) & 31]), kLog2e, -m));
-          ps[(2 * q) & 7] += e0;
-          ps[(2 * q + 1) & 7] += e1;
+          float x0, x1;
+          f2_unpack(f2_fma(f2_pack(__uint_as_float(v[c >> 5][c & 31]), __uint_as_float(v[c >> 5][(c & 31) + 1])),
+                           l2e2, nm2), x0, x1);
+          const float e0 = ptx_exp2(x0), e1 = ptx_exp2(x1);
+          ps[q & 3] = f2_add(ps[q & 3], f2_pack(e0, e1));
           w[q] = pack_h2(e0, e1);
         }
         tc::st_32x32b_x32(tP + (uint32_t)(hf * 32), w);
       }
-      l += ((ps[0] + ps[1]) + (ps[2] + ps[3])) + ((ps[4] + ps[5]) + (ps[6] + ps[7]));
+      float s0, s1, s2, s3;
+      f2_unpack(f2_add(ps[0], ps[1]), s0, s1);
+      f2_unpack(f2_add(ps[2], ps[3]), s2, s3);
+      l += (s0 + s1) + (s2 + s3);
       tc::wait_st();
       tc::fence_before();
       ptx::mbar_arrive(&bars[BPF + t]);
     }
     // ---------------------------------------------------------------- epilogue
-    if (ok && wait_rows(&bars[BPV + t], (n - 1) & 1, abort_flag)) {
+    const bool live = tok < p.q_len;
+    const int hq = h * p.G + g;
+    const int64_t row = ((int64_t)b * p.Hq + hq) * p.q_len + tok;
+    const int64_t prow = row * p.splits + split;  // partial slot of this row and split
+    if (n == 0) {  // an empty key range: a partial with no mass
+      if (live) {
+        p.ws_m[prow] = -INFINITY;
+        p.ws_l[prow] = 0.f;
+      }
+    } else if (ok && wait_rows(&bars[BPV + t], (n - 1) & 1, abort_flag)) {
       tc::fence_after();
-      const bool live = tok < p.q_len;
-      const int hq = h * p.G + g;
-      const int64_t row = ((int64_t)b * p.Hq + hq) * p.q_len + tok;
       const float inv = l > 0.f ? 1.f / l : 0.f;
 #pragma unroll 1
       for (int c = 0; c < 4; ++c) {
@@ -478,7 +524,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
         tc::ld_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
         tc::wait_ld();
         tc::after_wait(o);
-        if (live) {
+        if (live && p.splits > 1) {
+          float4 *dst = reinterpret_cast<float4 *>(p.ws_o + prow * kTile + c * 32);
+#pragma unroll
+          for (int e = 0; e < 8; ++e)
+            dst[e] = make_float4(__uint_as_float(o[4 * e]), __uint_as_float(o[4 * e + 1]),
+                                 __uint_as_float(o[4 * e + 2]), __uint_as_float(o[4 * e + 3]));
+        } else if (live) {
           if (p.out_dtype == CQ_F32) {
             float4 *dst = reinterpret_cast<float4 *>((float *)p.out + row * kTile + c * 32);
 #pragma unroll
@@ -504,7 +556,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
           }
         }
       }
-      if (live && p.lse) p.lse[row] = l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : -INFINITY;
+      if (live && p.splits > 1) {
+        p.ws_m[prow] = (m == -INFINITY) ? -INFINITY : m * 0.6931471805599453f;
+        p.ws_l[prow] = l;
+      } else if (live && p.lse) {
+        p.lse[row] = l > 0.f ? (m + __log2f(l)) * 0.6931471805599453f : -INFINITY;
+      }
     }
   }
 
@@ -530,39 +587,80 @@ bool prefill_supported(const cq_paged_cache &c, int n_q_heads, int q_len) {
   return G >= 1 && G <= 16 && (G & (G - 1)) == 0;
 }
 
-static void prefill_shape(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len, int &n_kt, int &TQ,
-                          int &n_qt) {
+static int sm_count() {
+  int dev = 0, n = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev) != cudaSuccess)
+    n = 0;
+  return n > 0 ? n : 148;
+}
+
+struct Shape {
+  int n_kt, TQ, n_qt, splits;
+  int64_t rows;  // output rows B * Hq * q_len
+};
+
+// Tile counts, and the number of key-range splits per query-tile pair: the
+// count (1..8, at least 4 key tiles each) whose CTAs fill whole waves of SMs
+// best, each extra split charged 1.5 % for its pipeline fill and merge.
+static Shape prefill_shape(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len) {
+  Shape sh;
   const int G = n_q_heads / c.kv_heads;
-  n_kt = (int)((T + kTile - 1) / kTile);
-  TQ = kTile / G;
-  n_qt = ((q_len + TQ - 1) / TQ + 1) & ~1;  // whole pairs: the tail tile of an odd count is all padding
+  sh.n_kt = (int)((T + kTile - 1) / kTile);
+  sh.TQ = kTile / G;
+  sh.n_qt = ((q_len + sh.TQ - 1) / sh.TQ + 1) & ~1;  // whole pairs: the tail tile of an odd count is all padding
+  sh.rows = (int64_t)c.batch * n_q_heads * q_len;
+  const int64_t pairs = (int64_t)c.batch * c.kv_heads * (sh.n_qt / 2);
+  const int nsm = sm_count();
+  sh.splits = 1;
+  double best = (double)((pairs + nsm - 1) / nsm);
+  for (int s = 2; s <= 8 && sh.n_kt / s >= 4; ++s) {
+    const double cost = (double)((pairs * s + nsm - 1) / nsm) / s * (1.0 + 0.015 * (s - 1));
+    if (cost < best - 1e-9) {
+      best = cost;
+      sh.splits = s;
+    }
+  }
+  return sh;
+}
+
+static size_t partial_bytes(const Shape &sh) {
+  return sh.splits > 1 ? (size_t)sh.rows * sh.splits * (2 + kTile) * sizeof(float) : 0;
 }
 
 size_t prefill_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len) {
   if (!prefill_supported(c, n_q_heads, q_len)) return 0;
-  int n_kt, TQ, n_qt;
-  prefill_shape(c, T, n_q_heads, q_len, n_kt, TQ, n_qt);
+  const Shape sh = prefill_shape(c, T, n_q_heads, q_len);
   const size_t units = (size_t)c.batch * c.kv_heads;
-  return units * (2 * (size_t)n_kt + (size_t)n_qt) * kImgBytes;
+  return units * (2 * (size_t)sh.n_kt + (size_t)sh.n_qt) * kImgBytes + partial_bytes(sh);
 }
 
 struct Plan {
-  int n_kt, TQ, n_qt, units;
+  int n_kt, TQ, n_qt, units, splits;
+  int64_t rows;
   uint8_t *kimg, *vimg, *qimg;
+  float *ws_m, *ws_l, *ws_o;  // split partials (splits > 1)
 };
 
 static int make_plan(const cq_paged_cache &cache, int64_t T, int Hq, int q_len, void *ws, size_t ws_bytes, Plan &pl) {
   CQ_REQUIRE(prefill_supported(cache, Hq, q_len), CQ_ERR_UNSUPPORTED,
              "query-chunk path: needs head_dim 128, q_len >= 16 and a GQA group that is a power of two <= 16");
-  prefill_shape(cache, T, Hq, q_len, pl.n_kt, pl.TQ, pl.n_qt);
+  const Shape sh = prefill_shape(cache, T, Hq, q_len);
+  pl.n_kt = sh.n_kt;
+  pl.TQ = sh.TQ;
+  pl.n_qt = sh.n_qt;
+  pl.splits = sh.splits;
+  pl.rows = sh.rows;
   const size_t need = prefill_workspace(cache, T, Hq, q_len);
   CQ_REQUIRE(ws && ws_bytes >= need, CQ_ERR_WORKSPACE, "cq_attention: workspace too small");
   CQ_REQUIRE(((uintptr_t)ws & 15) == 0, CQ_ERR_INVALID, "cq_attention: workspace must be 16-byte aligned for query chunks");
   pl.units = cache.batch * cache.kv_heads;
-  CQ_REQUIRE((int64_t)pl.units * pl.n_qt < (1LL << 31), CQ_ERR_INVALID, "cq_attention: grid too large");
+  CQ_REQUIRE((int64_t)pl.units * pl.n_qt * pl.splits < (1LL << 31), CQ_ERR_INVALID, "cq_attention: grid too large");
   pl.kimg = (uint8_t *)ws;
   pl.vimg = pl.kimg + (size_t)pl.units * pl.n_kt * kImgBytes;
   pl.qimg = pl.vimg + (size_t)pl.units * pl.n_kt * kImgBytes;
+  pl.ws_o = (float *)(pl.qimg + (size_t)pl.units * pl.n_qt * kImgBytes);  // first: 16-byte aligned rows
+  pl.ws_m = pl.ws_o + pl.rows * pl.splits * kTile;
+  pl.ws_l = pl.ws_m + pl.rows * pl.splits;
   return CQ_OK;
 }
 
@@ -622,10 +720,16 @@ int prefill_attend(const cq_paged_cache &cache, int64_t T, int Hq, int q_len, bo
   P.out = out;
   P.out_dtype = out_dtype;
   P.lse = lse_out;
+  P.splits = pl.splits;
+  P.ws_m = pl.ws_m;
+  P.ws_l = pl.ws_l;
+  P.ws_o = pl.ws_o;
   cudaError_t e = cudaFuncSetAttribute(attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, kSmemBytes);
   if (e != cudaSuccess) return set_error(CQ_ERR_CUDA, std::string("prefill attn_kernel smem: ") + cudaGetErrorString(e));
-  attn_kernel<<<(unsigned)(pl.units * (pl.n_qt / 2)), kThreads, kSmemBytes, st>>>(P);
-  return check_launch("prefill attn_kernel");
+  attn_kernel<<<(unsigned)(pl.units * (pl.n_qt / 2) * pl.splits), kThreads, kSmemBytes, st>>>(P);
+  r = check_launch("prefill attn_kernel");
+  if (r || pl.splits == 1) return r;
+  return launch_split_combine(pl.ws_m, pl.ws_l, pl.ws_o, pl.rows, pl.splits, kTile, out, out_dtype, lse_out, st);
 }
 
 int run_prefill(const cq_paged_cache &cache, const CacheView &cv, int64_t T, const void *q, int q_dtype, int Hq,

@@ -19,5 +19,8 @@ int prefill_prepare(const cq_paged_cache &cache, const CacheView &cv, int64_t T,
 int prefill_attend(const cq_paged_cache &cache, int64_t T, int Hq, int q_len, bool causal, void *out, int out_dtype,
                    float *lse_out, void *ws, size_t ws_bytes, cudaStream_t st);
 int read_prefill_error(int clear);
+// merge of split-KV partials (m natural-log, l, unnormalised o; [row][split]) into out and lse (cq_attention.cu)
+int launch_split_combine(const float *ws_m, const float *ws_l, const float *ws_o, int64_t rows, int splits, int D,
+                         void *out, int out_dtype, float *lse_out, cudaStream_t st);
 
 }  // namespace cq

@@ -65,6 +65,8 @@ CASES = [
     (1, 1, 16, 513, 16, 64, 32, 3, 0.05, "f16", True),      # GQA 16, FT-V3, shortest chunk
     (2, 4, 16, 2100, 300, 64, 32, 3, 0.05, "bf16", True),   # FT-V3, several key tiles
     (1, 2, 8, 256, 256, 32, 8, 4, 0.0, "f16", True),        # chunk = whole cache (first prefill)
+    (1, 2, 8, 1024, 1024, 32, 8, 4, 0.0, "bf16", True),     # key-range splits, some ranges empty
+    (2, 2, 8, 3000, 64, 32, 8, 4, 0.0, "f16", False),       # key-range splits, mask None
 ]
 
 
