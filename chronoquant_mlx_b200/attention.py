@@ -109,10 +109,11 @@ def chronoquant_sdpa(queries: torch.Tensor, keys, values, cache, scale: float, m
     return _run(desc, T, queries, scale, mask, causal, out, cache.workspace, queries.device)
 
 
-def chronoquant_sdpa_with_lse(queries: torch.Tensor, cache, scale: float):
-    """Decode/prefill attention (mask None for q_len 1, causal otherwise)
-    returning (out fp32 [B, Hq, Tq, D], lse fp32 [B, Hq, Tq]) for merging
-    sequence shards (see ``distributed.py``)."""
+def chronoquant_sdpa_with_lse(queries: torch.Tensor, cache, scale: float, causal: bool = True):
+    """Decode/prefill attention returning (out fp32 [B, Hq, Tq, D], lse fp32
+    [B, Hq, Tq]) for merging sequence shards (``distributed.py``).  ``causal``
+    applies the end-anchored causal mask when Tq > 1 (no effect for Tq 1); a
+    shard whose keys all precede the queries passes False."""
     B, Hq, Tq, D = queries.shape
     require_cuda(queries)
     st = cache.store
@@ -126,7 +127,7 @@ def chronoquant_sdpa_with_lse(queries: torch.Tensor, cache, scale: float):
     need = ctypes.c_size_t(0)
     _lib.check(L.cq_attention_workspace(ctypes.byref(desc), T, Hq, Tq, 0, ctypes.byref(need)), "attention")
     ws = cache.workspace(need.value)
-    _lib.check(L.cq_attention(ctypes.byref(desc), T, q.data_ptr(), cq_dtype(q), Hq, Tq, 1, qs[0], qs[1], qs[2],
-                              float(scale), out.data_ptr(), _lib.CQ_F32, lse.data_ptr(), ws.data_ptr(),
+    _lib.check(L.cq_attention(ctypes.byref(desc), T, q.data_ptr(), cq_dtype(q), Hq, Tq, 1 if causal else 0, qs[0],
+                              qs[1], qs[2], float(scale), out.data_ptr(), _lib.CQ_F32, lse.data_ptr(), ws.data_ptr(),
                               ws.numel() * 4, 0, stream_ptr(queries.device)), "attention")
     return out, lse

@@ -1,0 +1,77 @@
+"""Process bodies for the gloo (CPU) tests of the sequence-split protocol.
+
+Each rank holds one shard of a sequence (``shard_bounds``), computes its exact
+partial attention with the oracle (float64 numpy: the test's checker), and
+exchanges partials with ``exchange_partials`` over a gloo process group.
+Results go back through a multiprocessing queue."""
+
+import datetime
+import math
+import os
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from oracle import cq_oracle as O
+
+
+def _init(rank, world, port, timeout_s):
+    os.environ["MASTER_ADDR"] = "127.0.0.1"
+    os.environ["MASTER_PORT"] = str(port)
+    dist.init_process_group("gloo", rank=rank, world_size=world,
+                            timeout=datetime.timedelta(seconds=timeout_s))
+
+
+def exact_partial(q_scaled, k, v, causal):
+    """(o [B,Hq,Tq,D], lse [B,Hq,Tq]) of float64 attention of q over one
+    shard's decoded k/v; causal anchors the mask at the end of the shard."""
+    B, Hq, Tq, D = q_scaled.shape
+    Hkv, T = k.shape[1], k.shape[2]
+    if T == 0:
+        return np.zeros((B, Hq, Tq, D)), np.full((B, Hq, Tq), -np.inf)
+    qg = q_scaled.astype(np.float64).reshape(B, Hkv, Hq // Hkv, Tq, D)
+    s = np.einsum("bgrqd,bgtd->bgrqt", qg, k.astype(np.float64))
+    if causal and Tq > 1:
+        s = np.where(O.causal_mask(Tq, T), s, -np.inf)
+    m = s.max(-1, keepdims=True)
+    p = np.exp(s - m)
+    lsum = p.sum(-1)
+    o = np.einsum("bgrqt,bgtd->bgrqd", p, v.astype(np.float64)) / lsum[..., None]
+    return o.reshape(B, Hq, Tq, D), (m[..., 0] + np.log(lsum)).reshape(B, Hq, Tq)
+
+
+def shard_worker(rank, world, port, K, V, q_scaled, stride_k, stride_v, queue):
+    """Encode this rank's shard with the oracle, take the exact partial, all-gather."""
+    from chronoquant_mlx_b200.distributed import exchange_partials, shard_bounds
+    try:
+        _init(rank, world, port, 30)
+        T = K.shape[2]
+        lo, hi = shard_bounds(T, world, stride_k, stride_v)[rank]
+        c = O.OracleCache(stride_k=stride_k, stride_v=stride_v)
+        if hi > lo:
+            c.update_and_fetch(K[:, :, lo:hi], V[:, :, lo:hi])
+            k, v = c.reconstruct_history_f32()
+        else:
+            k = np.zeros(K.shape[:2] + (0, K.shape[3]))
+            v = k
+        o, lse = exact_partial(q_scaled, k, v, causal=rank == world - 1)
+        o_all, lse_all = exchange_partials(torch.from_numpy(o), torch.from_numpy(lse))
+        queue.put((rank, o_all.numpy(), lse_all.numpy(), None))
+        dist.destroy_process_group()
+    except Exception as e:  # report instead of hanging the parent
+        queue.put((rank, None, None, repr(e)))
+
+
+def failing_worker(rank, world, port, queue):
+    """Rank 1 fails before the exchange (a host-side fault); rank 0 must see
+    an error from its collective within the process-group timeout."""
+    from chronoquant_mlx_b200.distributed import exchange_partials
+    _init(rank, world, port, 5)
+    if rank == 1:
+        os._exit(3)  # leaves without joining the collective (exit code 3)
+    try:
+        exchange_partials(torch.zeros(1, 2, 1, 8), torch.zeros(1, 2, 1))
+        queue.put((rank, "no error"))
+    except Exception as e:
+        queue.put((rank, "error: " + type(e).__name__))
