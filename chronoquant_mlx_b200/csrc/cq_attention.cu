@@ -152,6 +152,36 @@ __global__ void combine_kernel(const float *ws_m, const float *ws_l, const float
   if (row >= rows) return;
   const float *m = ws_m + row * splits;
   const float *l = ws_l + row * splits;
+  if (D == 128 && splits <= 8 && ((uintptr_t)ws_o & 15) == 0) {
+    // one float4 of head dims per lane: weights exp(m_s - M) once per row, 16-byte loads
+    float M = -INFINITY;
+    for (int s = 0; s < splits; ++s) M = fmaxf(M, m[s]);
+    float w[8], L = 0.f;
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      w[s] = (s < splits && m[s] != -INFINITY) ? expf(m[s] - M) : 0.f;
+      if (s < splits) L += l[s] * w[s];
+    }
+    const float inv = (L > 0.f) ? 1.f / L : 0.f;
+    float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int s = 0; s < 8; ++s) {
+      if (s < splits && w[s] != 0.f) {
+        const float4 o = reinterpret_cast<const float4 *>(ws_o + (row * splits + s) * 128)[lane];
+        acc.x += o.x * w[s];
+        acc.y += o.y * w[s];
+        acc.z += o.z * w[s];
+        acc.w += o.w * w[s];
+      }
+    }
+    const int64_t base = row * 128 + lane * 4;
+    store_from_float(out, base, acc.x * inv, out_dtype);
+    store_from_float(out, base + 1, acc.y * inv, out_dtype);
+    store_from_float(out, base + 2, acc.z * inv, out_dtype);
+    store_from_float(out, base + 3, acc.w * inv, out_dtype);
+    if (lse_out && lane == 0) lse_out[row] = (L > 0.f) ? M + logf(L) : -INFINITY;
+    return;
+  }
   float M = -INFINITY;
   for (int s = 0; s < splits; ++s) M = fmaxf(M, m[s]);
   float L = 0.f;

@@ -427,73 +427,77 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
         break;
       }
       tc::fence_after();
-      uint32_t v[4][32];
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tc::ld_32x32b_x32(tS(t) + trow + (uint32_t)(c * 32), v[c]);
-      tc::wait_ld();
-#pragma unroll
-      for (int c = 0; c < 4; ++c) tc::after_wait(v[c]);
-
       const int64_t k0 = (int64_t)(j0 + j) * kTile;
-      if (k0 + kTile > lim) {  // causal edge or keys past T
+      const bool edge = k0 + kTile > lim;  // causal edge or keys past T
+      // Two passes over S_t so that only part of a row is live in registers:
+      // the row max (64 columns per load pair), then the exponentials.
+      auto load_half = [&](int hf, uint32_t (&va)[32], uint32_t (&vb)[32]) {
+        tc::ld_32x32b_x32(tS(t) + trow + (uint32_t)(hf * 64), va);
+        tc::ld_32x32b_x32(tS(t) + trow + (uint32_t)(hf * 64 + 32), vb);
+        tc::wait_ld();
+        tc::after_wait(va);
+        tc::after_wait(vb);
+        if (edge) {
 #pragma unroll
-        for (int c = 0; c < 128; ++c)
-          if (k0 + c >= lim) v[c >> 5][c & 31] = __float_as_uint(-INFINITY);
-      }
+          for (int c = 0; c < 32; ++c) {
+            if (k0 + hf * 64 + c >= lim) va[c] = __float_as_uint(-INFINITY);
+            if (k0 + hf * 64 + 32 + c >= lim) vb[c] = __float_as_uint(-INFINITY);
+          }
+        }
+      };
       // row max as a tree over 8 independent partial maxima (one thread owns the row)
       float pm[8];
 #pragma unroll
-      for (int u = 0; u < 8; ++u) pm[u] = __uint_as_float(v[0][u]);
+      for (int u = 0; u < 8; ++u) pm[u] = -INFINITY;
 #pragma unroll
-      for (int c = 8; c < 128; ++c) pm[c & 7] = fmaxf(pm[c & 7], __uint_as_float(v[c >> 5][c & 31]));
+      for (int hf = 0; hf < 2; ++hf) {
+        uint32_t va[32], vb[32];
+        load_half(hf, va, vb);
+#pragma unroll
+        for (int c = 0; c < 32; ++c)
+          pm[c & 7] = fmaxf(pm[c & 7], fmaxf(__uint_as_float(va[c]), __uint_as_float(vb[c])));
+      }
       const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                              fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * kLog2e;
-      if (mx > m + kRescaleThreshold) {
-        const float f = ptx_exp2(m - mx);  // 0 while m = -inf
-        if (j > 0) {
-          // O holds tiles 0..j-1 at the old base: wait for the last PV, rescale in place
-          if (!wait_rows(&bars[BPV + t], (j - 1) & 1, abort_flag)) {
-            ok = false;
-            break;
-          }
-          tc::fence_after();
-#pragma unroll 1
-          for (int c = 0; c < 4; ++c) {
-            uint32_t o[32];
-            tc::ld_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
-            tc::wait_ld();
-            tc::after_wait(o);
-#pragma unroll
-            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-            tc::st_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
-          }
-          tc::wait_st();
-        }
+      float f = 1.f;  // rescale of O and l when the running max moves up by more than the threshold
+      const bool rescale = mx > m + kRescaleThreshold;
+      if (rescale) {
+        f = ptx_exp2(m - mx);  // 0 while m = -inf
         l *= f;
         m = mx;
       }
-      // P_t (fp16 pairs) goes over columns 0-63 of S_t, whose values are all in
-      // registers.  The PV MMA of key tile j-1 read the previous P_t there before
-      // S_t(j) overwrote it: MMAs complete in issue order.
+      // P_t (fp16 pairs) goes over columns 0-63 of S_t: half hf is written to
+      // columns 32*hf.., inside the columns already read.  The PV MMA of key
+      // tile j-1 read the previous P_t there before S_t(j) overwrote it: MMAs
+      // complete in issue order.
       const uint32_t tP = tS(t) + trow;
-      // exponent arguments and row sums as packed fp32 pairs: (s * log2 e - m) for
-      // two keys per instruction, 4 independent pair partial sums
       // while no key of the row has been visible (m = -inf), every score is -inf and P is 0
       const float nm = (m == -INFINITY) ? 0.f : -m;
       const uint64_t l2e2 = f2_pack(kLog2e, kLog2e), nm2 = f2_pack(nm, nm);
-      uint64_t ps[4] = {0ull, 0ull, 0ull, 0ull};
+      uint64_t ps[4] = {0ull, 0ull, 0ull, 0ull};  // 4 independent pair partial sums
 #pragma unroll
       for (int hf = 0; hf < 2; ++hf) {
         uint32_t w[32];
 #pragma unroll
-        for (int q = 0; q < 32; ++q) {
-          const int c = hf * 64 + 2 * q;
-          float x0, x1;
-          f2_unpack(f2_fma(f2_pack(__uint_as_float(v[c >> 5][c & 31]), __uint_as_float(v[c >> 5][(c & 31) + 1])),
-                           l2e2, nm2), x0, x1);
-          const float e0 = ptx_exp2(x0), e1 = ptx_exp2(x1);
-          ps[q & 3] = f2_add(ps[q & 3], f2_pack(e0, e1));
-          w[q] = pack_h2(e0, e1);
+        for (int sub = 0; sub < 2; ++sub) {  // 32 columns at a time: no register spills
+          uint32_t va[32];
+          tc::ld_32x32b_x32(tS(t) + trow + (uint32_t)(hf * 64 + sub * 32), va);
+          tc::wait_ld();
+          tc::after_wait(va);
+          if (edge) {
+#pragma unroll
+            for (int c = 0; c < 32; ++c)
+              if (k0 + hf * 64 + sub * 32 + c >= lim) va[c] = __float_as_uint(-INFINITY);
+          }
+#pragma unroll
+          for (int q = sub * 16; q < sub * 16 + 16; ++q) {
+            const int c = (2 * q) & 31;
+            float x0, x1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(va[c]), __uint_as_float(va[c + 1])), l2e2, nm2), x0, x1);
+            const float e0 = ptx_exp2(x0), e1 = ptx_exp2(x1);
+            ps[q & 3] = f2_add(ps[q & 3], f2_pack(e0, e1));
+            w[q] = pack_h2(e0, e1);
+          }
         }
         tc::st_32x32b_x32(tP + (uint32_t)(hf * 32), w);
       }
@@ -501,6 +505,25 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
       f2_unpack(f2_add(ps[0], ps[1]), s0, s1);
       f2_unpack(f2_add(ps[2], ps[3]), s2, s3);
       l += (s0 + s1) + (s2 + s3);
+      if (rescale && j > 0) {
+        // O holds tiles 0..j-1 at the old base: once their last PV is done, scale it in
+        // place (before P_t(j) is released, so before PV_t(j) accumulates onto it)
+        if (!wait_rows(&bars[BPV + t], (j - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tc::ld_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
+          tc::wait_ld();
+          tc::after_wait(o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+          tc::st_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
+        }
+      }
       tc::wait_st();
       tc::fence_before();
       ptx::mbar_arrive(&bars[BPF + t]);
