@@ -20,6 +20,7 @@ CQ_ERR_UNSUPPORTED = -2
 CQ_ERR_CUDA = -3
 CQ_ERR_WORKSPACE = -4
 
+CQ_ABI_VERSION = 2  # CQ_ABI_VERSION of include/chronoquant_b200.h
 CQ_F16, CQ_BF16, CQ_F32 = 0, 1, 2
 CQ_ORDER_NATURAL, CQ_ORDER_MMA = 0, 1
 CQ_SCALE_BY_PFRAME, CQ_SCALE_BY_TOKEN = 0, 1

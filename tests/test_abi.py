@@ -39,7 +39,16 @@ def test_binding_covers_header():
 
 
 def test_abi_version():
-    assert _lib.lib().cq_abi_version() == 2
+    assert _lib.lib().cq_abi_version() == _lib.CQ_ABI_VERSION == 2
+    hdr = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
+                            "chronoquant_b200.h")).read()
+    assert "#define CQ_ABI_VERSION 2" in hdr
+
+
+def test_graft_build_entry():
+    """The driver's build check: build() compiles (incrementally) and loads the library."""
+    import __graft_entry__
+    __graft_entry__.build()
 
 
 def _desc(**over):
