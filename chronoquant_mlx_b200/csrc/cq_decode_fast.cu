@@ -695,6 +695,7 @@ __device__ void finish_units(const Params &p, const Len &L, unsigned char *smem)
   __shared__ float s_ML[8][2];         // per head: M, L
   __shared__ int s_glob[kMaxWarps];    // the warp's partial of this unit is in global memory
   __shared__ int s_src[kMaxWarps];     // else: float offset of its on-chip partial
+  __shared__ const float *s_optr[kMaxWarps];  // output rows of the warp's partial (shared or global, generic)
   const int G = p.gqa;
   const int *fin_unit = (const int *)(smem + p.off_fin);
   const int w0 = blockIdx.x * p.nwc;
@@ -725,6 +726,7 @@ __device__ void finish_units(const Params &p, const Len &L, unsigned char *smem)
         src = p.off_strad / 4 + k * kFinFloats;
       s_src[j] = src;
       s_glob[j] = src < 0;
+      s_optr[j] = src >= 0 ? smf + src + 16 : p.ws_o + ((int64_t)wa + j + u) * G * HD;
     }
     __syncthreads();
     // per head: 16 lanes, one per warp (shuffle reductions stay inside each half-warp)
@@ -756,25 +758,45 @@ __device__ void finish_units(const Params &p, const Len &L, unsigned char *smem)
     }
     __syncthreads();
     const int b = u / p.cv.H, h = u - b * p.cv.H;
-    for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
-      const int hh = idx / HD, d = idx - hh * HD;
-      float acc = 0.f;
+    // four lanes per float4 of head dims, each summing a quarter of the warps' partials (one
+    // generic load each, no branch on where the partial lives), combined by shuffles
+    for (int base = 0; base < G * (HD / 4); base += blockDim.x >> 2) {
+      const int item = base + (threadIdx.x >> 2), jq = threadIdx.x & 3;
+      const bool valid = item < G * (HD / 4);
+      const int hh = valid ? item / (HD / 4) : 0, d = valid ? (item - hh * (HD / 4)) * 4 : 0;
+      float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
-      for (int j = 0; j < kMaxWarps; ++j) {  // fixed bound: all loads issue before they are used
-        if (j < nw) {
-          const float o =
-              s_glob[j] ? p.ws_o[(((int64_t)wa + j + u) * G + hh) * HD + d] : smf[s_src[j] + 16 + hh * HD + d];
-          acc += o * s_w[j][hh];
+      for (int r = 0; r < kMaxWarps / 4; ++r) {
+        const int j = jq + 4 * r;
+        if (valid && j < nw) {
+          const float4 o = *reinterpret_cast<const float4 *>(s_optr[j] + hh * HD + d);
+          const float w = s_w[j][hh];
+          acc.x = fmaf(o.x, w, acc.x);
+          acc.y = fmaf(o.y, w, acc.y);
+          acc.z = fmaf(o.z, w, acc.z);
+          acc.w = fmaf(o.w, w, acc.w);
         }
       }
+#pragma unroll
+      for (int x = 1; x < 4; x <<= 1) {
+        acc.x += __shfl_xor_sync(0xffffffffu, acc.x, x);
+        acc.y += __shfl_xor_sync(0xffffffffu, acc.y, x);
+        acc.z += __shfl_xor_sync(0xffffffffu, acc.z, x);
+        acc.w += __shfl_xor_sync(0xffffffffu, acc.w, x);
+      }
+      if (!valid || jq != 0) continue;
       const float M = s_ML[hh][0], L = s_ML[hh][1];
       if (whole) {
         const int64_t row = (int64_t)b * p.Hq + h * G + hh;
-        store_from_float(p.out, row * HD + d, (L > 0.f) ? acc / L : 0.f, p.out_dtype);
+        const float inv = (L > 0.f) ? 1.f / L : 0.f;
+        store_from_float(p.out, row * HD + d, acc.x * inv, p.out_dtype);
+        store_from_float(p.out, row * HD + d + 1, acc.y * inv, p.out_dtype);
+        store_from_float(p.out, row * HD + d + 2, acc.z * inv, p.out_dtype);
+        store_from_float(p.out, row * HD + d + 3, acc.w * inv, p.out_dtype);
         if (p.lse_out && d == 0) p.lse_out[row] = (L > 0.f) ? (M + log2f(L)) * LN2 : -INFINITY;
       } else {
         const int64_t cs = ((int64_t)blockIdx.x + u) * G + hh;
-        p.cs_o[cs * HD + d] = acc;
+        *reinterpret_cast<float4 *>(p.cs_o + cs * HD + d) = acc;
         if (d == 0) {
           p.cs_m[cs] = M;
           p.cs_l[cs] = L;
@@ -830,37 +852,49 @@ __device__ void finish_units(const Params &p, const Len &L, unsigned char *smem)
       const int c_hi = warp_of(p, L, (int64_t)u * L.cpu + L.cpu - 1) / p.nwc;
       const int b = u / p.cv.H, h = u - b * p.cv.H;
       const int np = c_hi - c_lo + 1;
-      for (int idx = threadIdx.x; idx < G * HD; idx += blockDim.x) {
-        const int hh = idx / HD, d = idx - hh * HD;
+      for (int idx = threadIdx.x; idx < G * (HD / 4); idx += blockDim.x) {
+        const int hh = idx / (HD / 4), d = (idx - hh * (HD / 4)) * 4;
         const int64_t i0 = ((int64_t)c_lo + u) * G + hh;
-        float M = -INFINITY, L = 0.f, acc = 0.f;
-        // all loads of up to 4 partials issued together, then merged
+        float M = -INFINITY, L = 0.f;
+        float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
+        // all loads of up to 4 partials issued together, then merged (one float4 of dims per thread)
         for (int j0 = 0; j0 < np; j0 += 4) {
-          float m[4], l[4], o[4];
+          float m[4], l[4];
+          float4 o[4];
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const bool ok = j0 + j < np;
             const int64_t i = i0 + (int64_t)(j0 + j) * G;
             m[j] = ok ? __ldcg(p.cs_m + i) : -INFINITY;
             l[j] = ok ? __ldcg(p.cs_l + i) : 0.f;
-            o[j] = ok ? __ldcg(p.cs_o + i * HD + d) : 0.f;
+            o[j] = ok ? __ldcg(reinterpret_cast<const float4 *>(p.cs_o + i * HD + d)) : make_float4(0.f, 0.f, 0.f, 0.f);
           }
           float Mn = M;
 #pragma unroll
           for (int j = 0; j < 4; ++j) Mn = fmaxf(Mn, m[j]);
           const float fo = (M == -INFINITY) ? 0.f : fast_exp2(M - Mn);
           L *= fo;
-          acc *= fo;
+          acc.x *= fo;
+          acc.y *= fo;
+          acc.z *= fo;
+          acc.w *= fo;
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const float f = (m[j] == -INFINITY) ? 0.f : fast_exp2(m[j] - Mn);
             L += l[j] * f;
-            acc += o[j] * f;
+            acc.x = fmaf(o[j].x, f, acc.x);
+            acc.y = fmaf(o[j].y, f, acc.y);
+            acc.z = fmaf(o[j].z, f, acc.z);
+            acc.w = fmaf(o[j].w, f, acc.w);
           }
           M = Mn;
         }
         const int64_t row = (int64_t)b * p.Hq + h * G + hh;
-        store_from_float(p.out, row * HD + d, (L > 0.f) ? acc / L : 0.f, p.out_dtype);
+        const float inv = (L > 0.f) ? 1.f / L : 0.f;
+        store_from_float(p.out, row * HD + d, acc.x * inv, p.out_dtype);
+        store_from_float(p.out, row * HD + d + 1, acc.y * inv, p.out_dtype);
+        store_from_float(p.out, row * HD + d + 2, acc.z * inv, p.out_dtype);
+        store_from_float(p.out, row * HD + d + 3, acc.w * inv, p.out_dtype);
         if (p.lse_out && d == 0) p.lse_out[row] = (L > 0.f) ? (M + log2f(L)) * LN2 : -INFINITY;
       }
     }
@@ -998,6 +1032,7 @@ static bool make_layout(const cq_paged_cache &c, Layout &L) {
   L.off_fin = kMaxWarps * 4 * 8;  // after the mbarriers [warp][slot]: each warp's last unit
   L.off_strad = up128(L.off_fin + kMaxWarps * 4);
   L.off_warp = up128(L.off_strad + kStrad * kFinFloats * 4);
+  if (L.warp_bytes & 15) return false;  // on-chip partials are read as float4
   L.nwc = std::min(kMaxWarps, (kMaxSmem - L.off_warp) / L.warp_bytes);
   L.total = L.off_warp + L.nwc * L.warp_bytes;
   return L.nwc >= 4;
@@ -1095,13 +1130,15 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
   const size_t cslots = (size_t)(pl.grid + pl.units) * p.gqa;   // CTA partials
   const size_t need = (slots + cslots) * (2 + HD) * sizeof(float) + (size_t)pl.units * sizeof(unsigned long long);
   CQ_REQUIRE(ws && ws_bytes >= need, CQ_ERR_WORKSPACE, "cq_attention: workspace too small");
-  p.ws_m = (float *)ws;
+  CQ_REQUIRE(((uintptr_t)ws & 15) == 0, CQ_ERR_INVALID, "cq_attention: workspace must be 16-byte aligned");
+  // output partials first: their rows stay 16-byte aligned for vector loads
+  p.ws_o = (float *)ws;
+  p.cs_o = p.ws_o + slots * HD;
+  p.ws_m = p.cs_o + cslots * HD;
   p.ws_l = p.ws_m + slots;
-  p.ws_o = p.ws_l + slots;
-  p.cs_m = p.ws_o + slots * HD;
+  p.cs_m = p.ws_l + slots;
   p.cs_l = p.cs_m + cslots;
-  p.cs_o = p.cs_l + cslots;
-  p.done = (unsigned long long *)(p.cs_o + cslots * HD);  // 8-byte aligned: (2 + HD) * 4 bytes per slot
+  p.done = (unsigned long long *)(p.cs_l + cslots);  // 8-byte aligned: 2 * (slots + cslots) floats precede it
   static std::atomic<unsigned long long> calls{0};
   p.stamp = (++calls) & 0xffffffffffffull;
   if (!p.stamp) p.stamp = (++calls) & 0xffffffffffffull;
