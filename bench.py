@@ -739,10 +739,14 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--page-tokens", type=int, default=None, help="cache page size (default: the cache's choice)")
     ap.add_argument("--cpu-rows", type=int, default=128, help="config 4 CPU sample: query rows per kv-head")
+    ap.add_argument("--context", type=int, default=None,
+                    help="config 4: cached tokens before the chunk (default 65536; smaller for profiler captures)")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     cfg = CONFIGS[args.config]
+    if args.config == 4 and args.context is not None:
+        cfg = dict(cfg, T=args.context, name=f"{cfg['name']}-ctx{args.context}")
     if args.config == 4:
         if args.impl == "reference":
             run_reference_prefill(args, cfg)
