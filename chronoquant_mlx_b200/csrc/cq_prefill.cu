@@ -429,33 +429,28 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
       tc::fence_after();
       const int64_t k0 = (int64_t)(j0 + j) * kTile;
       const bool edge = k0 + kTile > lim;  // causal edge or keys past T
-      // Two passes over S_t so that only part of a row is live in registers:
-      // the row max (64 columns per load pair), then the exponentials.
-      auto load_half = [&](int hf, uint32_t (&va)[32], uint32_t (&vb)[32]) {
-        tc::ld_32x32b_x32(tS(t) + trow + (uint32_t)(hf * 64), va);
-        tc::ld_32x32b_x32(tS(t) + trow + (uint32_t)(hf * 64 + 32), vb);
-        tc::wait_ld();
-        tc::after_wait(va);
-        tc::after_wait(vb);
-        if (edge) {
-#pragma unroll
-          for (int c = 0; c < 32; ++c) {
-            if (k0 + hf * 64 + c >= lim) va[c] = __float_as_uint(-INFINITY);
-            if (k0 + hf * 64 + 32 + c >= lim) vb[c] = __float_as_uint(-INFINITY);
-          }
-        }
-      };
+      // Two passes over S_t: the row max (all 128 columns in one tensor-memory round
+      // trip), then the exponentials 32 columns at a time (registers for P stay free).
       // row max as a tree over 8 independent partial maxima (one thread owns the row)
       float pm[8];
 #pragma unroll
       for (int u = 0; u < 8; ++u) pm[u] = -INFINITY;
+      {  // the whole row in one tensor-memory round trip (its registers are free again for pass 2)
+        uint32_t v4[4][32];
 #pragma unroll
-      for (int hf = 0; hf < 2; ++hf) {
-        uint32_t va[32], vb[32];
-        load_half(hf, va, vb);
+        for (int c = 0; c < 4; ++c) tc::ld_32x32b_x32(tS(t) + trow + (uint32_t)(c * 32), v4[c]);
+        tc::wait_ld();
 #pragma unroll
-        for (int c = 0; c < 32; ++c)
-          pm[c & 7] = fmaxf(pm[c & 7], fmaxf(__uint_as_float(va[c]), __uint_as_float(vb[c])));
+        for (int c = 0; c < 4; ++c) tc::after_wait(v4[c]);
+        if (edge) {
+#pragma unroll
+          for (int c = 0; c < 128; ++c)
+            if (k0 + c >= lim) v4[c >> 5][c & 31] = __float_as_uint(-INFINITY);
+        }
+#pragma unroll
+        for (int c = 0; c < 64; ++c)
+          pm[c & 7] = fmaxf(pm[c & 7], fmaxf(__uint_as_float(v4[c >> 5][c & 31]),
+                                             __uint_as_float(v4[(c + 64) >> 5][(c + 64) & 31])));
       }
       const float mx = fmaxf(fmaxf(fmaxf(pm[0], pm[1]), fmaxf(pm[2], pm[3])),
                              fmaxf(fmaxf(pm[4], pm[5]), fmaxf(pm[6], pm[7]))) * kLog2e;
