@@ -231,7 +231,8 @@ enum {
   BEMPTY = BFULL + kRing,  // [kRing] ring slot free (every MMA reading it done)
   BSF = BEMPTY + kRing,  // [2] S of query tile t ready in tensor memory
   BPF = BSF + 2,         // [2] P of query tile t written (over S_t) by its 128 softmax threads
-  BPV = BPF + 2,         // [2] PV MMA of query tile t done (O_t stable)
+  BPH = BPF + 2,         // [2] the first half of P_t (keys 0-63) written, O_t rescaled if needed
+  BPV = BPH + 2,         // [2] PV MMA of query tile t done (O_t stable)
   BDR = BPV + 2,         // drain: every MMA of the CTA done
   NBARS = BDR + 1
 };
@@ -316,7 +317,7 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
   auto full_parity = [](int L) { return (uint32_t)((L / kRing) & 1); };
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < NBARS; ++i) ptx::mbar_init(&bars[i], (i == BPF || i == BPF + 1) ? 128u : 1u);
+    for (int i = 0; i < NBARS; ++i) ptx::mbar_init(&bars[i], (i >= BPF && i < BPF + 4) ? 128u : 1u);
     *abort_flag = 0;
     ptx::fence_mbar_init();
   }
@@ -366,9 +367,9 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
           tc::mma_f16_ss(tS(t), tc::desc_sw128(sQ(t) + ko), tc::desc_sw128(sR(L) + ko), idesc, k > 0 ? 1u : 0u);
         }
       };
-      auto mma_pv = [&](int t, int j, int L) {  // P_t from tensor memory (columns 0-63 of S_t)
+      auto mma_pv = [&](int t, int j, int L, int half) {  // P_t from tensor memory (columns 0-63 of S_t)
 #pragma unroll
-        for (int k = 0; k < 8; ++k) {
+        for (int k = 4 * half; k < 4 * half + 4; ++k) {
           const uint32_t ko = (uint32_t)(k >> 2) * kHalfBytes + (uint32_t)(k & 3) * 32;
           tc::mma_f16_ts(tO(t), tS(t) + (uint32_t)k * 8, tc::desc_sw128(sR(L) + ko), idesc,
                          (j > 0 || k > 0) ? 1u : 0u);
@@ -386,9 +387,13 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
       for (int j = 0; ok && j < n; ++j) {
         const int Lv = 2 * j + 1, Lk = 2 * j + 2;
         const bool more = j + 1 < n;
-        if (!wait_bar(&bars[BPF + 0], j & 1, abort_flag) || !landed(Lv)) break;
+        // each PV in two halves of its keys: the first as soon as that half of P is written
+        if (!wait_bar(&bars[BPH + 0], j & 1, abort_flag) || !landed(Lv)) break;
         tc::fence_after();
-        mma_pv(0, j, Lv);
+        mma_pv(0, j, Lv, 0);
+        if (!wait_bar(&bars[BPF + 0], j & 1, abort_flag)) break;
+        tc::fence_after();
+        mma_pv(0, j, Lv, 1);
         tc::commit(&bars[BPV + 0]);
         if (more) {
           if (!landed(Lk)) break;
@@ -396,9 +401,12 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
           mma_s(0, Lk);
           tc::commit(&bars[BSF + 0]);
         }
+        if (!wait_bar(&bars[BPH + 1], j & 1, abort_flag)) break;
+        tc::fence_after();
+        mma_pv(1, j, Lv, 0);
         if (!wait_bar(&bars[BPF + 1], j & 1, abort_flag)) break;
         tc::fence_after();
-        mma_pv(1, j, Lv);
+        mma_pv(1, j, Lv, 1);
         tc::commit(&bars[BPV + 1]);
         tc::commit(&bars[BEMPTY + Lv % kRing]);
         if (more) {
@@ -461,10 +469,30 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
         l *= f;
         m = mx;
       }
+      if (rescale && j > 0) {
+        // O holds tiles 0..j-1 at the old base: once their last PV is done, scale it in
+        // place (before the first half of P_t(j) is released, so before PV_t(j) starts)
+        if (!wait_rows(&bars[BPV + t], (j - 1) & 1, abort_flag)) {
+          ok = false;
+          break;
+        }
+        tc::fence_after();
+#pragma unroll 1
+        for (int c = 0; c < 4; ++c) {
+          uint32_t o[32];
+          tc::ld_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
+          tc::wait_ld();
+          tc::after_wait(o);
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
+          tc::st_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
+        }
+      }
       // P_t (fp16 pairs) goes over columns 0-63 of S_t: half hf is written to
-      // columns 32*hf.., inside the columns already read.  The PV MMA of key
-      // tile j-1 read the previous P_t there before S_t(j) overwrote it: MMAs
-      // complete in issue order.
+      // columns 32*hf.., inside the columns already read, and released on its own
+      // (BPH, then BPF) so that the first half of PV_t(j) runs while the second
+      // half of P is computed.  The PV MMA of key tile j-1 read the previous P_t
+      // there before S_t(j) overwrote it: MMAs complete in issue order.
       const uint32_t tP = tS(t) + trow;
       // while no key of the row has been visible (m = -inf), every score is -inf and P is 0
       const float nm = (m == -INFINITY) ? 0.f : -m;
@@ -495,33 +523,14 @@ __global__ void __launch_bounds__(kThreads, 1) attn_kernel(AttnParams p) {
           }
         }
         tc::st_32x32b_x32(tP + (uint32_t)(hf * 32), w);
+        tc::wait_st();
+        tc::fence_before();
+        ptx::mbar_arrive(&bars[(hf == 0 ? BPH : BPF) + t]);
       }
       float s0, s1, s2, s3;
       f2_unpack(f2_add(ps[0], ps[1]), s0, s1);
       f2_unpack(f2_add(ps[2], ps[3]), s2, s3);
       l += (s0 + s1) + (s2 + s3);
-      if (rescale && j > 0) {
-        // O holds tiles 0..j-1 at the old base: once their last PV is done, scale it in
-        // place (before P_t(j) is released, so before PV_t(j) accumulates onto it)
-        if (!wait_rows(&bars[BPV + t], (j - 1) & 1, abort_flag)) {
-          ok = false;
-          break;
-        }
-        tc::fence_after();
-#pragma unroll 1
-        for (int c = 0; c < 4; ++c) {
-          uint32_t o[32];
-          tc::ld_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
-          tc::wait_ld();
-          tc::after_wait(o);
-#pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * f);
-          tc::st_32x32b_x32(tO(t) + trow + (uint32_t)(c * 32), o);
-        }
-      }
-      tc::wait_st();
-      tc::fence_before();
-      ptx::mbar_arrive(&bars[BPF + t]);
     }
     // ---------------------------------------------------------------- epilogue
     const bool live = tok < p.q_len;
