@@ -25,7 +25,7 @@
 //                   rescale of O; P as fp16 into tensor memory over its own
 //                   S columns, read there by the PV MMA;
 //        warp 8     copies: one bulk copy per 32 KB tile image into a 5-slot
-//                   K/V ring (no multicast);
+//                   K/V ring (each CTA loads its own tiles);
 //        warp 9     MMA issue (one thread) and tensor-memory allocation.
 //      The MMAs alternate between the tiles (PV_a, S_a, PV_b, S_b per key
 //      tile), so one tile's softmax runs while the tensor core works for the

@@ -75,3 +75,28 @@ def failing_worker(rank, world, port, queue):
         queue.put((rank, "no error"))
     except Exception as e:
         queue.put((rank, "error: " + type(e).__name__))
+
+
+def nccl_worker(rank, world, port, K, V, q, stride_k, stride_v, queue):
+    """One GPU per rank: encode this rank's shard with the CUDA path, run
+    sequence_parallel_attention (NCCL all-gather over NVLink + cq_lse_merge)."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=60),
+                                device_id=torch.device("cuda", rank))
+        from chronoquant_mlx_b200 import ChronoQuantCache
+        from chronoquant_mlx_b200.distributed import sequence_parallel_attention, shard_bounds
+        lo, hi = shard_bounds(K.shape[2], world, stride_k, stride_v)[rank]
+        c = ChronoQuantCache(stride_k=stride_k, stride_v=stride_v)
+        dev = torch.device("cuda", rank)
+        c.update_and_fetch(torch.from_numpy(K[:, :, lo:hi]).to(dev), torch.from_numpy(V[:, :, lo:hi]).to(dev))
+        out = sequence_parallel_attention(torch.from_numpy(q).to(dev), c, 1 / math.sqrt(q.shape[-1]))
+        torch.cuda.synchronize()
+        queue.put((rank, out.float().cpu().numpy(), None))
+        dist.barrier()
+        dist.destroy_process_group()
+    except Exception as e:
+        queue.put((rank, None, repr(e)))

@@ -141,3 +141,28 @@ def test_shard_partials_merge_on_gpu(q_len):
     ref = O.exact_sdpa(qs, k32, v32, causal=True)
     err = np.abs(out.cpu().numpy() - ref)
     assert (err <= 2e-3 + 1e-2 * np.abs(ref)).all(), err.max()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("q_len", [1, 64])
+def test_nccl_sequence_split_two_gpus(q_len):
+    """Two ranks on two GPUs: each holds half the sequence, the partials cross
+    NVLink in one NCCL all-gather, and every rank's merged output matches
+    exact attention over the whole sequence."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    B, Hkv, Hq, T, sk, sv = 2, 2, 8, 2048, 32, 8
+    K, V = O.ar1_kv(B, Hkv, T, 128, seed=31)
+    q = (np.random.default_rng(4).standard_normal((B, Hq, q_len, 128)) / math.sqrt(128)).astype(np.float16)
+    port = _free_port()
+    res, codes = _run(W.nccl_worker, lambda r: (r, 2, port, K, V, q, sk, sv), 2, timeout=180)
+    full = O.OracleCache(stride_k=sk, stride_v=sv)
+    full.update_and_fetch(K, V)
+    k32, v32 = full.reconstruct_history_f32()
+    qs = (q.astype(np.float64) * float(np.float16(1 / math.sqrt(128)))).astype(np.float16)
+    ref = O.exact_sdpa(qs, k32, v32, causal=True)
+    for rank, out, err in res:
+        assert err is None, err
+        e = np.abs(out - ref)
+        assert (e <= 2e-3 + 1e-2 * np.abs(ref)).all(), (rank, e.max())
+    assert codes == [0, 0]
