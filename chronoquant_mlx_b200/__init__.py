@@ -17,6 +17,7 @@ from .patch import (
 )
 from .attention import chronoquant_sdpa
 from .graph import DecodeGraph
+from .prompt_cache import load_prompt_cache, save_prompt_cache
 
 __all__ = [
     "ChronoQuantCache",
@@ -27,4 +28,6 @@ __all__ = [
     "create_full_throttle_caches",
     "chronoquant_sdpa",
     "DecodeGraph",
+    "save_prompt_cache",
+    "load_prompt_cache",
 ]

@@ -439,13 +439,45 @@ class ChronoQuantCache:
                                                   stream_ptr(kfc.device)), "state")
         self.offset = T
 
+    # The reference's meta_state is "" (cache.py:257-263): a restored cache takes
+    # its strides and bits from its constructor.  Here meta_state also carries
+    # the configuration, as strings (the prompt-cache file convention), so a
+    # saved cache restores self-described; "" is still accepted.
+    _META_TAG = "chronoquant/1"
+    _META_KEYS = ("stride_k", "stride_v", "delta_bits_k", "delta_bits_v", "dead_zone_k", "dead_zone_v",
+                  "use_fused", "per_layer_v_bits", "layer_idx", "page_tokens")
+
     @property
     def meta_state(self):
-        return ""
+        vals = [self.stride_k, self.stride_v, self.delta_bits_k, self.delta_bits_v, repr(float(self.dead_zone_k)),
+                repr(float(self.dead_zone_v)), int(bool(self.use_fused)),
+                ",".join(str(int(b)) for b in self.per_layer_v_bits), self.layer_idx, self.page_tokens]
+        return (self._META_TAG,) + tuple(f"{k}={v}" for k, v in zip(self._META_KEYS, vals))
 
     @meta_state.setter
     def meta_state(self, value):
-        pass
+        """Reconfigure an empty cache from ``meta_state`` (set it before
+        ``state``).  "" or an empty tuple leaves the configuration as built."""
+        if not value:
+            return
+        if isinstance(value, str):
+            value = (value,)
+        if value[0] != self._META_TAG:
+            raise ValueError(f"unknown meta_state {value[0]!r}")
+        if self.offset != 0 or self._store is not None:
+            raise ValueError("meta_state can only configure an empty cache")
+        kv = dict(item.split("=", 1) for item in value[1:])
+        unknown = set(kv) - set(self._META_KEYS)
+        if unknown:
+            raise ValueError(f"unknown meta_state keys {sorted(unknown)}")
+        bits_v = kv.get("per_layer_v_bits", "")
+        self.__init__(stride_k=int(kv["stride_k"]), stride_v=int(kv["stride_v"]),
+                      delta_bits_k=int(kv["delta_bits_k"]), delta_bits_v=int(kv["delta_bits_v"]),
+                      dead_zone_k=float(kv["dead_zone_k"]), dead_zone_v=float(kv["dead_zone_v"]),
+                      use_fused=bool(int(kv["use_fused"])),
+                      per_layer_v_bits=[int(b) for b in bits_v.split(",")] if bits_v else None,
+                      layer_idx=int(kv["layer_idx"]), page_tokens=int(kv["page_tokens"]), max_tokens=self.max_tokens)
+        self._codec_v = None  # V bits may have changed
 
     def is_trimmable(self):
         return False

