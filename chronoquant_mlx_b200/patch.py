@@ -53,6 +53,12 @@ def apply_patch():
     for module in _targets():
         module.scaled_dot_product_attention = _patched_sdpa
     _patched = True
+    # transformers models select attention by name: register "chronoquant" when it is installed
+    try:
+        from . import hf
+        hf.register()
+    except ImportError:
+        pass
     log.info("ChronoQuant SDPA patch applied to all loaded model modules.")
 
 
