@@ -329,6 +329,8 @@ def run_ours(args, cfg):
     h2d = hin[0].numel()
     d2h = hout.numel() * 2
 
+    fp16_base = fp16_decode_baseline(cfg, cache.offset, device, reps) if world == 1 else None
+
     peak, peak_kind = load_peak()
     achieved = mean_attn_bytes / (mean_attn_ms * 1e-3) / 1e9
     traffic = None
@@ -369,6 +371,10 @@ def run_ours(args, cfg):
                          "launch_ms": round(mean_attn_ms, 5), "launch_timing": "graph replays back to back"},
             "clocks": clk.summary(),
             "gpu_launches": args.steps,  # one fused encode+decode kernel per graph replay
+            "fp16_baseline": None if fp16_base is None else dict(
+                fp16_base, compressed_bytes_per_token_kv_head=round(
+                    active_bytes(1, 1, cache.offset, D, cfg["stride_k"], cfg["stride_v"]) / cache.offset, 2),
+                speedup_of_compressed_kernel=round(fp16_base["ms_per_step"] / mean_attn_ms, 3)),
         }
         if not args.no_cpu_baseline and world == 1:
             res["cpu_baseline"] = cpu_baseline(cfg, budget_s=args.cpu_budget)
@@ -616,6 +622,47 @@ def run_reference_prefill(args, cfg):
         "e2e": {"value": round(value, 6), "unit": "TFLOP/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out))
+
+
+def fp16_decode_baseline(cfg, T, device, reps):
+    """Decode attention of the same shape over an uncompressed fp16 cache (the
+    FlashDecoding baseline of BASELINE config 3): flash_attn_with_kvcache when
+    it runs on this GPU, else torch SDPA with GQA.  Times `reps` calls back to
+    back with CUDA events; reports bytes per token and kv-head (K+V) and the
+    fp16 cache read rate."""
+    import torch
+    import torch.nn.functional as F
+    B, H, Hq, D = cfg["B"], cfg["Hkv"], cfg["Hq"], cfg["D"]
+    g = torch.Generator(device=device).manual_seed(5)
+    k = torch.randn((B, T, H, D), generator=g, device=device, dtype=torch.float16)
+    v = torch.randn((B, T, H, D), generator=g, device=device, dtype=torch.float16)
+    q = (torch.randn((B, 1, Hq, D), generator=g, device=device) / math.sqrt(D)).to(torch.float16)
+    impl, fn = None, None
+    try:
+        from flash_attn import flash_attn_with_kvcache
+        flash_attn_with_kvcache(q, k, v, causal=False)
+        torch.cuda.synchronize()
+        impl, fn = "flash_attn_with_kvcache (flash-attn 2)", lambda: flash_attn_with_kvcache(q, k, v, causal=False)
+    except Exception as e:  # not built for this GPU
+        torch.cuda.synchronize()
+        note = f"flash_attn unavailable ({type(e).__name__})"
+        kt, vt, qt = k.transpose(1, 2), v.transpose(1, 2), q.transpose(1, 2)
+        impl = f"torch SDPA, enable_gqa ({note})"
+        fn = lambda: F.scaled_dot_product_attention(qt, kt, vt, enable_gqa=True)
+    for _ in range(3):
+        fn()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(reps):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    ms = e0.elapsed_time(e1) / reps
+    fp16_bytes = 2 * B * H * T * D * 2
+    del k, v
+    return {"impl": impl, "ms_per_step": round(ms, 5), "fp16_bytes_per_token_kv_head": 2 * D * 2,
+            "fp16_cache_gbs": round(fp16_bytes / (ms * 1e-3) / 1e9, 1), "tokens": T}
 
 
 # ----------------------------------------------------------------------------- CPU reference arm
