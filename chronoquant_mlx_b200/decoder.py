@@ -1,0 +1,218 @@
+"""A random-init Qwen3-style decoder that drives the compressed cache end to
+end: greedy decode where every step is one CUDA-graph replay.
+
+BASELINE config 5 asks for "decode tokens/s at 32k ctx" on a decoder of the
+Qwen3-8B shape (36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128,
+SwiGLU 12288, vocab 151936, RMSNorm, RoPE theta 1e6, bf16 weights N(0, 0.02))
+with Full-Throttle V3 caches.  The reference reaches this through mlx_lm
+models calling its patched SDPA (patch.py:12-43); here one module holds the
+whole step so that it can be captured:
+
+    per layer: RMSNorm -> fused QKV projection -> per-head q/k RMSNorm -> RoPE
+               -> cq_decode_step_at (encode the token into the layer's cache,
+                  attend over everything cached: one kernel)
+               -> o_proj + residual -> RMSNorm -> SwiGLU FFN + residual
+    then: final RMSNorm -> lm_head -> argmax, fed back as the next input ids.
+
+The GEMMs are cuBLAS (torch.matmul); norms, RoPE and SwiGLU are torch
+elementwise ops; attention is this package's kernel.  Every layer's cache
+length lives on the device and advances inside the kernel, the RoPE position
+is a device counter, and the sampled ids are written back in-graph, so a
+replay needs no host synchronisation.
+
+``fill_context`` writes a synthetic context (seeded random K/V per layer,
+encoded by the cache's own append kernel) instead of running a 32k-token
+prompt through the model; a decode step's cost does not depend on the
+values.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+
+import torch
+
+from . import _lib
+from ._tensors import cq_dtype, stream_ptr
+from .cache import ChronoQuantCache
+
+
+@dataclass
+class DecoderConfig:
+    layers: int = 36
+    hidden: int = 4096
+    heads: int = 32
+    kv_heads: int = 8
+    head_dim: int = 128
+    ffn: int = 12288
+    vocab: int = 151936
+    rope_theta: float = 1.0e6
+    eps: float = 1.0e-6
+
+
+def _rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    xf = x.float()
+    return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * w
+
+
+def _rope(x: torch.Tensor, cos: torch.Tensor, sin: torch.Tensor) -> torch.Tensor:
+    """Rotate-half RoPE of x [B, H, D] at one position (cos/sin [D])."""
+    h = x.shape[-1] // 2
+    rot = torch.cat((-x[..., h:], x[..., :h]), dim=-1)
+    return (x.float() * cos + rot.float() * sin).to(x.dtype)
+
+
+class Qwen3StyleDecoder:
+    """Random-init weights, one ChronoQuantCache per layer, and a graph-captured
+    greedy decode step for ``batch`` sequences of up to ``max_len`` tokens."""
+
+    def __init__(self, cfg: DecoderConfig, batch: int, max_len: int, cache_kwargs: dict | None = None,
+                 device="cuda", dtype=torch.bfloat16, seed: int = 0):
+        self.cfg, self.B, self.max_len = cfg, batch, max_len
+        self.device, self.dtype = torch.device(device), dtype
+        g = torch.Generator(device=self.device).manual_seed(seed)
+
+        def w(*shape):
+            return (torch.randn(shape, generator=g, device=self.device, dtype=torch.float32) * 0.02).to(dtype)
+
+        c = cfg
+        qkv = (c.heads + 2 * c.kv_heads) * c.head_dim
+        self.embed = w(c.vocab, c.hidden)
+        self.lm_head = w(c.vocab, c.hidden)
+        self.final_norm = torch.ones(c.hidden, device=self.device, dtype=dtype)
+        self.layers = []
+        for i in range(c.layers):
+            self.layers.append(dict(
+                ln1=torch.ones(c.hidden, device=self.device, dtype=dtype),
+                ln2=torch.ones(c.hidden, device=self.device, dtype=dtype),
+                q_norm=torch.ones(c.head_dim, device=self.device, dtype=dtype),
+                k_norm=torch.ones(c.head_dim, device=self.device, dtype=dtype),
+                wqkv=w(qkv, c.hidden), wo=w(c.hidden, c.heads * c.head_dim),
+                wgu=w(2 * c.ffn, c.hidden), wdown=w(c.hidden, c.ffn),
+                cache=ChronoQuantCache(layer_idx=i, max_tokens=max_len, **(cache_kwargs or {})),
+            ))
+        self.inv_freq = 1.0 / (c.rope_theta ** (torch.arange(0, c.head_dim, 2, device=self.device,
+                                                             dtype=torch.float32) / c.head_dim))
+        self.ids = torch.zeros(batch, dtype=torch.long, device=self.device)  # input ids of the next step
+        self.pos = torch.zeros((), dtype=torch.long, device=self.device)   # their position
+        self.out_ids = torch.zeros(batch, dtype=torch.long, device=self.device)
+        self.graph = None
+
+    # -- context ---------------------------------------------------------------
+    def fill_context(self, T0: int, chunk: int = 4096, seed: int = 1) -> None:
+        """Encode a synthetic T0-token context into every layer's cache."""
+        c = self.cfg
+        g = torch.Generator(device=self.device).manual_seed(seed)
+        for L in self.layers:
+            for t in range(0, T0, chunk):
+                n = min(chunk, T0 - t)
+                k = torch.randn((self.B, c.kv_heads, n, c.head_dim), generator=g, device=self.device).to(self.dtype)
+                v = torch.randn((self.B, c.kv_heads, n, c.head_dim), generator=g, device=self.device).to(self.dtype)
+                L["cache"].update_and_fetch(k, v)
+        self.pos.fill_(T0)
+        self._prepare_attention()
+
+    def _prepare_attention(self) -> None:
+        """Per-layer descriptors, device-resident lengths and one shared
+        workspace (layers run in order on one stream)."""
+        lib = _lib.lib()
+        need_max = 0
+        for L in self.layers:
+            st = L["cache"].store
+            st.ensure(self.max_len, self.max_len)
+            L["desc"] = st.descriptor()
+            L["len"] = torch.tensor([L["cache"].offset, 0], dtype=torch.int64, device=self.device)
+            need = ctypes.c_size_t(0)
+            _lib.check(lib.cq_attention_workspace(ctypes.byref(L["desc"]), self.max_len, self.cfg.heads, 1, 0,
+                                                  ctypes.byref(need)), "decoder")
+            need_max = max(need_max, need.value)
+        self.workspace = torch.zeros(max(1, (need_max + 3) // 4), dtype=torch.float32, device=self.device)
+        self.attn_out = torch.empty((self.B, self.cfg.heads, self.cfg.head_dim), dtype=self.dtype,
+                                    device=self.device)
+
+    # -- one decode step --------------------------------------------------------
+    def _attention(self, L: dict, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
+        """Encode this step's k/v [B, Hkv, D] into the layer's cache and attend
+        q [B, Hq, D] over everything cached: one cq_decode_step_at launch."""
+        ks, vs, qs = k.stride(), v.stride(), q.stride()
+        _lib.check(_lib.lib().cq_decode_step_at(
+            ctypes.byref(L["desc"]), k.data_ptr(), ks[0], ks[1], v.data_ptr(), vs[0], vs[1], cq_dtype(k),
+            L["len"].data_ptr(), self.max_len, q.data_ptr(), cq_dtype(q), self.cfg.heads, qs[0], qs[1],
+            1.0 / math.sqrt(self.cfg.head_dim), self.attn_out.data_ptr(), cq_dtype(self.attn_out), None,
+            self.workspace.data_ptr(), self.workspace.numel() * 4, stream_ptr(self.device)), "decoder")
+        return self.attn_out
+
+    def _step_body(self, attention=None) -> torch.Tensor:
+        c, B = self.cfg, self.B
+        attention = attention or self._attention
+        nq, nk = c.heads * c.head_dim, c.kv_heads * c.head_dim
+        x = self.embed[self.ids]
+        ang = self.pos.float() * self.inv_freq
+        cos = torch.cat((ang.cos(), ang.cos()))
+        sin = torch.cat((ang.sin(), ang.sin()))
+        for L in self.layers:
+            qkv = _rmsnorm(x, L["ln1"], c.eps) @ L["wqkv"].t()
+            q = _rope(_rmsnorm(qkv[:, :nq].view(B, c.heads, c.head_dim), L["q_norm"], c.eps), cos, sin)
+            k = _rope(_rmsnorm(qkv[:, nq:nq + nk].view(B, c.kv_heads, c.head_dim), L["k_norm"], c.eps), cos, sin)
+            v = qkv[:, nq + nk:].reshape(B, c.kv_heads, c.head_dim)
+            a = attention(L, q.contiguous(), k.contiguous(), v.contiguous())
+            x = x + a.reshape(B, nq) @ L["wo"].t()
+            gu = _rmsnorm(x, L["ln2"], c.eps) @ L["wgu"].t()
+            x = x + (torch.nn.functional.silu(gu[:, :c.ffn]) * gu[:, c.ffn:]) @ L["wdown"].t()
+        logits = _rmsnorm(x, self.final_norm, c.eps) @ self.lm_head.t()
+        self.out_ids.copy_(logits.argmax(-1))
+        self.ids.copy_(self.out_ids)
+        self.pos.add_(1)
+        return logits
+
+    def step_eager(self, attention=None) -> torch.Tensor:
+        """One decode step without a graph (``attention(L, q, k, v)`` may
+        replace the kernel, e.g. by a reference).  Returns logits [B, vocab]."""
+        return self._step_body(attention)
+
+    def capture(self) -> None:
+        """Capture one decode step as a CUDA graph (after ``fill_context``)."""
+        lib = _lib.lib()
+        c = self.cfg
+        # one-time set-up outside the capture: cuBLAS handles (one matmul of each
+        # shape) and the attention kernel's attributes (a read-only attention call)
+        x = torch.zeros((self.B, c.hidden), device=self.device, dtype=self.dtype)
+        L0 = self.layers[0]
+        for wt in (L0["wqkv"], L0["wgu"], self.lm_head):
+            x @ wt.t()
+        (torch.zeros((self.B, c.ffn), device=self.device, dtype=self.dtype) @ L0["wdown"].t())
+        q = torch.zeros((self.B, c.heads, c.head_dim), device=self.device, dtype=self.dtype)
+        qs = q.stride()
+        _lib.check(lib.cq_attention_at(ctypes.byref(L0["desc"]), L0["len"].data_ptr(), self.max_len, q.data_ptr(),
+                                       cq_dtype(q), c.heads, qs[0], qs[1], 1.0, self.attn_out.data_ptr(),
+                                       cq_dtype(self.attn_out), None, self.workspace.data_ptr(),
+                                       self.workspace.numel() * 4, stream_ptr(self.device)), "decoder")
+        torch.cuda.synchronize(self.device)
+        self.graph = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(self.graph):
+            self.logits = self._step_body()
+        torch.cuda.synchronize(self.device)
+
+    def decode(self, steps: int) -> torch.Tensor:
+        """Replay the captured step ``steps`` times (greedy, no host sync in
+        between); returns the last step's logits.  The caches' host-side
+        offsets follow the device lengths afterwards."""
+        start = self.layers[0]["cache"].offset
+        if start + steps > self.max_len:
+            raise ValueError(f"decode past max_len {self.max_len}")
+        for _ in range(steps):
+            self.graph.replay()
+        for L in self.layers:
+            L["cache"].offset += steps
+        return self.logits
+
+    def bytes_per_step(self) -> int:
+        """Algorithmic HBM bytes of one step: every weight once, every layer's
+        active compressed cache once (the reference accounting)."""
+        w = self.embed.shape[1] * self.embed.element_size() * self.B + self.lm_head.numel() * self.lm_head.element_size()
+        for L in self.layers:
+            w += sum(L[n].numel() * L[n].element_size() for n in ("wqkv", "wo", "wgu", "wdown"))
+            w += L["cache"].nbytes
+        return w
