@@ -592,8 +592,10 @@ def run_decoder(args, cfg):
     dc = DecoderConfig()
     n_steps = args.warmup + args.steps + 4
     t_setup = time.perf_counter()
-    dec = Qwen3StyleDecoder(dc, B, T0 + n_steps + 4, kw, device=device, seed=100 + rank)
-    dec.fill_context(T0, seed=200 + rank)
+    tp = world > 1 and args.tp
+    dec = Qwen3StyleDecoder(dc, B, T0 + n_steps + 4, kw, device=device, seed=100 if tp else 100 + rank,
+                            tp_group=dist.group.WORLD if tp else None)
+    dec.fill_context(T0, seed=200 if tp else 200 + rank)
     dec.ids.copy_(torch.arange(B, device=device) * 7 + 1)
     dec.capture()
     setup_s = time.perf_counter() - t_setup
@@ -614,17 +616,17 @@ def run_decoder(args, cfg):
         tt = torch.tensor([ms], device=device)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
-    value = world * B / (ms * 1e-3)
+    value = (1 if tp else world) * B / (ms * 1e-3)
 
     # the attention kernels alone: a graph of every layer's read-only attention
-    q = torch.zeros((B, dc.heads, dc.head_dim), device=device, dtype=torch.bfloat16)
+    q = torch.zeros((B, dec.heads, dc.head_dim), device=device, dtype=torch.bfloat16)
     qs = q.stride()
     lib = _lib.lib()
     ag = torch.cuda.CUDAGraph()
     with torch.cuda.graph(ag):
         for L in dec.layers:
             _lib.check(lib.cq_attention_at(ctypes.byref(L["desc"]), L["len"].data_ptr(), dec.max_len, q.data_ptr(),
-                                           cq_dtype(q), dc.heads, qs[0], qs[1], 1.0 / math.sqrt(dc.head_dim),
+                                           cq_dtype(q), dec.heads, qs[0], qs[1], 1.0 / math.sqrt(dc.head_dim),
                                            dec.attn_out.data_ptr(), cq_dtype(dec.attn_out), None,
                                            dec.workspace.data_ptr(), dec.workspace.numel() * 4,
                                            torch.cuda.current_stream().cuda_stream), "bench")
@@ -658,7 +660,7 @@ def run_decoder(args, cfg):
         res = {
             "metric": DECODER_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "weak", "vs_baseline": None,
+            "scaling": "strong" if tp else "weak", "vs_baseline": None,
             "dtype": "bf16 weights/activations, int4-residual/f16-anchor FT-V3 caches, f32 accumulate",
             "data": "random-init weights N(0,0.02); synthetic seeded K/V context encoded by the cache; greedy ids",
             "config": {"workload": cfg["name"], "batch": B, "context_tokens": T0, "layers": dc.layers,
@@ -666,21 +668,27 @@ def run_decoder(args, cfg):
                        "ffn": dc.ffn, "vocab": dc.vocab, "caches": "FT-V3 (64/32, 4/3 bits, dz 0/0.05)",
                        "step": "one CUDA-graph replay: 36 x (RMSNorm, QKV, q/k norm, RoPE, fused append+decode "
                                "attention, o_proj, SwiGLU) + lm_head + argmax",
-                       "parallelism": f"dp{world} (independent replicas, no collective)",
+                       "parallelism": (f"tp{world} (kv-head tensor parallel, NCCL all-reduce after o_proj and "
+                                       "the down projection)") if tp else f"dp{world} (independent replicas)",
                        "setup_seconds": round(setup_s, 1)},
             "attention_ms_per_step": round(attn_ms, 4),
             "compressed_cache_bytes": cache_bytes,
-            "e2e": {"value": round(world * B / (e_ms * 1e-3), 1), "unit": "tokens/s", "h2d_bytes_per_step": 0,
+            "e2e": {"value": round((1 if tp else world) * B / (e_ms * 1e-3), 1), "unit": "tokens/s",
+                    "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": B * 8, "steps": e_steps},
             "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + compressed caches, each read once)",
                          "achieved": round(bytes_step / (ms * 1e-3) / 1e9, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(bytes_step / (ms * 1e-3) / 1e9 / peak, 4), "peak_source": peak_kind,
                          "traffic": None, "algorithmic_bytes_per_step": bytes_step},
             "clocks": clk.summary(),
-            "gpu_launches": args.steps * dc.layers,  # this package's kernels: one attention kernel per layer
+            # this package's kernels per step: per layer two RMSNorms, q/k norm + RoPE, the fused
+            # append+decode kernel and SwiGLU; one final RMSNorm
+            "gpu_launches": args.steps * (5 * dc.layers + 1),
         }
         print(json.dumps(res))
     if world > 1:
+        dec.graph = None  # graphs holding NCCL work go before the process group
+        torch.cuda.synchronize()
         dist.barrier()
         dist.destroy_process_group()
 
@@ -914,6 +922,7 @@ def main():
     ap.add_argument("--cpu-budget", type=float, default=15.0)
     ap.add_argument("--page-tokens", type=int, default=None, help="cache page size (default: the cache's choice)")
     ap.add_argument("--cpu-rows", type=int, default=128, help="config 4 CPU sample: query rows per kv-head")
+    ap.add_argument("--tp", action="store_true", help="config 5 under torchrun: kv-head tensor parallel")
     ap.add_argument("--context", type=int, default=None,
                     help="config 4: cached tokens before the chunk (default 65536; smaller for profiler captures)")
     args = ap.parse_args()

@@ -32,6 +32,7 @@ EXPORTED = [
     "cq_dequantize_delta", "cq_pack_int4", "cq_unpack_int4", "cq_sdpa_reference_layout",
     "cq_sdpa_reference_layout_workspace", "cq_attention_static_scratch", "cq_decode_chunk_tokens",
     "cq_append_at", "cq_attention_at", "cq_decode_step_at", "cq_prefill_prepare", "cq_prefill_attend",
+    "cq_rmsnorm", "cq_qk_norm_rope", "cq_silu_mul",
 ]
 
 
@@ -95,6 +96,9 @@ def _declare(lib):
         "cq_attention_at": [C, P, I64, P, ctypes.c_int, I32, I64, I64, F, P, ctypes.c_int, P, P, SZ, P],
         "cq_decode_step_at": [C, P, I64, I64, P, I64, I64, ctypes.c_int, P, I64, P, ctypes.c_int, I32, I64, I64, F, P,
                               ctypes.c_int, P, P, SZ, P],
+        "cq_rmsnorm": [P, P, P, I64, I32, F, ctypes.c_int, P],
+        "cq_qk_norm_rope": [P, I64, I32, I32, I32, I32, P, P, P, P, F, P, P, P, ctypes.c_int, P],
+        "cq_silu_mul": [P, P, I64, I32, ctypes.c_int, P],
         "cq_prefill_prepare": [C, I64, P, ctypes.c_int, I32, I32, I64, I64, I64, F, P, SZ, P],
         "cq_prefill_attend": [C, I64, I32, I32, I32, P, ctypes.c_int, P, P, SZ, P],
         "cq_attention_static_scratch": [C, I64, P, ctypes.c_int, I32, I32, I32, I64, I64, I64, F, P, ctypes.c_int,

@@ -14,8 +14,9 @@ whole step so that it can be captured:
                -> o_proj + residual -> RMSNorm -> SwiGLU FFN + residual
     then: final RMSNorm -> lm_head -> argmax, fed back as the next input ids.
 
-The GEMMs are cuBLAS (torch.matmul); norms, RoPE and SwiGLU are torch
-elementwise ops; attention is this package's kernel.  Every layer's cache
+The GEMMs are cuBLAS (torch.matmul); RMSNorm, the per-head q/k norm with
+RoPE and the SwiGLU product are this package's fused kernels (cq_rmsnorm,
+cq_qk_norm_rope, cq_silu_mul); attention is its decode kernel.  Every layer's cache
 length lives on the device and advances inside the kernel, the RoPE position
 is a device counter, and the sampled ids are written back in-graph, so a
 replay needs no host synchronisation.
@@ -69,28 +70,54 @@ class Qwen3StyleDecoder:
     greedy decode step for ``batch`` sequences of up to ``max_len`` tokens."""
 
     def __init__(self, cfg: DecoderConfig, batch: int, max_len: int, cache_kwargs: dict | None = None,
-                 device="cuda", dtype=torch.bfloat16, seed: int = 0):
+                 device="cuda", dtype=torch.bfloat16, seed: int = 0, tp_group=None):
+        """``tp_group``: a torch.distributed (NCCL) group over which the layers
+        are tensor-parallel by kv-head: this rank keeps kv_heads/N kv-heads
+        with their query heads and ffn/N of each FFN; the o_proj and down
+        projections end in an all-reduce.  The full weights are drawn the same
+        way on every rank and sliced, so any N gives the same model."""
         self.cfg, self.B, self.max_len = cfg, batch, max_len
         self.device, self.dtype = torch.device(device), dtype
+        self.group = tp_group
+        if tp_group is not None:
+            import torch.distributed as dist
+            self.rank, self.world = dist.get_rank(tp_group), dist.get_world_size(tp_group)
+        else:
+            self.rank, self.world = 0, 1
+        c = cfg
+        if c.kv_heads % self.world or c.ffn % self.world:
+            raise ValueError("kv_heads and ffn must divide by the tensor-parallel size")
+        self.heads, self.kv_heads, self.ffn = c.heads // self.world, c.kv_heads // self.world, c.ffn // self.world
         g = torch.Generator(device=self.device).manual_seed(seed)
 
         def w(*shape):
             return (torch.randn(shape, generator=g, device=self.device, dtype=torch.float32) * 0.02).to(dtype)
 
-        c = cfg
-        qkv = (c.heads + 2 * c.kv_heads) * c.head_dim
+        r, D = self.rank, c.head_dim
+        hq, hk, f = self.heads, self.kv_heads, self.ffn
+
+        def local_qkv(full):  # rows [q heads | k heads | v heads] -> this rank's heads of each
+            q0, k0 = c.heads * D, (c.heads + c.kv_heads) * D
+            return torch.cat((full[r * hq * D:(r + 1) * hq * D], full[q0 + r * hk * D:q0 + (r + 1) * hk * D],
+                              full[k0 + r * hk * D:k0 + (r + 1) * hk * D])).contiguous()
+
         self.embed = w(c.vocab, c.hidden)
         self.lm_head = w(c.vocab, c.hidden)
         self.final_norm = torch.ones(c.hidden, device=self.device, dtype=dtype)
         self.layers = []
         for i in range(c.layers):
+            wqkv = local_qkv(w((c.heads + 2 * c.kv_heads) * D, c.hidden))
+            wo = w(c.hidden, c.heads * D)[:, r * hq * D:(r + 1) * hq * D].contiguous()
+            wgu_full = w(2 * c.ffn, c.hidden)
+            wgu = torch.cat((wgu_full[r * f:(r + 1) * f], wgu_full[c.ffn + r * f:c.ffn + (r + 1) * f])).contiguous()
+            del wgu_full
+            wdown = w(c.hidden, c.ffn)[:, r * f:(r + 1) * f].contiguous()
             self.layers.append(dict(
                 ln1=torch.ones(c.hidden, device=self.device, dtype=dtype),
                 ln2=torch.ones(c.hidden, device=self.device, dtype=dtype),
-                q_norm=torch.ones(c.head_dim, device=self.device, dtype=dtype),
-                k_norm=torch.ones(c.head_dim, device=self.device, dtype=dtype),
-                wqkv=w(qkv, c.hidden), wo=w(c.hidden, c.heads * c.head_dim),
-                wgu=w(2 * c.ffn, c.hidden), wdown=w(c.hidden, c.ffn),
+                q_norm=torch.ones(D, device=self.device, dtype=dtype),
+                k_norm=torch.ones(D, device=self.device, dtype=dtype),
+                wqkv=wqkv, wo=wo, wgu=wgu, wdown=wdown,
                 cache=ChronoQuantCache(layer_idx=i, max_tokens=max_len, **(cache_kwargs or {})),
             ))
         self.inv_freq = 1.0 / (c.rope_theta ** (torch.arange(0, c.head_dim, 2, device=self.device,
@@ -105,12 +132,13 @@ class Qwen3StyleDecoder:
         """Encode a synthetic T0-token context into every layer's cache."""
         c = self.cfg
         g = torch.Generator(device=self.device).manual_seed(seed)
+        h0, h1 = self.rank * self.kv_heads, (self.rank + 1) * self.kv_heads  # this rank's kv-heads
         for L in self.layers:
             for t in range(0, T0, chunk):
                 n = min(chunk, T0 - t)
                 k = torch.randn((self.B, c.kv_heads, n, c.head_dim), generator=g, device=self.device).to(self.dtype)
                 v = torch.randn((self.B, c.kv_heads, n, c.head_dim), generator=g, device=self.device).to(self.dtype)
-                L["cache"].update_and_fetch(k, v)
+                L["cache"].update_and_fetch(k[:, h0:h1].contiguous(), v[:, h0:h1].contiguous())
         self.pos.fill_(T0)
         self._prepare_attention()
 
@@ -125,12 +153,11 @@ class Qwen3StyleDecoder:
             L["desc"] = st.descriptor()
             L["len"] = torch.tensor([L["cache"].offset, 0], dtype=torch.int64, device=self.device)
             need = ctypes.c_size_t(0)
-            _lib.check(lib.cq_attention_workspace(ctypes.byref(L["desc"]), self.max_len, self.cfg.heads, 1, 0,
+            _lib.check(lib.cq_attention_workspace(ctypes.byref(L["desc"]), self.max_len, self.heads, 1, 0,
                                                   ctypes.byref(need)), "decoder")
             need_max = max(need_max, need.value)
         self.workspace = torch.zeros(max(1, (need_max + 3) // 4), dtype=torch.float32, device=self.device)
-        self.attn_out = torch.empty((self.B, self.cfg.heads, self.cfg.head_dim), dtype=self.dtype,
-                                    device=self.device)
+        self.attn_out = torch.empty((self.B, self.heads, self.cfg.head_dim), dtype=self.dtype, device=self.device)
 
     # -- one decode step --------------------------------------------------------
     def _attention(self, L: dict, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
@@ -139,29 +166,46 @@ class Qwen3StyleDecoder:
         ks, vs, qs = k.stride(), v.stride(), q.stride()
         _lib.check(_lib.lib().cq_decode_step_at(
             ctypes.byref(L["desc"]), k.data_ptr(), ks[0], ks[1], v.data_ptr(), vs[0], vs[1], cq_dtype(k),
-            L["len"].data_ptr(), self.max_len, q.data_ptr(), cq_dtype(q), self.cfg.heads, qs[0], qs[1],
+            L["len"].data_ptr(), self.max_len, q.data_ptr(), cq_dtype(q), self.heads, qs[0], qs[1],
             1.0 / math.sqrt(self.cfg.head_dim), self.attn_out.data_ptr(), cq_dtype(self.attn_out), None,
             self.workspace.data_ptr(), self.workspace.numel() * 4, stream_ptr(self.device)), "decoder")
         return self.attn_out
 
+    def _norm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
+        y = torch.empty_like(x)
+        _lib.check(_lib.lib().cq_rmsnorm(x.data_ptr(), w.data_ptr(), y.data_ptr(), x.shape[0], x.shape[1],
+                                         self.cfg.eps, cq_dtype(x), stream_ptr(self.device)), "decoder")
+        return y
+
+    def _reduce(self, partial: torch.Tensor) -> torch.Tensor:
+        """Sum a row-parallel projection's partial outputs over the tensor-parallel ranks."""
+        if self.world > 1:
+            import torch.distributed as dist
+            dist.all_reduce(partial, group=self.group)
+        return partial
+
     def _step_body(self, attention=None) -> torch.Tensor:
         c, B = self.cfg, self.B
         attention = attention or self._attention
-        nq, nk = c.heads * c.head_dim, c.kv_heads * c.head_dim
+        nq, nk = self.heads * c.head_dim, self.kv_heads * c.head_dim
+        lib, st, dt = _lib.lib(), stream_ptr(self.device), cq_dtype(self.embed)
         x = self.embed[self.ids]
-        ang = self.pos.float() * self.inv_freq
-        cos = torch.cat((ang.cos(), ang.cos()))
-        sin = torch.cat((ang.sin(), ang.sin()))
         for L in self.layers:
-            qkv = _rmsnorm(x, L["ln1"], c.eps) @ L["wqkv"].t()
-            q = _rope(_rmsnorm(qkv[:, :nq].view(B, c.heads, c.head_dim), L["q_norm"], c.eps), cos, sin)
-            k = _rope(_rmsnorm(qkv[:, nq:nq + nk].view(B, c.kv_heads, c.head_dim), L["k_norm"], c.eps), cos, sin)
-            v = qkv[:, nq + nk:].reshape(B, c.kv_heads, c.head_dim)
-            a = attention(L, q.contiguous(), k.contiguous(), v.contiguous())
-            x = x + a.reshape(B, nq) @ L["wo"].t()
-            gu = _rmsnorm(x, L["ln2"], c.eps) @ L["wgu"].t()
-            x = x + (torch.nn.functional.silu(gu[:, :c.ffn]) * gu[:, c.ffn:]) @ L["wdown"].t()
-        logits = _rmsnorm(x, self.final_norm, c.eps) @ self.lm_head.t()
+            qkv = self._norm(x, L["ln1"]) @ L["wqkv"].t()
+            q = torch.empty((B, self.heads, c.head_dim), device=self.device, dtype=self.dtype)
+            k = torch.empty((B, self.kv_heads, c.head_dim), device=self.device, dtype=self.dtype)
+            v = torch.empty_like(k)
+            _lib.check(lib.cq_qk_norm_rope(qkv.data_ptr(), qkv.stride(0), B, self.heads, self.kv_heads, c.head_dim,
+                                           L["q_norm"].data_ptr(), L["k_norm"].data_ptr(), self.inv_freq.data_ptr(),
+                                           self.pos.data_ptr(), c.eps, q.data_ptr(), k.data_ptr(), v.data_ptr(), dt,
+                                           st), "decoder")
+            a = attention(L, q, k, v)
+            x = x + self._reduce(a.reshape(B, nq) @ L["wo"].t())
+            gu = self._norm(x, L["ln2"]) @ L["wgu"].t()
+            h = torch.empty((B, self.ffn), device=self.device, dtype=self.dtype)
+            _lib.check(lib.cq_silu_mul(gu.data_ptr(), h.data_ptr(), B, self.ffn, dt, st), "decoder")
+            x = x + self._reduce(h @ L["wdown"].t())
+        logits = self._norm(x, self.final_norm) @ self.lm_head.t()
         self.out_ids.copy_(logits.argmax(-1))
         self.ids.copy_(self.out_ids)
         self.pos.add_(1)
@@ -182,11 +226,13 @@ class Qwen3StyleDecoder:
         L0 = self.layers[0]
         for wt in (L0["wqkv"], L0["wgu"], self.lm_head):
             x @ wt.t()
-        (torch.zeros((self.B, c.ffn), device=self.device, dtype=self.dtype) @ L0["wdown"].t())
-        q = torch.zeros((self.B, c.heads, c.head_dim), device=self.device, dtype=self.dtype)
+        (torch.zeros((self.B, self.ffn), device=self.device, dtype=self.dtype) @ L0["wdown"].t())
+        if self.world > 1:  # the communicator exists before the capture
+            self._reduce(torch.zeros((self.B, c.hidden), device=self.device, dtype=self.dtype))
+        q = torch.zeros((self.B, self.heads, c.head_dim), device=self.device, dtype=self.dtype)
         qs = q.stride()
         _lib.check(lib.cq_attention_at(ctypes.byref(L0["desc"]), L0["len"].data_ptr(), self.max_len, q.data_ptr(),
-                                       cq_dtype(q), c.heads, qs[0], qs[1], 1.0, self.attn_out.data_ptr(),
+                                       cq_dtype(q), self.heads, qs[0], qs[1], 1.0, self.attn_out.data_ptr(),
                                        cq_dtype(self.attn_out), None, self.workspace.data_ptr(),
                                        self.workspace.numel() * 4, stream_ptr(self.device)), "decoder")
         torch.cuda.synchronize(self.device)

@@ -292,6 +292,24 @@ int cq_attention_static_scratch(const cq_paged_cache *cache, int64_t T, const vo
                                 int64_t q_sq, float scale, void *out, int out_dtype, float *lse_out,
                                 int32_t num_splits, void *stream);
 
+/* Decoder helpers (no reference counterpart: the reference gets its model
+ * from mlx_lm).  The elementwise steps of the decoder that drives the cache
+ * end to end, each one kernel, rounding as the unfused
+ * torch ops do:
+ *   cq_rmsnorm       y[r] = dtype(x[r] * rsqrt(mean(x[r]^2) + eps)) * w, rows of dim;
+ *   cq_qk_norm_rope  per head of fused QKV rows [batch][(Hq + 2 Hkv) * 128] (row
+ *                    stride in elements): RMSNorm over head_dim with q_norm_w /
+ *                    k_norm_w for the q / k heads, rotate-half RoPE at position
+ *                    *pos with inv_freq[64] (fp32); q, k, v written contiguous
+ *                    [batch][H][128];
+ *   cq_silu_mul      y = dtype(silu(g)) * u for gu rows [gate (ffn) | up (ffn)].
+ * dtype CQ_F16 or CQ_BF16 for every tensor argument except inv_freq and pos. */
+int cq_rmsnorm(const void *x, const void *w, void *y, int64_t rows, int32_t dim, float eps, int dtype, void *stream);
+int cq_qk_norm_rope(const void *qkv, int64_t row_stride, int32_t batch, int32_t n_q_heads, int32_t n_kv_heads,
+                    int32_t head_dim, const void *q_norm_w, const void *k_norm_w, const float *inv_freq,
+                    const int64_t *pos, float eps, void *q_out, void *k_out, void *v_out, int dtype, void *stream);
+int cq_silu_mul(const void *gu, void *y, int64_t rows, int32_t ffn, int dtype, void *stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -100,3 +100,44 @@ def nccl_worker(rank, world, port, K, V, q, stride_k, stride_v, queue):
         dist.destroy_process_group()
     except Exception as e:
         queue.put((rank, None, repr(e)))
+
+
+def tp_decoder_worker(rank, world, port, steps, queue):
+    """Kv-head tensor-parallel decoder on `world` GPUs against the same decoder
+    on one GPU (rank 0), same weights, context and input ids every step."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        from chronoquant_mlx_b200.decoder import DecoderConfig, Qwen3StyleDecoder
+        cfg = DecoderConfig(layers=2, hidden=512, heads=8, kv_heads=2, head_dim=128, ffn=1024, vocab=1000)
+        tp = Qwen3StyleDecoder(cfg, 2, 320, device=dev, seed=9, tp_group=dist.group.WORLD)
+        tp.fill_context(300)
+        tp.capture()
+        one = None
+        if rank == 0:
+            one = Qwen3StyleDecoder(cfg, 2, 320, device=dev, seed=9)
+            one.fill_context(300)
+            one.capture()
+        rels = []
+        for s in range(steps):
+            ids = torch.tensor([3 + s, 50 + s], device=dev)
+            tp.ids.copy_(ids)
+            lt = tp.decode(1).float().clone()
+            if one is not None:
+                one.ids.copy_(ids)
+                lo = one.decode(1).float()
+                rels.append(float((lt - lo).norm() / lo.norm()))
+        torch.cuda.synchronize()
+        del tp.graph  # graphs holding NCCL work go before the process group
+        if one is not None:
+            del one.graph
+        dist.barrier()
+        dist.destroy_process_group()
+        queue.put((rank, rels, None))
+    except Exception as e:
+        queue.put((rank, None, repr(e)))

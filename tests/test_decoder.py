@@ -66,3 +66,89 @@ def test_graph_decode_matches_eager_and_reference(cache_kwargs):
     # update_and_fetch does (deeper layers see slightly different attention outputs)
     for x, y in zip(g.layers[0]["cache"].state, r.layers[0]["cache"].state):
         assert torch.equal(x.view(torch.uint8), y.view(torch.uint8))
+
+
+def test_tensor_parallel_matches_one_gpu():
+    """Two GPUs, kv-head tensor parallel (1 kv-head, 4 query heads and half the
+    FFN per GPU, all-reduces after o_proj and the down projection, all in the
+    captured graph): logits within 2e-2 relative of the one-GPU decoder with
+    the same weights (bf16 partial sums are added in another order)."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 2:
+        pytest.skip("needs two GPUs")
+    import multiprocessing as mp
+    import socket
+    import _dist_workers as W
+    sk = socket.socket()
+    sk.bind(("127.0.0.1", 0))
+    port = sk.getsockname()[1]
+    sk.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=W.tp_decoder_worker, args=(r, 2, port, 3, q)) for r in range(2)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=240) for _ in range(2)], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=60)
+    for rank, rels, err in res:
+        assert err is None, err
+    assert len(res[0][1]) == 3 and all(r < 2e-2 for r in res[0][1]), res[0][1]
+
+
+def _ulps(a: torch.Tensor, b: torch.Tensor) -> torch.Tensor:
+    """Distance in units of the last place of a and b's common dtype (bf16/fp16
+    bit patterns read as ordered integers)."""
+    ia = a.contiguous().view(torch.int16).int()
+    ib = b.contiguous().view(torch.int16).int()
+    ia = torch.where(ia < 0, -32768 - ia, ia)
+    ib = torch.where(ib < 0, -32768 - ib, ib)
+    return (ia - ib).abs()
+
+
+@pytest.mark.parametrize("dtype", [torch.bfloat16, torch.float16])
+def test_fused_elementwise_ops_match_torch(dtype):
+    """cq_rmsnorm, cq_qk_norm_rope and cq_silu_mul against the torch
+    expressions they replace (decoder._rmsnorm, decoder._rope, silu(g)*u): at
+    most one ulp apart (the fp32 sum of squares and exp are evaluated in another
+    order / by another routine), and nearly all elements identical."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from chronoquant_mlx_b200 import _lib
+    from chronoquant_mlx_b200._tensors import cq_dtype, stream_ptr
+    from chronoquant_mlx_b200.decoder import _rmsnorm, _rope
+    lib, st, dt = _lib.lib(), stream_ptr(torch.device("cuda")), cq_dtype(torch.empty(0, dtype=dtype))
+    gen = torch.Generator(device="cuda").manual_seed(11)
+    B, Hq, Hkv, D, hidden, ffn, eps = 5, 8, 2, 128, 1000, 3000, 1e-6
+
+    x = torch.randn(B, hidden, device="cuda", generator=gen).to(dtype) * 3
+    w = (1 + 0.2 * torch.randn(hidden, device="cuda", generator=gen)).to(dtype)
+    y = torch.empty_like(x)
+    _lib.check(lib.cq_rmsnorm(x.data_ptr(), w.data_ptr(), y.data_ptr(), B, hidden, eps, dt, st), "test")
+    d = _ulps(y, _rmsnorm(x, w, eps))
+    assert int(d.max()) <= 1 and float((d > 0).float().mean()) < 0.02
+
+    qkv = torch.randn(B, (Hq + 2 * Hkv) * D + 64, device="cuda", generator=gen).to(dtype)[:, 64:]  # strided rows
+    wq = (1 + 0.2 * torch.randn(D, device="cuda", generator=gen)).to(dtype)
+    wk = (1 + 0.2 * torch.randn(D, device="cuda", generator=gen)).to(dtype)
+    inv_freq = 1.0 / (1.0e6 ** (torch.arange(0, D, 2, device="cuda", dtype=torch.float32) / D))
+    pos = torch.tensor(12345, device="cuda")
+    q = torch.empty(B, Hq, D, device="cuda", dtype=dtype)
+    k = torch.empty(B, Hkv, D, device="cuda", dtype=dtype)
+    v = torch.empty_like(k)
+    _lib.check(lib.cq_qk_norm_rope(qkv.data_ptr(), qkv.stride(0), B, Hq, Hkv, D, wq.data_ptr(), wk.data_ptr(),
+                                   inv_freq.data_ptr(), pos.data_ptr(), eps, q.data_ptr(), k.data_ptr(),
+                                   v.data_ptr(), dt, st), "test")
+    ang = pos.float() * inv_freq
+    cos, sin = torch.cat((ang.cos(), ang.cos())), torch.cat((ang.sin(), ang.sin()))
+    rq = _rope(_rmsnorm(qkv[:, :Hq * D].reshape(B, Hq, D), wq, eps), cos, sin)
+    rk = _rope(_rmsnorm(qkv[:, Hq * D:(Hq + Hkv) * D].reshape(B, Hkv, D), wk, eps), cos, sin)
+    assert torch.equal(v, qkv[:, (Hq + Hkv) * D:].reshape(B, Hkv, D))
+    for got, ref in ((q, rq), (k, rk)):
+        d = _ulps(got, ref)
+        assert int(d.max()) <= 1 and float((d > 0).float().mean()) < 0.02, (int(d.max()), float((d > 0).float().mean()))
+
+    gu = torch.randn(B, 2 * ffn, device="cuda", generator=gen).to(dtype) * 4
+    h = torch.empty(B, ffn, device="cuda", dtype=dtype)
+    _lib.check(lib.cq_silu_mul(gu.data_ptr(), h.data_ptr(), B, ffn, dt, st), "test")
+    d = _ulps(h, torch.nn.functional.silu(gu[:, :ffn]) * gu[:, ffn:])
+    assert int(d.max()) <= 1 and float((d > 0).float().mean()) < 0.02
