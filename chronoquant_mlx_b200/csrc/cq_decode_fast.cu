@@ -25,9 +25,12 @@
 //             it exceeds the running one by 8, so p <= 256);
 //   output    O += anchor_v(t) * p_t + codes_v(t) * (p_t * scale_t), both as
 //             MMAs with tokens as the reduction axis: V anchors are gathered
-//             per token with ldmatrix.trans, V codes dequantise in registers
-//             (MMA nibble order), P moves to the operand layout with
-//             movmatrix.trans.
+//             per token with ldmatrix.trans; V codes (MMA nibble order) enter
+//             as the fp16 values 64 + n = code + 72 made by bit operations
+//             alone, and 72 * sum_t(p_t * scale_t) -- one more MMA with the
+//             same fp16 weights -- is subtracted when the partial is written;
+//             P moves to the operand layout with movmatrix.trans, and
+//             P * scale as one half2 product with two tokens' scales.
 //
 // Work: warp w of the grid takes the contiguous, balanced chunk range
 // [w*tc/W, (w+1)*tc/W) of the unit-major chunk index and writes one partial
@@ -285,11 +288,13 @@ struct WarpState {
   float m[2];     // running max (log2 units) of heads 2t, 2t+1
   float l[2];     // this thread's partial sums
   float o[8][4];  // O^T fragments: [m-tile i][c0..c3]
+  float vb[4];    // 72 * sum of the fp16 code weights P' (same fragment layout): the V code offset
 };
 
 __device__ __forceinline__ void reset(WarpState &st) {
   st.m[0] = st.m[1] = -INFINITY;
   st.l[0] = st.l[1] = 0.f;
+  st.vb[0] = st.vb[1] = st.vb[2] = st.vb[3] = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -305,7 +310,7 @@ struct LaneAddr {
   uint32_t cdK;   // K code row of token g (tile base 0), word group t
   uint32_t cdV;   // V code row of token 2t (tile base 0), words 2g, 2g+1
   uint32_t scK;   // K scale of token g
-  uint32_t scV;   // V scale of token g
+  uint32_t scV;   // V scales of tokens 2t, 2t+1 (one 32-bit word)
   uint32_t kfV;   // V anchor row of this lane's ldmatrix row (tile 0)
   uint32_t kfV0;  // V anchor row 0, same column half
   uint32_t qa;    // q.anchor table, heads 2t, 2t+1
@@ -318,7 +323,7 @@ struct LaneAddr {
     cdV = sa + G::O_CD1 + (2 * t - 1) * 64 + g * 8;
     dv8 = v8 ? 7 : 8;
     scK = sa + G::O_SC0 + g * 2;
-    scV = sa + G::O_SC1 + g * 2;
+    scV = sa + G::O_SC1 + t * 4;
     kfV0 = sa + G::O_KF1 + ((mi & 1) ? 16 : 0);
     kfV = kfV0 + ((v8 ? (mi >> 1) : 0) * (HD * 2));
     qa = qa_base + t * 8;
@@ -339,7 +344,6 @@ __device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, 
   constexpr int NT = 2;
   const int g = lane >> 2;
   float s[NT][4];
-  float sv[NT][2];
   // ---------------- scores S^T[token][head] = scale_t * (q.codes_t) + q.anchor
 #pragma unroll
   for (int tile = 0; tile < NT; ++tile) {
@@ -349,8 +353,6 @@ __device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, 
     const uint4 wk1 = ptx::lds_u128(A.cdK + rk + 8 * 64);
     const float sk0 = lds_half_as_float(A.scK + tb * 2) * LOG2E;
     const float sk1 = lds_half_as_float(A.scK + (tb + 8) * 2) * LOG2E;
-    sv[tile][0] = lds_half_as_float(A.scV + tb * 2);
-    sv[tile][1] = lds_half_as_float(A.scV + (tb + 8) * 2);
     const float2 qa = ptx::lds_f2(A.qa + (uint32_t)((tb >> lsk) * 32));  // one K anchor per tile (stride >= 16)
     // raw nibbles (1024+n, 1024+16n) against q (q/16 on the 16n lanes); the
     // accumulator starts at -q.(all-8 word), which removes the raw offset
@@ -370,15 +372,9 @@ __device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, 
     s[tile][2] = fmaf(sk1, ca[2] + cb[2], qa.x);
     s[tile][3] = fmaf(sk1, ca[3] + cb[3], qa.y);
     if (MASK) {
-      // tokens past the end: score -inf, V scale 0 (their slot bytes are stale)
-      if (tb + g >= nvalid) {
-        s[tile][0] = s[tile][1] = -INFINITY;
-        sv[tile][0] = 0.f;
-      }
-      if (tb + g + 8 >= nvalid) {
-        s[tile][2] = s[tile][3] = -INFINITY;
-        sv[tile][1] = 0.f;
-      }
+      // tokens past the end: score -inf (their slot bytes are stale)
+      if (tb + g >= nvalid) s[tile][0] = s[tile][1] = -INFINITY;
+      if (tb + g + 8 >= nvalid) s[tile][2] = s[tile][3] = -INFINITY;
     }
   }
   // ---------------- online softmax over the chunk (base 2), lazy rescale
@@ -403,6 +399,10 @@ __device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, 
       st.m[1] = n1;
       st.l[0] *= f0;
       st.l[1] *= f1;
+      st.vb[0] *= f0;
+      st.vb[1] *= f1;
+      st.vb[2] *= f0;
+      st.vb[3] *= f1;
 #pragma unroll
       for (int i = 0; i < 8; ++i) {
         st.o[i][0] *= f0;
@@ -423,11 +423,22 @@ __device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, 
     const float p3 = fast_exp2(s[tile][3] - st.m[1]);
     st.l[0] += p0 + p2;
     st.l[1] += p1 + p3;
-    // P (anchor term) and P' = P * scale_v (code term) as B operands
+    // P (anchor term) and P' = P * scale_v (code term) as B operands: in the
+    // operand layout a lane holds tokens 2t, 2t+1 (and 2t+8, 2t+9) of head g,
+    // whose V scales are one 32-bit word each
     const uint32_t bP0 = ptx::movmatrix_trans(ptx::pack_half2(p0, p1));
     const uint32_t bP1 = ptx::movmatrix_trans(ptx::pack_half2(p2, p3));
-    const uint32_t bS0 = ptx::movmatrix_trans(ptx::pack_half2(p0 * sv[tile][0], p1 * sv[tile][0]));
-    const uint32_t bS1 = ptx::movmatrix_trans(ptx::pack_half2(p2 * sv[tile][1], p3 * sv[tile][1]));
+    uint32_t sw0 = ptx::lds_u32(A.scV + tb * 2), sw1 = ptx::lds_u32(A.scV + (tb + 8) * 2);
+    if (MASK) {
+      // scales past the end are stale bytes (P is 0 there, but 0 * inf is not)
+      const int t2 = tb + 2 * (lane & 3);
+      if (t2 >= nvalid) sw0 = 0u;
+      else if (t2 + 1 >= nvalid) sw0 &= 0xffffu;
+      if (t2 + 8 >= nvalid) sw1 = 0u;
+      else if (t2 + 9 >= nvalid) sw1 &= 0xffffu;
+    }
+    const uint32_t bS0 = ptx::h22u(__hmul2(ptx::u2h2(bP0), ptx::u2h2(sw0)));
+    const uint32_t bS1 = ptx::h22u(__hmul2(ptx::u2h2(bP1), ptx::u2h2(sw1)));
     // V anchors: O += A_v^T P, ldmatrix.trans gathers each token's anchor row
     {
       uint32_t base = A.kfV + (uint32_t)((tb >> lsv) * (HD * 2));
@@ -460,14 +471,16 @@ __device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, 
         for (int half = 0; half < 2; ++half) {
           const uint32_t sel = half ? 0x7632u : 0x5410u;
           uint32_t xa[4], xc[4];
-          ptx::nibbles_to_half2(__byte_perm(wa, wb, sel), xa);  // nibbles 4*half + 0..3 of tokens (a, b)
-          ptx::nibbles_to_half2(__byte_perm(wc, wd, sel), xc);
+          ptx::nibbles_to_half2_64(__byte_perm(wa, wb, sel), xa);  // nibbles 4*half + 0..3 of tokens (a, b)
+          ptx::nibbles_to_half2_64(__byte_perm(wc, wd, sel), xc);
           // nibble j of word q <-> m-tile 4q + j/2, row g (+8 when j is odd)
           const int i0 = 4 * q + 2 * half;
           ptx::mma_f16_16816(st.o[i0], xa[0], xa[1], xc[0], xc[1], bS0, bS1);
           ptx::mma_f16_16816(st.o[i0 + 1], xa[2], xa[3], xc[2], xc[3], bS0, bS1);
         }
       }
+      // the offset 72 of every code value: 72 * sum_t P'_t, exactly as the MMAs above weight it
+      ptx::mma_f16_16816(st.vb, ptx::HALF2_72, ptx::HALF2_72, ptx::HALF2_72, ptx::HALF2_72, bS0, bS1);
     }
   }
 }
@@ -479,6 +492,10 @@ __device__ void flush_to(const Params &p, WarpState &st, float *pm, float *pl, f
   const int g = lane >> 2, t = lane & 3;
   const int G = p.gqa;
   float l0 = st.l[0], l1 = st.l[1];
+#pragma unroll
+  for (int i = 0; i < 8; ++i)
+#pragma unroll
+    for (int j = 0; j < 4; ++j) st.o[i][j] -= st.vb[j];  // codes were 64 + n = (n - 8) + 72
 #pragma unroll
   for (int o = 4; o < 32; o <<= 1) {
     l0 += __shfl_xor_sync(0xffffffffu, l0, o);

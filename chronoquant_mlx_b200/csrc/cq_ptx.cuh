@@ -192,6 +192,18 @@ __device__ __forceinline__ void nibbles_to_half2(uint32_t x, uint32_t (&out)[4])
   out[3] = h22u(__hfma2(u2h2(hi1), SCALE_HI, BIAS_HI));
 }
 
+// Codes of nibbles_to_half2 plus 72, with no arithmetic: each nibble is moved
+// to bits 4-7 of its 16-bit half under the fp16 exponent of 64 (0x5400, one
+// unit in the last place = 1/16), which reads as 64 + n = (n - 8) + 72.
+__device__ __forceinline__ void nibbles_to_half2_64(uint32_t x, uint32_t (&out)[4]) {
+  const uint32_t MAGIC = 0x54005400u;
+  out[0] = lop3_and_or(x << 4, 0x00f000f0u, MAGIC);
+  out[1] = lop3_and_or(x, 0x00f000f0u, MAGIC);
+  out[2] = lop3_and_or(x >> 4, 0x00f000f0u, MAGIC);
+  out[3] = lop3_and_or(x >> 8, 0x00f000f0u, MAGIC);
+}
+constexpr uint32_t HALF2_72 = 0x54805480u;  // (72, 72)
+
 // Raw form of nibbles_to_half2 without the bias removal: out[0], out[2] hold
 // 1024 + n (nibbles 0 and 2 of each 16-bit half), out[1], out[3] hold 1024 + 16n
 // (nibbles 1 and 3).  A dot product with these values equals the dot product
