@@ -593,9 +593,12 @@ def run_decoder(args, cfg):
     n_steps = args.warmup + args.steps + 4
     t_setup = time.perf_counter()
     tp = world > 1 and args.tp
-    dec = Qwen3StyleDecoder(dc, B, T0 + n_steps + 4, kw, device=device, seed=100 if tp else 100 + rank,
-                            tp_group=dist.group.WORLD if tp else None)
-    dec.fill_context(T0, seed=200 if tp else 200 + rank)
+    split = world > 1 and args.seqsplit and not tp
+    one_model = tp or split  # every rank runs the same sequences (else: independent replicas)
+    dec = Qwen3StyleDecoder(dc, B, T0 + n_steps + 4, kw, device=device, seed=100 if one_model else 100 + rank,
+                            tp_group=dist.group.WORLD if tp else None,
+                            seq_group=dist.group.WORLD if split else None)
+    dec.fill_context(T0, seed=200 if one_model else 200 + rank)
     dec.ids.copy_(torch.arange(B, device=device) * 7 + 1)
     dec.capture()
     setup_s = time.perf_counter() - t_setup
@@ -616,7 +619,7 @@ def run_decoder(args, cfg):
         tt = torch.tensor([ms], device=device)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         ms = float(tt.item())
-    value = (1 if tp else world) * B / (ms * 1e-3)
+    value = (1 if one_model else world) * B / (ms * 1e-3)
 
     # the attention kernels alone: a graph of every layer's read-only attention
     q = torch.zeros((B, dec.heads, dc.head_dim), device=device, dtype=torch.bfloat16)
@@ -660,7 +663,7 @@ def run_decoder(args, cfg):
         res = {
             "metric": DECODER_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms, 4), "higher_is_better": True,
-            "scaling": "strong" if tp else "weak", "vs_baseline": None,
+            "scaling": "strong" if one_model else "weak", "vs_baseline": None,
             "dtype": "bf16 weights/activations, int4-residual/f16-anchor FT-V3 caches, f32 accumulate",
             "data": "random-init weights N(0,0.02); synthetic seeded K/V context encoded by the cache; greedy ids",
             "config": {"workload": cfg["name"], "batch": B, "context_tokens": T0, "layers": dc.layers,
@@ -669,11 +672,14 @@ def run_decoder(args, cfg):
                        "step": "one CUDA-graph replay: 36 x (RMSNorm, QKV, q/k norm, RoPE, fused append+decode "
                                "attention, o_proj, SwiGLU) + lm_head + argmax",
                        "parallelism": (f"tp{world} (kv-head tensor parallel, NCCL all-reduce after o_proj and "
-                                       "the down projection)") if tp else f"dp{world} (independent replicas)",
+                                       "the down projection)") if tp else
+                                      (f"seq{world} (token ranges of one sequence per rank, NCCL all-gather of "
+                                       "partial attention + log-sum-exp merge per layer)") if split else
+                                      f"dp{world} (independent replicas)",
                        "setup_seconds": round(setup_s, 1)},
             "attention_ms_per_step": round(attn_ms, 4),
             "compressed_cache_bytes": cache_bytes,
-            "e2e": {"value": round((1 if tp else world) * B / (e_ms * 1e-3), 1), "unit": "tokens/s",
+            "e2e": {"value": round((1 if one_model else world) * B / (e_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": B * 8, "steps": e_steps},
             "roofline": {"bound": "hbm", "kernel": "whole decode step (weights + compressed caches, each read once)",
@@ -682,8 +688,9 @@ def run_decoder(args, cfg):
                          "traffic": None, "algorithmic_bytes_per_step": bytes_step},
             "clocks": clk.summary(),
             # this package's kernels per step: per layer two RMSNorms, q/k norm + RoPE, the fused
-            # append+decode kernel and SwiGLU; one final RMSNorm
-            "gpu_launches": args.steps * (5 * dc.layers + 1),
+            # append+decode kernel (or the read-only attention) and SwiGLU, plus the partial merge
+            # under a sequence split; one final RMSNorm
+            "gpu_launches": args.steps * ((6 if split else 5) * dc.layers + 1),
         }
         print(json.dumps(res))
     if world > 1:
@@ -923,13 +930,22 @@ def main():
     ap.add_argument("--page-tokens", type=int, default=None, help="cache page size (default: the cache's choice)")
     ap.add_argument("--cpu-rows", type=int, default=128, help="config 4 CPU sample: query rows per kv-head")
     ap.add_argument("--tp", action="store_true", help="config 5 under torchrun: kv-head tensor parallel")
+    ap.add_argument("--seqsplit", action="store_true",
+                    help="config 5: one sequence (batch 1, 524288-token context unless --context), split by "
+                         "token ranges over the torchrun ranks")
     ap.add_argument("--context", type=int, default=None,
-                    help="config 4: cached tokens before the chunk (default 65536; smaller for profiler captures)")
+                    help="config 4: cached tokens before the chunk (default 65536; smaller for profiler "
+                         "captures); config 5: context tokens")
     args = ap.parse_args()
     if args.warmup < 3:
         args.warmup = 3
     cfg = CONFIGS[args.config]
     if args.config == 4 and args.context is not None:
+        cfg = dict(cfg, T=args.context, name=f"{cfg['name']}-ctx{args.context}")
+    if args.config == 5 and args.seqsplit:
+        T = args.context or 524288
+        cfg = dict(cfg, B=1, T=T, name=f"cfg5-qwen3-8b-shape-ftv3-seqsplit-{T}")
+    elif args.config == 5 and args.context is not None:
         cfg = dict(cfg, T=args.context, name=f"{cfg['name']}-ctx{args.context}")
     if args.config == 5:
         if args.impl == "reference":

@@ -143,17 +143,18 @@ __device__ __forceinline__ int64_t warp_of_chunk(int64_t x, int64_t tc, int nwar
 struct Len {
   int64_t T, tc;
   int cpu, small;
+  int nw;  // warps with work: min(grid warps, tc), so every one of them owns at least one chunk
 };
 
 // Warp owning chunk x, first chunk of warp w, unit of chunk x -- in 32-bit
 // arithmetic when the plan is small enough (the usual case).
 __device__ __forceinline__ int warp_of(const Params &p, const Len &L, int64_t x) {
-  if (L.small) return (int)(((uint32_t)x + 1u) * (uint32_t)p.nwarps + (uint32_t)L.tc - 1u) / (uint32_t)L.tc - 1;
-  return (int)warp_of_chunk(x, L.tc, p.nwarps);
+  if (L.small) return (int)(((uint32_t)x + 1u) * (uint32_t)L.nw + (uint32_t)L.tc - 1u) / (uint32_t)L.tc - 1;
+  return (int)warp_of_chunk(x, L.tc, L.nw);
 }
 __device__ __forceinline__ int64_t first_chunk(const Params &p, const Len &L, int w) {
-  if (L.small) return (int64_t)(((uint32_t)w * (uint32_t)L.tc) / (uint32_t)p.nwarps);
-  return (int64_t)w * L.tc / p.nwarps;
+  if (L.small) return (int64_t)(((uint32_t)w * (uint32_t)L.tc) / (uint32_t)L.nw);
+  return (int64_t)w * L.tc / L.nw;
 }
 __device__ __forceinline__ int unit_of(const Len &L, int64_t x) {
   if (L.small) return (int)((uint32_t)x / (uint32_t)L.cpu);
@@ -716,7 +717,7 @@ __device__ void finish_units(const Params &p, const Len &L, unsigned char *smem)
   const int G = p.gqa;
   const int *fin_unit = (const int *)(smem + p.off_fin);
   const int w0 = blockIdx.x * p.nwc;
-  const int w1 = min(w0 + p.nwc, p.nwarps) - 1;
+  const int w1 = min(w0 + p.nwc, L.nw) - 1;
   const int64_t cfirst = first_chunk(p, L, w0), clast = first_chunk(p, L, w1 + 1);
   if (clast <= cfirst) return;  // no chunks in this CTA's range (short cache, large grid)
   const int u0 = unit_of(L, cfirst), nu = unit_of(L, clast - 1) - u0 + 1;
@@ -942,14 +943,18 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const __grid_
     }
     L.cpu = (int)((L.T + p.C - 1) / p.C);
     L.tc = (int64_t)p.cv.B * p.cv.H * L.cpu;
-    L.small = (uint64_t)L.tc * (uint64_t)(p.nwarps + 1) < (1ull << 32);
+    // A launch sized for a longer length (graph replays) has more warps than
+    // this length has chunks: only the first tc of them take work, one chunk
+    // or more each; every merge counts only those warps.
+    L.nw = (int)(L.tc < (int64_t)p.nwarps ? (L.tc > 0 ? L.tc : 1) : (int64_t)p.nwarps);
+    L.small = (uint64_t)L.tc * (uint64_t)(L.nw + 1) < (1ull << 32);
     s_len = L;
   }
   __syncthreads();
   const Len L = s_len;
   if (L.T == 0) return;  // no length: nothing written (the error word says why)
   const int wg = blockIdx.x * nwc + warp;
-  if (wg < p.nwarps) warp_main<G>(p, L, smem, bar, wg, warp, lane);
+  if (wg < L.nw) warp_main<G>(p, L, smem, bar, wg, warp, lane);
   __syncthreads();
   finish_units(p, L, smem);
   if (p.len_rw) {  // every CTA has read the old length: the last one to finish advances it

@@ -21,6 +21,12 @@ length lives on the device and advances inside the kernel, the RoPE position
 is a device counter, and the sampled ids are written back in-graph, so a
 replay needs no host synchronisation.
 
+Two multi-GPU modes, each inside the captured step: kv-head tensor
+parallelism (``tp_group``: NCCL all-reduce after o_proj and the down
+projection) and a sequence split of one long context (``seq_group``: each
+rank's range of every layer's cache, partial attention with log-sum-exp,
+NCCL all-gather, cq_lse_merge).
+
 ``fill_context`` writes a synthetic context (seeded random K/V per layer,
 encoded by the cache's own append kernel) instead of running a 32k-token
 prompt through the model; a decode step's cost does not depend on the
@@ -70,15 +76,29 @@ class Qwen3StyleDecoder:
     greedy decode step for ``batch`` sequences of up to ``max_len`` tokens."""
 
     def __init__(self, cfg: DecoderConfig, batch: int, max_len: int, cache_kwargs: dict | None = None,
-                 device="cuda", dtype=torch.bfloat16, seed: int = 0, tp_group=None):
+                 device="cuda", dtype=torch.bfloat16, seed: int = 0, tp_group=None, seq_group=None):
         """``tp_group``: a torch.distributed (NCCL) group over which the layers
         are tensor-parallel by kv-head: this rank keeps kv_heads/N kv-heads
         with their query heads and ffn/N of each FFN; the o_proj and down
         projections end in an all-reduce.  The full weights are drawn the same
-        way on every rank and sliced, so any N gives the same model."""
+        way on every rank and sliced, so any N gives the same model.
+
+        ``seq_group``: a group over which every sequence's context is split
+        by token ranges (``distributed.shard_bounds``): each rank keeps the
+        whole model and, per layer, the compressed cache of its range; the
+        last rank owns the tail and encodes the new tokens.  Each layer's
+        attention is a partial (output, log-sum-exp) per rank, all-gathered
+        (NCCL) and merged by cq_lse_merge, all inside the captured step."""
         self.cfg, self.B, self.max_len = cfg, batch, max_len
         self.device, self.dtype = torch.device(device), dtype
-        self.group = tp_group
+        if tp_group is not None and seq_group is not None:
+            raise ValueError("tensor parallel and sequence split are separate modes")
+        self.group, self.seq_group = tp_group, seq_group
+        self.seq_rank, self.seq_world = 0, 1
+        if seq_group is not None:
+            import torch.distributed as dist
+            self.seq_rank, self.seq_world = dist.get_rank(seq_group), dist.get_world_size(seq_group)
+        self.tail = self.seq_rank == self.seq_world - 1  # this rank encodes the new tokens
         if tp_group is not None:
             import torch.distributed as dist
             self.rank, self.world = dist.get_rank(tp_group), dist.get_world_size(tp_group)
@@ -129,16 +149,26 @@ class Qwen3StyleDecoder:
 
     # -- context ---------------------------------------------------------------
     def fill_context(self, T0: int, chunk: int = 4096, seed: int = 1) -> None:
-        """Encode a synthetic T0-token context into every layer's cache."""
+        """Encode a synthetic T0-token context into every layer's cache (under
+        a sequence split, this rank's token range of it)."""
         c = self.cfg
         g = torch.Generator(device=self.device).manual_seed(seed)
         h0, h1 = self.rank * self.kv_heads, (self.rank + 1) * self.kv_heads  # this rank's kv-heads
+        t_lo, t_hi = 0, T0
+        if self.seq_group is not None:
+            from .distributed import shard_bounds
+            c0 = self.layers[0]["cache"]
+            t_lo, t_hi = shard_bounds(T0, self.seq_world, c0.stride_k, c0.stride_v)[self.seq_rank]
+            if t_hi <= t_lo:
+                raise ValueError("sequence split: every rank needs a non-empty token range")
         for L in self.layers:
             for t in range(0, T0, chunk):
                 n = min(chunk, T0 - t)
                 k = torch.randn((self.B, c.kv_heads, n, c.head_dim), generator=g, device=self.device).to(self.dtype)
                 v = torch.randn((self.B, c.kv_heads, n, c.head_dim), generator=g, device=self.device).to(self.dtype)
-                L["cache"].update_and_fetch(k[:, h0:h1].contiguous(), v[:, h0:h1].contiguous())
+                a, b = max(t, t_lo) - t, min(t + n, t_hi) - t  # the part of this chunk in the rank's range
+                if a < b:
+                    L["cache"].update_and_fetch(k[:, h0:h1, a:b].contiguous(), v[:, h0:h1, a:b].contiguous())
         self.pos.fill_(T0)
         self._prepare_attention()
 
@@ -158,18 +188,48 @@ class Qwen3StyleDecoder:
             need_max = max(need_max, need.value)
         self.workspace = torch.zeros(max(1, (need_max + 3) // 4), dtype=torch.float32, device=self.device)
         self.attn_out = torch.empty((self.B, self.heads, self.cfg.head_dim), dtype=self.dtype, device=self.device)
+        if self.seq_group is not None:  # this rank's partial and every rank's, gathered
+            W, D = self.seq_world, self.cfg.head_dim
+            self.o_part = torch.empty((self.B, self.heads, D), dtype=torch.float32, device=self.device)
+            self.lse_part = torch.empty((self.B, self.heads), dtype=torch.float32, device=self.device)
+            self.o_all = torch.empty((W, self.B, self.heads, D), dtype=torch.float32, device=self.device)
+            self.lse_all = torch.empty((W, self.B, self.heads), dtype=torch.float32, device=self.device)
 
     # -- one decode step --------------------------------------------------------
     def _attention(self, L: dict, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
         """Encode this step's k/v [B, Hkv, D] into the layer's cache and attend
-        q [B, Hq, D] over everything cached: one cq_decode_step_at launch."""
+        q [B, Hq, D] over everything cached: one cq_decode_step_at launch.
+        Under a sequence split the tail rank does that and the others attend
+        their fixed range (cq_attention_at); each writes an fp32 partial with
+        its log-sum-exp, and the gathered partials are merged (cq_lse_merge)."""
+        lib = _lib.lib()
         ks, vs, qs = k.stride(), v.stride(), q.stride()
-        _lib.check(_lib.lib().cq_decode_step_at(
-            ctypes.byref(L["desc"]), k.data_ptr(), ks[0], ks[1], v.data_ptr(), vs[0], vs[1], cq_dtype(k),
-            L["len"].data_ptr(), self.max_len, q.data_ptr(), cq_dtype(q), self.heads, qs[0], qs[1],
-            1.0 / math.sqrt(self.cfg.head_dim), self.attn_out.data_ptr(), cq_dtype(self.attn_out), None,
-            self.workspace.data_ptr(), self.workspace.numel() * 4, stream_ptr(self.device)), "decoder")
+        scale = 1.0 / math.sqrt(self.cfg.head_dim)
+        split = self.seq_group is not None
+        out = self.o_part if split else self.attn_out
+        lse = self.lse_part.data_ptr() if split else None
+        if self.tail:
+            _lib.check(lib.cq_decode_step_at(
+                ctypes.byref(L["desc"]), k.data_ptr(), ks[0], ks[1], v.data_ptr(), vs[0], vs[1], cq_dtype(k),
+                L["len"].data_ptr(), self.max_len, q.data_ptr(), cq_dtype(q), self.heads, qs[0], qs[1], scale,
+                out.data_ptr(), cq_dtype(out), lse, self.workspace.data_ptr(), self.workspace.numel() * 4,
+                stream_ptr(self.device)), "decoder")
+        else:
+            _lib.check(lib.cq_attention_at(
+                ctypes.byref(L["desc"]), L["len"].data_ptr(), self.max_len, q.data_ptr(), cq_dtype(q), self.heads,
+                qs[0], qs[1], scale, out.data_ptr(), cq_dtype(out), lse, self.workspace.data_ptr(),
+                self.workspace.numel() * 4, stream_ptr(self.device)), "decoder")
+        if split:
+            self._merge_partials()
         return self.attn_out
+
+    def _merge_partials(self) -> None:
+        import torch.distributed as dist
+        dist.all_gather_into_tensor(self.o_all, self.o_part, group=self.seq_group)
+        dist.all_gather_into_tensor(self.lse_all, self.lse_part, group=self.seq_group)
+        _lib.check(_lib.lib().cq_lse_merge(self.lse_all.data_ptr(), self.o_all.data_ptr(), self.seq_world,
+                                           self.B * self.heads, self.cfg.head_dim, self.attn_out.data_ptr(),
+                                           cq_dtype(self.attn_out), stream_ptr(self.device)), "decoder")
 
     def _norm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         y = torch.empty_like(x)
@@ -229,6 +289,10 @@ class Qwen3StyleDecoder:
         (torch.zeros((self.B, self.ffn), device=self.device, dtype=self.dtype) @ L0["wdown"].t())
         if self.world > 1:  # the communicator exists before the capture
             self._reduce(torch.zeros((self.B, c.hidden), device=self.device, dtype=self.dtype))
+        if self.seq_group is not None:
+            self.o_part.zero_()
+            self.lse_part.zero_()
+            self._merge_partials()
         q = torch.zeros((self.B, self.heads, c.head_dim), device=self.device, dtype=self.dtype)
         qs = q.stride()
         _lib.check(lib.cq_attention_at(ctypes.byref(L0["desc"]), L0["len"].data_ptr(), self.max_len, q.data_ptr(),
@@ -250,8 +314,9 @@ class Qwen3StyleDecoder:
             raise ValueError(f"decode past max_len {self.max_len}")
         for _ in range(steps):
             self.graph.replay()
-        for L in self.layers:
-            L["cache"].offset += steps
+        if self.tail:  # under a sequence split only the tail rank's caches grow
+            for L in self.layers:
+                L["cache"].offset += steps
         return self.logits
 
     def bytes_per_step(self) -> int:

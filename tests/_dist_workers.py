@@ -141,3 +141,47 @@ def tp_decoder_worker(rank, world, port, steps, queue):
         queue.put((rank, rels, None))
     except Exception as e:
         queue.put((rank, None, repr(e)))
+
+
+def seq_decoder_worker(rank, world, port, steps, queue):
+    """Sequence-split decoder on `world` GPUs (each rank a token range of the
+    context, partials merged by log-sum-exp) against the same decoder on one
+    GPU (rank 0): same weights, context and input ids every step."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        from chronoquant_mlx_b200.decoder import DecoderConfig, Qwen3StyleDecoder
+        cfg = DecoderConfig(layers=2, hidden=512, heads=8, kv_heads=2, head_dim=128, ffn=1024, vocab=1000)
+        kw = dict(stride_k=64, stride_v=32, delta_bits_v=3, dead_zone_v=0.05)
+        sp = Qwen3StyleDecoder(cfg, 1, 1100, kw, device=dev, seed=9, seq_group=dist.group.WORLD)
+        sp.fill_context(1000)
+        sp.capture()
+        one = None
+        if rank == 0:
+            one = Qwen3StyleDecoder(cfg, 1, 1100, kw, device=dev, seed=9)
+            one.fill_context(1000)
+            one.capture()
+        rels, lens = [], []
+        for s in range(steps):
+            ids = torch.tensor([3 + 7 * s], device=dev)
+            sp.ids.copy_(ids)
+            ls = sp.decode(1).float().clone()
+            if one is not None:
+                one.ids.copy_(ids)
+                lo = one.decode(1).float()
+                rels.append(float((ls - lo).norm() / lo.norm()))
+        torch.cuda.synchronize()
+        lens = [int(L["len"][0]) for L in sp.layers]
+        del sp.graph  # graphs holding NCCL work go before the process group
+        if one is not None:
+            del one.graph
+        dist.barrier()
+        dist.destroy_process_group()
+        queue.put((rank, rels, lens, None))
+    except Exception as e:
+        queue.put((rank, None, None, repr(e)))
