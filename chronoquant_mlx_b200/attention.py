@@ -22,6 +22,7 @@ import ctypes
 import torch
 
 from . import _lib
+from .trace import traced
 from ._tensors import cq_dtype, require_cuda, stream_ptr
 
 
@@ -84,6 +85,7 @@ def _run(desc, T, queries, scale, mask, causal, out, ws_holder, device):
     return out
 
 
+@traced("cq.sdpa")
 def chronoquant_sdpa(queries: torch.Tensor, keys, values, cache, scale: float, mask=None):
     """Attention of ``queries`` [B, Hq, Tq, D] (fp16/bf16 CUDA) over everything
     ``cache`` holds, including tokens just appended by ``update_and_fetch``.
@@ -109,6 +111,7 @@ def chronoquant_sdpa(queries: torch.Tensor, keys, values, cache, scale: float, m
     return _run(desc, T, queries, scale, mask, causal, out, cache.workspace, queries.device)
 
 
+@traced("cq.sdpa_lse")
 def chronoquant_sdpa_with_lse(queries: torch.Tensor, cache, scale: float, causal: bool = True):
     """Decode/prefill attention returning (out fp32 [B, Hq, Tq, D], lse fp32
     [B, Hq, Tq]) for merging sequence shards (``distributed.py``).  ``causal``

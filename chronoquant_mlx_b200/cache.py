@@ -26,6 +26,7 @@ import math
 import torch
 
 from . import _lib
+from .trace import traced
 from ._tensors import cq_dtype, require_cuda, stream_ptr
 from .base import create_causal_mask
 from .codec import ChronoQuantCodec
@@ -238,6 +239,7 @@ class ChronoQuantCache:
         return self._store
 
     # -- cache protocol -----------------------------------------------------------
+    @traced("cq.append")
     def update_and_fetch(self, keys: torch.Tensor, values: torch.Tensor):
         """Encode new K/V tokens into the cache and return the inputs unchanged
         (cache.py:198-215).  keys/values: [B, H_kv, S, head_dim] fp16/bf16 CUDA."""
@@ -382,6 +384,7 @@ class ChronoQuantCache:
                    "reconstruct_history")
         return out
 
+    @traced("cq.reconstruct")
     def reconstruct_history(self):
         """Decoded fp16 K and V [B, H, offset, D], rounded as the reference's
         fallback (fp16 code*scale, then fp16 anchor + that)."""

@@ -33,6 +33,7 @@ import math
 import torch
 
 from . import _lib
+from .trace import traced
 from ._tensors import cq_dtype, require_cuda, stream_ptr
 
 
@@ -67,6 +68,7 @@ def local_partials(queries: torch.Tensor, cache, scale: float, tail: bool):
     return chronoquant_sdpa_with_lse(queries, cache, scale, causal=tail or Tq == 1)
 
 
+@traced("cq.seq_exchange")
 def exchange_partials(o: torch.Tensor, lse: torch.Tensor, group=None):
     """All-gather every rank's partials: (o [world, ...], lse [world, ...]),
     rank-major.  Every rank calls it with the same shapes, in the same order."""
@@ -79,6 +81,7 @@ def exchange_partials(o: torch.Tensor, lse: torch.Tensor, group=None):
     return torch.stack(os_), torch.stack(ls_)
 
 
+@traced("cq.seq_merge")
 def merge_partials(o_all: torch.Tensor, lse_all: torch.Tensor, out_dtype=torch.float32) -> torch.Tensor:
     """Combine gathered partials on the device with cq_lse_merge (CUDA only:
     there is no host fallback).  o_all: [parts, ..., D] fp32, lse_all:

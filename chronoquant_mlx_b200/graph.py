@@ -35,6 +35,7 @@ import ctypes
 import torch
 
 from . import _lib
+from .trace import traced
 from ._tensors import cq_dtype, require_cuda, stream_ptr
 
 
@@ -113,6 +114,7 @@ class DecodeGraph:
                                               self.workspace.data_ptr(), self.workspace.numel() * 4,
                                               stream_ptr(q.device)), "DecodeGraph")
 
+    @traced("cq.graph_replay")
     def replay(self) -> torch.Tensor:
         """Run one step on the current contents of ``keys``/``values``/``queries``."""
         c = self.cache
@@ -127,6 +129,7 @@ class DecodeGraph:
         self._synced = c.offset
         return self.out
 
+    @traced("cq.graph_step")
     def step(self, keys: torch.Tensor, values: torch.Tensor, queries: torch.Tensor) -> torch.Tensor:
         """Encode ``keys``/``values`` [B, H, S, D] and attend ``queries``
         [B, Hq, 1, D]; returns the graph's output buffer [B, Hq, 1, D]."""
