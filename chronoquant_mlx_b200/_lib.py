@@ -12,7 +12,9 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libchronoquant_b200.so")
+# CQ_CHECKS=1 at import selects the bounds-checked debug build (build.py --checks)
+CHECKS = os.environ.get("CQ_CHECKS", "0") not in ("", "0")
+LIB_PATH = os.path.join(_HERE, "libchronoquant_b200_checks.so" if CHECKS else "libchronoquant_b200.so")
 
 CQ_OK = 0
 CQ_ERR_INVALID = -1
@@ -120,8 +122,9 @@ def lib():
         if _lib is None:
             if not os.path.exists(LIB_PATH):
                 raise ImportError(
-                    f"libchronoquant_b200.so not found at {LIB_PATH}; build it with "
-                    "`python -m chronoquant_mlx_b200.build` (nvcc, sm_100a). There is no CPU fallback.")
+                    f"{os.path.basename(LIB_PATH)} not found at {LIB_PATH}; build it with "
+                    f"`python -m chronoquant_mlx_b200.build{' --checks' if CHECKS else ''}` (nvcc, sm_100a). "
+                    "There is no CPU fallback.")
             _lib = _declare(ctypes.CDLL(LIB_PATH))
     return _lib
 

@@ -290,6 +290,8 @@ int launch_split_combine(const float *ws_m, const float *ws_l, const float *ws_o
   return check_launch("combine_kernel");
 }
 
+int read_bounds_error_attention(int clear) { return read_bounds_error_here(clear); }
+
 }  // namespace cq
 
 using namespace cq;

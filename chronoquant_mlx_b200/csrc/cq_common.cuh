@@ -123,10 +123,66 @@ __host__ __device__ inline void nibble_pos(int d, int D, int order, int &word, i
   }
 }
 
+// Debug builds (-DCQ_CHECKS, libchronoquant_b200_checks.so): every page
+// lookup is checked against the block-table row and the page pool.  A bad
+// index is recorded in this translation unit's word (device error
+// CQ_DEV_ERR_BOUNDS) and replaced by page 0, so the access stays inside the
+// pool and the host reads an error code instead of a fault.  Release builds
+// compile the checks out.
+constexpr int CQ_DEV_ERR_BOUNDS = 7;
+#ifdef CQ_CHECKS
+static __device__ int g_bounds_error;
+__device__ __forceinline__ bool bounds_ok(bool ok) {
+  if (!ok) atomicExch(&g_bounds_error, CQ_DEV_ERR_BOUNDS);
+  return ok;
+}
+#endif
+
 // Physical page of logical page lp of sequence b.
 __device__ __forceinline__ int64_t page_of(const CacheView &cv, int b, int64_t lp) {
+#ifdef CQ_CHECKS
+  if (!bounds_ok(b >= 0 && b < cv.B && lp >= 0 && lp < cv.max_pages)) return 0;
+  const int64_t pg =
+      cv.block_table ? (int64_t)cv.block_table[(int64_t)b * cv.max_pages + lp] : (int64_t)b * cv.max_pages + lp;
+  return bounds_ok(pg >= 0 && pg < cv.n_pages) ? pg : 0;
+#else
   return cv.block_table ? (int64_t)cv.block_table[(int64_t)b * cv.max_pages + lp] : (int64_t)b * cv.max_pages + lp;
+#endif
 }
+
+// The same for a cache known to have a block table (the decode kernel's layout).
+__device__ __forceinline__ int64_t table_page(const CacheView &cv, int b, int64_t lp) {
+#ifdef CQ_CHECKS
+  if (!bounds_ok(b >= 0 && b < cv.B && lp >= 0 && lp < cv.max_pages)) return 0;
+  const int64_t pg = (int64_t)cv.block_table[(int64_t)b * cv.max_pages + lp];
+  return bounds_ok(pg >= 0 && pg < cv.n_pages) ? pg : 0;
+#else
+  return (int64_t)cv.block_table[(int64_t)b * cv.max_pages + lp];
+#endif
+}
+
+// Host: this translation unit's bounds-error word (0 in release builds).
+static inline int read_bounds_error_here(int clear) {
+#ifdef CQ_CHECKS
+  int v = 0;
+  cudaMemcpyFromSymbol(&v, g_bounds_error, sizeof(int));
+  if (clear && v) {
+    const int z = 0;
+    cudaMemcpyToSymbol(g_bounds_error, &z, sizeof(int));
+  }
+  return v;
+#else
+  (void)clear;
+  return 0;
+#endif
+}
+
+// Per translation unit readers, combined by cq_device_error.
+int read_bounds_error_encode(int clear);
+int read_bounds_error_layout(int clear);
+int read_bounds_error_attention(int clear);
+int read_bounds_error_prefill(int clear);
+int read_bounds_error_decode(int clear);
 
 // Locations of token t (absolute) of (b, h) in component comp.
 struct TokLoc {

@@ -617,7 +617,7 @@ __device__ __forceinline__ void warp_main(const Params &p, const Len &L, unsigne
   cc.init(p, L, first, last);
   ci = cc;
   for (int s = 0; s < kNS && ci.valid(); ++s) {
-    const int64_t pg = p.cv.block_table[(int64_t)ci.b * p.cv.max_pages + ci.lp];
+    const int64_t pg = table_page(p.cv, ci.b, ci.lp);
     issue_chunk<G>(p, region_a + s * G::SLOT, &bar[s], ci, pg, lane);
     ci.next(p, L);
   }
@@ -633,7 +633,7 @@ __device__ __forceinline__ void warp_main(const Params &p, const Len &L, unsigne
   uint32_t ph = 0;
   for (; cc.valid(); cc.next(p, L)) {
     // page of the next chunk to issue, loaded early so its latency hides under this chunk
-    const int64_t pg_next = ci.valid() ? (int64_t)p.cv.block_table[(int64_t)ci.b * p.cv.max_pages + ci.lp] : 0;
+    const int64_t pg_next = ci.valid() ? table_page(p.cv, ci.b, ci.lp) : 0;
     if (cc.unit != cur_unit) {
       if (cur_unit >= 0) {
         const int a = cur_unit - u0;
@@ -656,7 +656,7 @@ __device__ __forceinline__ void warp_main(const Params &p, const Len &L, unsigne
     const uint32_t sa = region_a + s * G::SLOT;
     const int nvalid = cc.nvalid(p, L);
     if (p.fuse && cc.cu == L.cpu - 1) {  // this step's new token lies in the unit's last chunk
-      const int64_t pg = p.cv.block_table[(int64_t)cc.b * p.cv.max_pages + cc.lp];
+      const int64_t pg = table_page(p.cv, cc.b, cc.lp);
       unsigned char *slot = region + s * G::SLOT;
       if (p.x_dtype == CQ_BF16)
         encode_new_token<G, CQ_BF16>(p, slot, pg, cc.b, cc.h, L.T - 1, (uint32_t *)qa, lane);
@@ -1228,6 +1228,8 @@ int read_fast_error(int clear) {
   return v;
 }
 
+int read_bounds_error_decode(int clear) { return read_bounds_error_here(clear); }
+
 }  // namespace cq
 
 extern "C" int cq_decode_chunk_tokens(int32_t stride_k, int32_t stride_v, int32_t page_tokens, int32_t head_dim) {
@@ -1242,7 +1244,13 @@ int read_append_error(int clear);
 extern "C" int cq_device_error(int *code, int clear) {
   if (!code) return cq::set_error(CQ_ERR_INVALID, "cq_device_error: code is null");
   const int a = cq::read_fast_error(clear), b = cq::read_append_error(clear), c = cq::read_prefill_error(clear);
-  *code = a ? a : (b ? b : c);
+  int d = 0;  // bounds checks of a CQ_CHECKS build
+  for (int (*rd)(int) : {cq::read_bounds_error_encode, cq::read_bounds_error_layout, cq::read_bounds_error_attention,
+                         cq::read_bounds_error_prefill, cq::read_bounds_error_decode}) {
+    const int v = rd(clear);
+    if (!d) d = v;
+  }
+  *code = a ? a : (b ? b : (c ? c : d));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cq::set_error(CQ_ERR_CUDA, cudaGetErrorString(e));
   return CQ_OK;

@@ -182,6 +182,8 @@ int read_append_error(int clear) {
   return v;
 }
 
+int read_bounds_error_encode(int clear) { return read_bounds_error_here(clear); }
+
 }  // namespace cq
 
 using namespace cq;

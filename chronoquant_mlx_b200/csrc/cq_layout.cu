@@ -184,6 +184,8 @@ __global__ void unpack_kernel(const uint32_t *packed, int64_t rows, int dim, int
 
 inline unsigned blocks_for(int64_t threads, int bs) { return (unsigned)((threads + bs - 1) / bs); }
 
+int read_bounds_error_layout(int clear) { return read_bounds_error_here(clear); }
+
 }  // namespace cq
 
 using namespace cq;

@@ -777,4 +777,6 @@ int read_prefill_error(int clear) {
   return v;
 }
 
+int read_bounds_error_prefill(int clear) { return read_bounds_error_here(clear); }
+
 }  // namespace cq

@@ -126,8 +126,9 @@ int cq_decode_chunk_tokens(int32_t stride_k, int32_t stride_v, int32_t page_toke
  * wait), 4 = a device-resident length outside [1, mapped tokens] (attention
  * wrote nothing), 5 = a device-resident append past the mapped pages (append
  * wrote nothing), 6 = the tensor-core query-chunk kernel gave up on a bounded
- * wait (its output is incomplete).  Synchronises the device; clear != 0
- * resets the word. */
+ * wait (its output is incomplete), 7 = (debug build with -DCQ_CHECKS only) a
+ * page index outside the block-table row or the page pool, replaced by page 0
+ * (results invalid).  Synchronises the device; clear != 0 resets the word. */
 int cq_device_error(int *code, int clear);
 
 /* Encode S new tokens at absolute positions t0..t0+S-1 for K and V in one
