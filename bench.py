@@ -2,7 +2,7 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5] [--impl ours|reference]
 
-Workload (BASELINE config 2 by default): one attention layer, B=8 sequences,
+Workload (bench config 2 by default): one attention layer, B=8 sequences,
 32 query / 8 KV heads, head_dim 128, a compressed context of T=16384 tokens
 per sequence in the Standard preset (stride_k 32, stride_v 8, INT4 residuals,
 dead zone 0).  One step = append one new token per sequence (the streaming
@@ -769,7 +769,7 @@ def run_reference_prefill(args, cfg):
 
 def fp16_decode_baseline(cfg, T, device, reps):
     """Decode attention of the same shape over an uncompressed fp16 cache (the
-    FlashDecoding baseline of BASELINE config 3): flash_attn_with_kvcache when
+    FlashDecoding baseline of bench config 3): flash_attn_with_kvcache when
     it runs on this GPU, else torch SDPA with GQA.  Times `reps` calls back to
     back with CUDA events; reports bytes per token and kv-head (K+V) and the
     fp16 cache read rate."""

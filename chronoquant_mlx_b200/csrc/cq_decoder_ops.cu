@@ -1,5 +1,5 @@
 // cq_decoder_ops.cu -- the elementwise steps of the decoder that drives the
-// compressed cache end to end, fused so that a decode
+// compressed cache end to end (bench config 5), fused so that a decode
 // step is a handful of kernels per layer instead of dozens of small ones:
 //
 //   cq_rmsnorm        y = bf16(x * rsqrt(mean(x^2) + eps)) * w        (per row)

@@ -1,7 +1,7 @@
 """A random-init Qwen3-style decoder that drives the compressed cache end to
 end: greedy decode where every step is one CUDA-graph replay.
 
-BASELINE config 5 asks for "decode tokens/s at 32k ctx" on a decoder of the
+Bench config 5 (bench.py --config 5) measures "decode tokens/s at 32k ctx" on a decoder of the
 Qwen3-8B shape (36 layers, hidden 4096, 32 q / 8 kv heads, head_dim 128,
 SwiGLU 12288, vocab 151936, RMSNorm, RoPE theta 1e6, bf16 weights N(0, 0.02))
 with Full-Throttle V3 caches.  The reference reaches this through mlx_lm
@@ -223,10 +223,14 @@ class Qwen3StyleDecoder:
             self._merge_partials()
         return self.attn_out
 
-    def _merge_partials(self) -> None:
+    def _gather_partials(self) -> None:
+        """Every rank's partial into o_all / lse_all (rank-major)."""
         import torch.distributed as dist
         dist.all_gather_into_tensor(self.o_all, self.o_part, group=self.seq_group)
         dist.all_gather_into_tensor(self.lse_all, self.lse_part, group=self.seq_group)
+
+    def _merge_partials(self) -> None:
+        self._gather_partials()
         _lib.check(_lib.lib().cq_lse_merge(self.lse_all.data_ptr(), self.o_all.data_ptr(), self.seq_world,
                                            self.B * self.heads, self.cfg.head_dim, self.attn_out.data_ptr(),
                                            cq_dtype(self.attn_out), stream_ptr(self.device)), "decoder")

@@ -295,7 +295,7 @@ int cq_attention_static_scratch(const cq_paged_cache *cache, int64_t T, const vo
 
 /* Decoder helpers (no reference counterpart: the reference gets its model
  * from mlx_lm).  The elementwise steps of the decoder that drives the cache
- * end to end, each one kernel, rounding as the unfused
+ * end to end (bench config 5), each one kernel, rounding as the unfused
  * torch ops do:
  *   cq_rmsnorm       y[r] = dtype(x[r] * rsqrt(mean(x[r]^2) + eps)) * w, rows of dim;
  *   cq_qk_norm_rope  per head of fused QKV rows [batch][(Hq + 2 Hkv) * 128] (row

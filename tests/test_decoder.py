@@ -1,4 +1,4 @@
-"""The end-to-end decoder (BASELINE config 5's shape, here shrunk): one greedy
+"""The end-to-end decoder (bench config 5's shape, here shrunk): one greedy
 decode step as a CUDA-graph replay, through the compressed caches.
 
 Bars: graph replays give logits within 1e-3 relative (L2) of the same decoder
@@ -182,3 +182,66 @@ def test_sequence_split_matches_one_gpu():
         assert err is None, err
     assert len(res[0][1]) == 3 and all(r < 1e-2 for r in res[0][1]), res[0][1]
     assert res[0][2] == [512, 512] and res[1][2] == [491, 491], (res[0][2], res[1][2])
+
+
+def test_sequence_split_on_one_gpu_matches_unsplit():
+    """The sequence-split decoder's logic on one GPU: two decoders hold the
+    two token ranges of one 1000-token context (rank 0: tokens 0-511; the
+    tail: 512-999 and every new token) and step eagerly in two host threads.
+    A host exchange stands in for the NCCL all-gather; the device merge
+    (cq_lse_merge) is the real one.  Logits within 1e-2 relative of the
+    unsplit decoder with the same weights, context and ids; only the tail's
+    caches grow."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    import threading
+    import types
+    dev = torch.device("cuda")
+    kw = dict(stride_k=64, stride_v=32, delta_bits_v=3, dead_zone_v=0.05)
+    bar = threading.Barrier(2, timeout=120)
+    parts = [None, None]
+
+    def gather(dec):
+        torch.cuda.synchronize()
+        parts[dec.seq_rank] = (dec.o_part.clone(), dec.lse_part.clone())
+        bar.wait()
+        for r, (o, lse) in enumerate(parts):
+            dec.o_all[r].copy_(o)
+            dec.lse_all[r].copy_(lse)
+        torch.cuda.synchronize()
+        bar.wait()  # both have read before either writes the next layer's partial
+
+    ranks = []
+    for r in range(2):
+        d = Qwen3StyleDecoder(CFG, 1, 1100, kw, device=dev, seed=9)
+        d.seq_group, d.seq_rank, d.seq_world, d.tail = object(), r, 2, r == 1
+        d._gather_partials = types.MethodType(gather, d)
+        d.fill_context(1000)
+        ranks.append(d)
+    one = Qwen3StyleDecoder(CFG, 1, 1100, kw, device=dev, seed=9)
+    one.fill_context(1000)
+    assert [d.layers[0]["cache"].offset for d in ranks] == [512, 488]
+    for s in range(3):
+        ids = torch.tensor([3 + 7 * s], device=dev)
+        for d in (*ranks, one):
+            d.ids.copy_(ids)
+        out, errs = [None, None], []
+
+        def run(r):
+            try:
+                out[r] = ranks[r].step_eager().float().clone()
+            except Exception as e:  # reported below
+                errs.append(repr(e))
+                bar.abort()
+        th = [threading.Thread(target=run, args=(r,)) for r in range(2)]
+        for t in th:
+            t.start()
+        for t in th:
+            t.join(timeout=300)
+        assert not errs, errs
+        lo = one.step_eager().float()
+        for r in range(2):
+            rel = float((out[r] - lo).norm() / lo.norm())
+            assert rel < 1e-2, (s, r, rel)
+    torch.cuda.synchronize()
+    assert [int(d.layers[0]["len"][0]) for d in ranks] == [512, 491]

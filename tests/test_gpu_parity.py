@@ -358,7 +358,7 @@ def test_prefill_chunk_causal_vs_exact():
 
 
 def test_full_size_config2_properties():
-    """BASELINE config 2 sizes (B8 Hkv8 Hq32 T16384): encode of two rows
+    """bench config 2 sizes (B8 Hkv8 Hq32 T16384): encode of two rows
     bit-exact against the oracle, export->import idempotent, decode of two
     heads against exact attention."""
     from chronoquant_mlx_b200 import ChronoQuantCache, chronoquant_sdpa

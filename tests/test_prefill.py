@@ -11,7 +11,7 @@ update_and_fetch) and compares ``chronoquant_sdpa`` with
 * exact float64 attention on the same fp16 values: max-abs 1e-3 / relative
   5e-3 (the kernel rounds only the softmax weights, to fp16).
 
-The full-size case (65536 cached tokens + a 2048-token
+The full-size case (bench config 4: 65536 cached tokens + a 2048-token
 chunk, 32 query heads over 8 kv-heads) checks sampled rows against exact
 float64 attention on the device's fp16 reconstruction, which other tests pin
 bit-exact to the oracle."""
@@ -127,7 +127,7 @@ def test_prefill_lse_and_strided_queries():
 
 
 def test_prefill_config4_sampled_rows():
-    """B1 Hq32 Hkv8 D128, 65536 compressed tokens then a
+    """bench config 4: B1 Hq32 Hkv8 D128, 65536 compressed tokens then a
     2048-token chunk (Standard strides), causal.  Sampled rows (query-tile
     edges, first/last tokens, every GQA position) against exact float64
     attention on the device's fp16 reconstruction."""
