@@ -22,7 +22,7 @@ CQ_ERR_UNSUPPORTED = -2
 CQ_ERR_CUDA = -3
 CQ_ERR_WORKSPACE = -4
 
-CQ_ABI_VERSION = 2  # CQ_ABI_VERSION of include/chronoquant_b200.h
+CQ_ABI_VERSION = 3  # CQ_ABI_VERSION of include/chronoquant_b200.h
 CQ_F16, CQ_BF16, CQ_F32 = 0, 1, 2
 CQ_ORDER_NATURAL, CQ_ORDER_MMA = 0, 1
 CQ_SCALE_BY_PFRAME, CQ_SCALE_BY_TOKEN = 0, 1
@@ -30,7 +30,7 @@ CQ_STATIC_SCRATCH_BYTES = 8 << 20  # cq_attention_static_scratch's fixed per-dev
 
 EXPORTED = [
     "cq_abi_version", "cq_last_error", "cq_device_error", "cq_append", "cq_attention", "cq_attention_workspace",
-    "cq_attention_masked", "cq_lse_merge", "cq_reconstruct", "cq_export_state", "cq_import_state", "cq_quantize_delta",
+    "cq_attention_masked", "cq_lse_merge", "cq_lse_merge_packed", "cq_reconstruct", "cq_export_state", "cq_import_state", "cq_quantize_delta",
     "cq_dequantize_delta", "cq_pack_int4", "cq_unpack_int4", "cq_sdpa_reference_layout",
     "cq_sdpa_reference_layout_workspace", "cq_attention_static_scratch", "cq_decode_chunk_tokens",
     "cq_append_at", "cq_attention_at", "cq_decode_step_at", "cq_prefill_prepare", "cq_prefill_attend",
@@ -83,6 +83,7 @@ def _declare(lib):
         "cq_attention_masked": [C, I64, P, ctypes.c_int, I32, I32, I64, I64, I64, F, P, ctypes.c_int, ctypes.c_int,
                                 I64, I64, I64, I64, P, ctypes.c_int, P, SZ, I32, P],
         "cq_lse_merge": [P, P, I32, I64, I32, P, ctypes.c_int, P],
+        "cq_lse_merge_packed": [P, I32, I64, I32, P, ctypes.c_int, P],
         "cq_reconstruct": [C, ctypes.c_int, I64, P, ctypes.c_int, P],
         "cq_export_state": [C, ctypes.c_int, I64, P, P, P, P],
         "cq_import_state": [C, ctypes.c_int, I64, P, P, P, P],

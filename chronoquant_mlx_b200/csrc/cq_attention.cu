@@ -198,24 +198,26 @@ __global__ void combine_kernel(const float *ws_m, const float *ws_l, const float
 }
 
 // out[r] = sum_i exp(lse_i - L) o_i over sequence shards (one warp per row).
-__global__ void lse_merge_kernel(const float *lse, const float *o, int n_parts, int64_t rows, int D, void *out,
-                                 int out_dtype) {
+// Part i's log-sum-exp of row r at lse[i * lse_ps + r], its output at
+// o[i * o_ps + r * D + d] (separate arrays, or one packed buffer per part).
+__global__ void lse_merge_kernel(const float *lse, const float *o, int n_parts, int64_t rows, int D, int64_t lse_ps,
+                                 int64_t o_ps, void *out, int out_dtype) {
   const int64_t row = ((int64_t)blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= rows) return;
   float M = -INFINITY;
-  for (int i = 0; i < n_parts; ++i) M = fmaxf(M, lse[(int64_t)i * rows + row]);
+  for (int i = 0; i < n_parts; ++i) M = fmaxf(M, lse[(int64_t)i * lse_ps + row]);
   float W = 0.f;
   for (int i = 0; i < n_parts; ++i) {
-    float x = lse[(int64_t)i * rows + row];
+    float x = lse[(int64_t)i * lse_ps + row];
     if (x != -INFINITY) W += expf(x - M);
   }
   const float inv = (W > 0.f) ? 1.f / W : 0.f;
   for (int d = lane; d < D; d += 32) {
     float v = 0.f;
     for (int i = 0; i < n_parts; ++i) {
-      float x = lse[(int64_t)i * rows + row];
-      if (x != -INFINITY) v += expf(x - M) * o[((int64_t)i * rows + row) * D + d];
+      float x = lse[(int64_t)i * lse_ps + row];
+      if (x != -INFINITY) v += expf(x - M) * o[(int64_t)i * o_ps + row * D + d];
     }
     store_from_float(out, row * D + d, v * inv, out_dtype);
   }
@@ -417,7 +419,22 @@ extern "C" int cq_lse_merge(const float *lse, const float *o, int32_t n_parts, i
              "cq_lse_merge: bad out dtype");
   if (rows == 0) return CQ_OK;
   int64_t blocks = (rows * 32 + 255) / 256;
-  lse_merge_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(lse, o, n_parts, rows, dim, out, out_dtype);
+  lse_merge_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(lse, o, n_parts, rows, dim, rows, rows * dim,
+                                                                       out, out_dtype);
+  return check_launch("lse_merge_kernel");
+}
+
+extern "C" int cq_lse_merge_packed(const float *parts, int32_t n_parts, int64_t rows, int32_t dim, void *out,
+                                   int out_dtype, void *stream) {
+  CQ_REQUIRE(parts && out, CQ_ERR_INVALID, "cq_lse_merge_packed: null pointer");
+  CQ_REQUIRE(n_parts >= 1 && rows >= 0 && dim >= 1, CQ_ERR_INVALID, "cq_lse_merge_packed: bad sizes");
+  CQ_REQUIRE(out_dtype == CQ_F16 || out_dtype == CQ_BF16 || out_dtype == CQ_F32, CQ_ERR_UNSUPPORTED,
+             "cq_lse_merge_packed: bad out dtype");
+  if (rows == 0) return CQ_OK;
+  const int64_t ps = rows * ((int64_t)dim + 1);  // floats per part: [rows][dim] outputs, then [rows] lse
+  int64_t blocks = (rows * 32 + 255) / 256;
+  lse_merge_kernel<<<(unsigned)blocks, 256, 0, (cudaStream_t)stream>>>(parts + rows * dim, parts, n_parts, rows, dim,
+                                                                       ps, ps, out, out_dtype);
   return check_launch("lse_merge_kernel");
 }
 

@@ -25,7 +25,7 @@ Two multi-GPU modes, each inside the captured step: kv-head tensor
 parallelism (``tp_group``: NCCL all-reduce after o_proj and the down
 projection) and a sequence split of one long context (``seq_group``: each
 rank's range of every layer's cache, partial attention with log-sum-exp,
-NCCL all-gather, cq_lse_merge).
+one NCCL all-gather per layer, cq_lse_merge_packed).
 
 ``fill_context`` writes a synthetic context (seeded random K/V per layer,
 encoded by the cache's own append kernel) instead of running a 32k-token
@@ -88,7 +88,7 @@ class Qwen3StyleDecoder:
         whole model and, per layer, the compressed cache of its range; the
         last rank owns the tail and encodes the new tokens.  Each layer's
         attention is a partial (output, log-sum-exp) per rank, all-gathered
-        (NCCL) and merged by cq_lse_merge, all inside the captured step."""
+        (NCCL) and merged by cq_lse_merge_packed, all inside the captured step."""
         self.cfg, self.B, self.max_len = cfg, batch, max_len
         self.device, self.dtype = torch.device(device), dtype
         if tp_group is not None and seq_group is not None:
@@ -188,12 +188,14 @@ class Qwen3StyleDecoder:
             need_max = max(need_max, need.value)
         self.workspace = torch.zeros(max(1, (need_max + 3) // 4), dtype=torch.float32, device=self.device)
         self.attn_out = torch.empty((self.B, self.heads, self.cfg.head_dim), dtype=self.dtype, device=self.device)
-        if self.seq_group is not None:  # this rank's partial and every rank's, gathered
-            W, D = self.seq_world, self.cfg.head_dim
-            self.o_part = torch.empty((self.B, self.heads, D), dtype=torch.float32, device=self.device)
-            self.lse_part = torch.empty((self.B, self.heads), dtype=torch.float32, device=self.device)
-            self.o_all = torch.empty((W, self.B, self.heads, D), dtype=torch.float32, device=self.device)
-            self.lse_all = torch.empty((W, self.B, self.heads), dtype=torch.float32, device=self.device)
+        if self.seq_group is not None:
+            # this rank's partial packed as [outputs B*Hq*D | log-sum-exp B*Hq] (one all-gather per
+            # layer), and every rank's, gathered rank-major
+            W, D, R = self.seq_world, self.cfg.head_dim, self.B * self.heads
+            self.part = torch.empty(R * (D + 1), dtype=torch.float32, device=self.device)
+            self.o_part = self.part[:R * D].view(self.B, self.heads, D)
+            self.lse_part = self.part[R * D:].view(self.B, self.heads)
+            self.parts_all = torch.empty((W, R * (D + 1)), dtype=torch.float32, device=self.device)
 
     # -- one decode step --------------------------------------------------------
     def _attention(self, L: dict, q: torch.Tensor, k: torch.Tensor, v: torch.Tensor) -> torch.Tensor:
@@ -201,7 +203,7 @@ class Qwen3StyleDecoder:
         q [B, Hq, D] over everything cached: one cq_decode_step_at launch.
         Under a sequence split the tail rank does that and the others attend
         their fixed range (cq_attention_at); each writes an fp32 partial with
-        its log-sum-exp, and the gathered partials are merged (cq_lse_merge)."""
+        its log-sum-exp, and the gathered partials are merged (cq_lse_merge_packed)."""
         lib = _lib.lib()
         ks, vs, qs = k.stride(), v.stride(), q.stride()
         scale = 1.0 / math.sqrt(self.cfg.head_dim)
@@ -224,16 +226,15 @@ class Qwen3StyleDecoder:
         return self.attn_out
 
     def _gather_partials(self) -> None:
-        """Every rank's partial into o_all / lse_all (rank-major)."""
+        """Every rank's packed partial into parts_all (rank-major)."""
         import torch.distributed as dist
-        dist.all_gather_into_tensor(self.o_all, self.o_part, group=self.seq_group)
-        dist.all_gather_into_tensor(self.lse_all, self.lse_part, group=self.seq_group)
+        dist.all_gather_into_tensor(self.parts_all, self.part, group=self.seq_group)
 
     def _merge_partials(self) -> None:
         self._gather_partials()
-        _lib.check(_lib.lib().cq_lse_merge(self.lse_all.data_ptr(), self.o_all.data_ptr(), self.seq_world,
-                                           self.B * self.heads, self.cfg.head_dim, self.attn_out.data_ptr(),
-                                           cq_dtype(self.attn_out), stream_ptr(self.device)), "decoder")
+        _lib.check(_lib.lib().cq_lse_merge_packed(self.parts_all.data_ptr(), self.seq_world, self.B * self.heads,
+                                                  self.cfg.head_dim, self.attn_out.data_ptr(),
+                                                  cq_dtype(self.attn_out), stream_ptr(self.device)), "decoder")
 
     def _norm(self, x: torch.Tensor, w: torch.Tensor) -> torch.Tensor:
         y = torch.empty_like(x)

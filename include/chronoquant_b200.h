@@ -21,7 +21,7 @@
  *                                                          -> cq_sdpa_reference_layout
  *   attention.py:23-74 chronoquant_sdpa (fused + fallback) -> cq_attention
  *   attention.py:61-74 fallback branch (query chunks)     -> cq_prefill_prepare / cq_prefill_attend
- *   (no reference counterpart) seq-split partial merge     -> cq_lse_merge
+ *   (no reference counterpart) seq-split partial merge     -> cq_lse_merge, cq_lse_merge_packed
  */
 #ifndef CHRONOQUANT_B200_H
 #define CHRONOQUANT_B200_H
@@ -33,7 +33,7 @@
 extern "C" {
 #endif
 
-#define CQ_ABI_VERSION 2
+#define CQ_ABI_VERSION 3
 
 /* status codes */
 #define CQ_OK 0
@@ -231,6 +231,13 @@ int cq_attention_masked(const cq_paged_cache *cache, int64_t T, const void *q, i
  * L = logsumexp_i lse_i; out: [rows][dim] in out_dtype. */
 int cq_lse_merge(const float *lse, const float *o, int32_t n_parts, int64_t rows, int32_t dim, void *out,
                  int out_dtype, void *stream);
+
+/* cq_lse_merge over partials packed one buffer per part, as a single
+ * all-gather delivers them: parts fp32 [n_parts][rows*dim + rows], each part
+ * its outputs [rows][dim] followed by its log-sum-exp [rows].  No reference
+ * counterpart (the reference runs on one device). */
+int cq_lse_merge_packed(const float *parts, int32_t n_parts, int64_t rows, int32_t dim, void *out, int out_dtype,
+                        void *stream);
 
 /* Decoded fp16 history of one component (0=K, 1=V) for tokens 0..T-1:
  * out [batch][kv_heads][T][head_dim].  mode 0 rounds like the reference's

@@ -39,10 +39,10 @@ def test_binding_covers_header():
 
 
 def test_abi_version():
-    assert _lib.lib().cq_abi_version() == _lib.CQ_ABI_VERSION == 2
+    assert _lib.lib().cq_abi_version() == _lib.CQ_ABI_VERSION == 3
     hdr = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))), "include",
                             "chronoquant_b200.h")).read()
-    assert "#define CQ_ABI_VERSION 2" in hdr
+    assert "#define CQ_ABI_VERSION 3" in hdr
 
 
 def test_graft_build_entry():

@@ -189,7 +189,7 @@ def test_sequence_split_on_one_gpu_matches_unsplit():
     two token ranges of one 1000-token context (rank 0: tokens 0-511; the
     tail: 512-999 and every new token) and step eagerly in two host threads.
     A host exchange stands in for the NCCL all-gather; the device merge
-    (cq_lse_merge) is the real one.  Logits within 1e-2 relative of the
+    (cq_lse_merge_packed) is the real one.  Logits within 1e-2 relative of the
     unsplit decoder with the same weights, context and ids; only the tail's
     caches grow."""
     if not torch.cuda.is_available():
@@ -203,11 +203,10 @@ def test_sequence_split_on_one_gpu_matches_unsplit():
 
     def gather(dec):
         torch.cuda.synchronize()
-        parts[dec.seq_rank] = (dec.o_part.clone(), dec.lse_part.clone())
+        parts[dec.seq_rank] = dec.part.clone()
         bar.wait()
-        for r, (o, lse) in enumerate(parts):
-            dec.o_all[r].copy_(o)
-            dec.lse_all[r].copy_(lse)
+        for r, part in enumerate(parts):
+            dec.parts_all[r].copy_(part)
         torch.cuda.synchronize()
         bar.wait()  # both have read before either writes the next layer's partial
 

@@ -411,6 +411,12 @@ def test_sequence_shard_merge():
     rows = of.numel() // 128
     _lib.check(_lib.lib().cq_lse_merge(lse.data_ptr(), o.data_ptr(), 2, rows, 128, out.data_ptr(), _lib.CQ_F32,
                                        torch.cuda.current_stream().cuda_stream))
+    # the same partials packed one buffer per part ([outputs | lse], as one all-gather delivers them)
+    packed = torch.cat([o.reshape(2, rows * 128), lse.reshape(2, rows)], dim=1).contiguous()
+    out_p = torch.empty_like(of)
+    _lib.check(_lib.lib().cq_lse_merge_packed(packed.data_ptr(), 2, rows, 128, out_p.data_ptr(), _lib.CQ_F32,
+                                              torch.cuda.current_stream().cuda_stream))
+    assert torch.equal(out_p, out)
     # shard b re-anchors at its first token, so compare against the exact union of both shards' decodes
     oa_ = O.OracleCache(stride_k=32, stride_v=8)
     oa_.update_and_fetch(K[:, :, :512], V[:, :, :512])
