@@ -942,6 +942,8 @@ def main():
     cfg = CONFIGS[args.config]
     if args.config == 4 and args.context is not None:
         cfg = dict(cfg, T=args.context, name=f"{cfg['name']}-ctx{args.context}")
+    if args.tp and args.seqsplit:
+        ap.error("--tp and --seqsplit are separate config-5 modes; pick one")
     if args.config == 5 and args.seqsplit:
         T = args.context or 524288
         cfg = dict(cfg, B=1, T=T, name=f"cfg5-qwen3-8b-shape-ftv3-seqsplit-{T}")
