@@ -60,6 +60,8 @@ class DecoderConfig:
 
 
 def _rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
+    """RMSNorm as the torch expression that cq_rmsnorm reproduces (the tests'
+    reference for the fused kernel)."""
     xf = x.float()
     return (xf * torch.rsqrt(xf.pow(2).mean(-1, keepdim=True) + eps)).to(x.dtype) * w
 

@@ -9,7 +9,12 @@ cache.py:131-160), fed the same input ids.  The 2e-2 covers bf16 activations
 carrying per-layer differences through the network to the logits, plus the
 decode kernel dequantising in fp32 (the fused path, kernels.py:152-155) where
 the reference rounds the reconstruction to fp16; the attention kernels' own
-bars are in test_gpu_parity.py."""
+bars are in test_gpu_parity.py.
+
+Also here: the fused elementwise kernels against the torch expressions they
+replace (one ulp), and the multi-GPU modes against the one-GPU decoder with
+the same weights -- kv-head tensor parallel and the sequence split on two
+GPUs, and the sequence split's logic on one GPU with a host exchange."""
 
 import math
 
