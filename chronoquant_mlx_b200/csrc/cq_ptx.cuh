@@ -171,30 +171,11 @@ __device__ __forceinline__ uint32_t lop3_and_or(uint32_t a, uint32_t b, uint32_t
 __device__ __forceinline__ __half2 u2h2(uint32_t x) { return *reinterpret_cast<__half2 *>(&x); }
 __device__ __forceinline__ uint32_t h22u(__half2 x) { return *reinterpret_cast<uint32_t *>(&x); }
 
-// The 16-bit halves of x hold nibble lanes; OR-ing a nibble n into the
-// mantissa of fp16 1024.0 (0x6400) gives exactly 1024 + n (or 1024 + 16n for
-// the high nibble of a byte).  Subtracting the bias leaves the signed code
-// n - 8 exactly.  Returns codes of nibbles {0,1,2,3} of each 16-bit half:
-//   out[0] = (nib0(lo), nib0(hi)), out[1] = nib1, out[2] = nib2, out[3] = nib3.
-__device__ __forceinline__ void nibbles_to_half2(uint32_t x, uint32_t (&out)[4]) {
-  const uint32_t MAGIC = 0x64006400u;
-  const __half2 BIAS_LO = u2h2(0x64086408u);   // 1032
-  const __half2 SCALE_HI = u2h2(0x2c002c00u);  // 1/16
-  const __half2 BIAS_HI = u2h2(0xd480d480u);   // -72
-  uint32_t lo0 = lop3_and_or(x, 0x000f000fu, MAGIC);
-  uint32_t hi0 = lop3_and_or(x, 0x00f000f0u, MAGIC);
-  uint32_t x8 = x >> 8;
-  uint32_t lo1 = lop3_and_or(x8, 0x000f000fu, MAGIC);
-  uint32_t hi1 = lop3_and_or(x8, 0x00f000f0u, MAGIC);
-  out[0] = h22u(__hsub2(u2h2(lo0), BIAS_LO));
-  out[1] = h22u(__hfma2(u2h2(hi0), SCALE_HI, BIAS_HI));
-  out[2] = h22u(__hsub2(u2h2(lo1), BIAS_LO));
-  out[3] = h22u(__hfma2(u2h2(hi1), SCALE_HI, BIAS_HI));
-}
-
-// Codes of nibbles_to_half2 plus 72, with no arithmetic: each nibble is moved
-// to bits 4-7 of its 16-bit half under the fp16 exponent of 64 (0x5400, one
-// unit in the last place = 1/16), which reads as 64 + n = (n - 8) + 72.
+// The 16-bit halves of x each hold four nibble lanes (stored value n = code +
+// 8).  Returns, for nibbles {0,1,2,3} of each half, the fp16 pair
+// (half lo, half hi) of code + 72 with no arithmetic: each nibble is moved to
+// bits 4-7 of its half under the fp16 exponent of 64 (0x5400, one unit in the
+// last place = 1/16), which reads as 64 + n = (n - 8) + 72.
 __device__ __forceinline__ void nibbles_to_half2_64(uint32_t x, uint32_t (&out)[4]) {
   const uint32_t MAGIC = 0x54005400u;
   out[0] = lop3_and_or(x << 4, 0x00f000f0u, MAGIC);
@@ -204,9 +185,9 @@ __device__ __forceinline__ void nibbles_to_half2_64(uint32_t x, uint32_t (&out)[
 }
 constexpr uint32_t HALF2_72 = 0x54805480u;  // (72, 72)
 
-// Raw form of nibbles_to_half2 without the bias removal: out[0], out[2] hold
-// 1024 + n (nibbles 0 and 2 of each 16-bit half), out[1], out[3] hold 1024 + 16n
-// (nibbles 1 and 3).  A dot product with these values equals the dot product
+// Raw nibble values under the fp16 exponent of 1024 (0x6400, one unit in the
+// last place = 1): out[0], out[2] hold 1024 + n (nibbles 0 and 2 of each
+// 16-bit half), out[1], out[3] hold 1024 + 16n (nibbles 1 and 3).  A dot product with these values equals the dot product
 // with the codes n - 8 plus a constant that does not depend on the codes; the
 // caller removes that constant (computed from the all-8 nibble pattern).
 __device__ __forceinline__ void nibbles_to_half2_raw(uint32_t x, uint32_t (&out)[4]) {
