@@ -6,12 +6,15 @@
 // math.  Here a warp streams chunks (32 or 64 tokens) of one (sequence,
 // kv-head) unit and serves every query head of the GQA group from one read.
 //
-// Every warp runs its own copy pipeline: two private shared-memory slots, each
-// filled by one 1-D bulk-async copy (the TMA engine) of a chunk block -- the
-// chunk's K/V anchors, code rows and per-token scales, stored contiguously by
-// the cache -- completion counted on the slot's mbarrier.  A warp waits only
-// for its own copies, never for other warps, and refills a slot as soon as it
-// has consumed it.  The kernel is instantiated per (stride_k, stride_v) pair,
+// Every warp runs its own copy pipeline of 1-D bulk-async copies (the TMA
+// engine) of chunk blocks -- the chunk's K/V anchors, code rows and per-token
+// scales, stored contiguously by the cache -- completion counted on
+// mbarriers.  For 32-token chunks a warp owns two slots, each filled with a
+// whole block.  For 64-token chunks a warp owns one K buffer and one V buffer:
+// the block's K part is refilled (with the next chunk's) as soon as the
+// chunk's scores are done, while the V part is still being consumed, so a
+// warp holds one block of buffers instead of two and 16 warps fit in shared
+// memory.  A warp waits only for its own copies, never for other warps.  The kernel is instantiated per (stride_k, stride_v) pair,
 // so the chunk geometry and every shared-memory offset are compile-time
 // constants.  Per chunk:
 //
@@ -69,7 +72,7 @@ constexpr int ERR_TIMEOUT_FULL = 1;
 constexpr int ERR_LENGTH = 4;  // a device-resident length outside [1, mapped tokens]
 constexpr int kQaBytes = 16 * 8 * 4;  // per-warp q.anchor table: 16 anchors x 8 heads, fp32
 constexpr int kQnBytes = 8 * 32 * 8;  // per-warp natural-order query fragments
-constexpr int kNS = 2;                // copy slots per warp
+constexpr int kBarsPerWarp = 4;       // a warp's copy barriers (at most two slots, or one K and one V buffer)
 
 constexpr int cx_log2(int x) { return x <= 1 ? 0 : 1 + cx_log2(x >> 1); }
 constexpr int cx_up16(int x) { return (x + 15) & ~15; }
@@ -93,7 +96,19 @@ struct Geo {
   static constexpr int O_CD1 = cx_up16(O_KF1 + AV * HD * 2);
   static constexpr int O_SC1 = cx_up16(O_CD1 + (C - AV) * (HD / 2));
   static constexpr int SLOT = cx_up16(O_SC1 + C * 2);
+  // 32-token chunks: two slots per warp, each filled with a whole block.
+  // 64-token chunks (SPLIT): the K part [0, O_KF1) and the V part [O_KF1,
+  // SLOT) of a block go to separate buffers, one of each per warp; the K
+  // buffer is refilled as soon as the chunk's scores are done and the V
+  // buffer once its output is accumulated, so a warp needs one block of
+  // buffers instead of two and 16 warps fit in shared memory.
+  static constexpr bool SPLIT = C == 64;
+  static constexpr int KB = O_KF1, VB = SLOT - O_KF1;
+  static constexpr int V_CD = O_CD1 - O_KF1, V_SC = O_SC1 - O_KF1;  // offsets inside the V part
+  static constexpr int NSK = SPLIT ? 1 : 2;                         // buffer pairs (SPLIT) or slots
+  static constexpr int BUF = NSK * SLOT;                            // a warp's copy buffers
   static_assert(SK >= 16 && SV >= 8 && C <= 64 && AK <= 16, "geometry outside the kernel's range");
+  static_assert(KB % 16 == 0 && VB % 16 == 0, "bulk copies need 16-byte sizes");
 };
 
 struct Params {
@@ -210,16 +225,19 @@ struct Cursor {
   }
 };
 
-// One bulk copy of a chunk's block (page `pg`) into `slot`, counted on
-// `bar`, issued by lane 0.  The whole block is copied even for the last,
-// partial chunk of a unit: the bytes past its valid tokens are masked.
-template <class G>
-__device__ __forceinline__ void issue_chunk(const Params &p, uint32_t slot, uint64_t *bar, const Cursor &c,
-                                            int64_t pg, int lane) {
+// One bulk copy of one part of a chunk's block (page `pg`): the K part
+// (PART 0: K anchors, codes, scales), the V part (PART 1) or the whole block
+// (PART 2) into `buf`, counted on `bar`, issued by lane 0.  The whole part is
+// copied even for the last, partial chunk of a unit: the bytes past its valid
+// tokens are masked.
+template <class G, int PART>
+__device__ __forceinline__ void issue_part(const Params &p, uint32_t buf, uint64_t *bar, const Cursor &c, int64_t pg,
+                                           int lane) {
   if (lane != 0) return;
-  ptx::mbar_arrive_expect_tx(bar, (uint32_t)G::SLOT);
-  const char *src = p.blk + (pg * p.cv.H + c.h) * p.phs + (int64_t)c.j * G::SLOT;
-  ptx::bulk_g2s_a(slot, src, (uint32_t)G::SLOT, bar);
+  constexpr int off = PART == 1 ? G::O_KF1 : 0, bytes = PART == 2 ? G::SLOT : (PART ? G::VB : G::KB);
+  ptx::mbar_arrive_expect_tx(bar, (uint32_t)bytes);
+  const char *src = p.blk + (pg * p.cv.H + c.h) * p.phs + (int64_t)c.j * G::SLOT + off;
+  ptx::bulk_g2s_a(buf, src, (uint32_t)bytes, bar);
 }
 
 struct QFrag {
@@ -302,32 +320,40 @@ __device__ __forceinline__ void reset(WarpState &st) {
     for (int j = 0; j < 4; ++j) st.o[i][j] = 0.f;
 }
 
-// Per-lane shared-memory byte addresses into one slot, derived from the slot
-// address and the lane.  Code rows are stored in P-frame order; the row of
-// chunk-local token x is x - x/stride - 1 (an I-frame lands on the previous
-// row, read harmlessly with scale 0).  For a 16-token tile at tb with
-// stride_k >= 16 the K rows of tokens tb + x are (tb - tb/stride_k) + x - 1.
-struct LaneAddr {
-  uint32_t cdK;   // K code row of token g (tile base 0), word group t
+// Per-lane shared-memory byte addresses into a K part.  Code rows are stored
+// in P-frame order; the row of chunk-local token x is x - x/stride - 1 (an
+// I-frame lands on the previous row, read harmlessly with scale 0).  For a
+// 16-token tile at tb with stride_k >= 16 the K rows of tokens tb + x are
+// (tb - tb/stride_k) + x - 1.
+struct KAddr {
+  uint32_t cdK;  // K code row of token g (tile base 0), word group t
+  uint32_t scK;  // K scale of token g
+  uint32_t qa;   // q.anchor table, heads 2t, 2t+1
+  template <class G>
+  __device__ __forceinline__ KAddr(G, uint32_t kb, uint32_t qa_base, int lane) {
+    const int g = lane >> 2, t = lane & 3;
+    cdK = kb + G::O_CD0 + (g - 1) * 64 + t * 16;
+    scK = kb + G::O_SC0 + g * 2;
+    qa = qa_base + t * 8;
+  }
+};
+
+// Per-lane shared-memory byte addresses into a V part.
+struct VAddr {
   uint32_t cdV;   // V code row of token 2t (tile base 0), words 2g, 2g+1
-  uint32_t scK;   // K scale of token g
   uint32_t scV;   // V scales of tokens 2t, 2t+1 (one 32-bit word)
   uint32_t kfV;   // V anchor row of this lane's ldmatrix row (tile 0)
   uint32_t kfV0;  // V anchor row 0, same column half
-  uint32_t qa;    // q.anchor table, heads 2t, 2t+1
   int dv8;        // V rows between tokens 2t and 2t+8
   template <class G>
-  __device__ __forceinline__ LaneAddr(G, uint32_t sa, uint32_t qa_base, int lane) {
+  __device__ __forceinline__ VAddr(G, uint32_t vb, int lane) {
     const int g = lane >> 2, t = lane & 3, mi = lane >> 3;
     constexpr bool v8 = G::LSV == 3;
-    cdK = sa + G::O_CD0 + (g - 1) * 64 + t * 16;
-    cdV = sa + G::O_CD1 + (2 * t - 1) * 64 + g * 8;
+    cdV = vb + G::V_CD + (2 * t - 1) * 64 + g * 8;
     dv8 = v8 ? 7 : 8;
-    scK = sa + G::O_SC0 + g * 2;
-    scV = sa + G::O_SC1 + t * 4;
-    kfV0 = sa + G::O_KF1 + ((mi & 1) ? 16 : 0);
+    scV = vb + G::V_SC + t * 4;
+    kfV0 = vb + ((mi & 1) ? 16 : 0);
     kfV = kfV0 + ((v8 ? (mi >> 1) : 0) * (HD * 2));
-    qa = qa_base + t * 8;
   }
 };
 
@@ -337,11 +363,15 @@ __device__ __forceinline__ float lds_half_as_float(uint32_t a) {
   return __half2float(__ushort_as_half(v));
 }
 
-// Two 16-token tiles starting at chunk-local token t0.
+// Scores of the two 16-token tiles at chunk-local token t0 and their softmax
+// update; P of the two tiles in the MMA B-operand layout (a lane holds tokens
+// 2t, 2t+1 (and 2t+8, 2t+9) of head g) into bp[0..1].  When the running max
+// moves, the output state is rescaled and the function returns true with the
+// factor for head g in `fh` (for the P of the chunk's earlier groups).
 template <class G, bool MASK>
-__device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, const QFrag &f, int t0, int nvalid,
-                                              int lane) {
-  constexpr int lsk = G::LSK, lsv = G::LSV;
+__device__ __forceinline__ bool k_group(WarpState &st, const KAddr &A, const QFrag &f, int t0, int nvalid, int lane,
+                                        uint2 (&bp)[2], __half2 &fh) {
+  constexpr int lsk = G::LSK;
   constexpr int NT = 2;
   const int g = lane >> 2;
   float s[NT][4];
@@ -373,12 +403,13 @@ __device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, 
     s[tile][2] = fmaf(sk1, ca[2] + cb[2], qa.x);
     s[tile][3] = fmaf(sk1, ca[3] + cb[3], qa.y);
     if (MASK) {
-      // tokens past the end: score -inf (their slot bytes are stale)
+      // tokens past the end: score -inf (their buffer bytes are stale)
       if (tb + g >= nvalid) s[tile][0] = s[tile][1] = -INFINITY;
       if (tb + g + 8 >= nvalid) s[tile][2] = s[tile][3] = -INFINITY;
     }
   }
-  // ---------------- online softmax over the chunk (base 2), lazy rescale
+  // ---------------- online softmax (base 2), lazy rescale
+  bool moved = false;
   {
     float mx0 = fmaxf(s[0][0], s[0][2]), mx1 = fmaxf(s[0][1], s[0][3]);
 #pragma unroll
@@ -411,12 +442,14 @@ __device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, 
         st.o[i][2] *= f0;
         st.o[i][3] *= f1;
       }
+      // the factor of head g (the operand layout's head) for the chunk's earlier P
+      const float a = __shfl_sync(0xffffffffu, f0, g >> 1), b = __shfl_sync(0xffffffffu, f1, g >> 1);
+      fh = __float2half2_rn((g & 1) ? b : a);
+      moved = true;
     }
   }
-  // ---------------- P V per tile
 #pragma unroll
   for (int tile = 0; tile < NT; ++tile) {
-    const int tb = t0 + tile * 16;
     // masked scores are -inf and the running max is finite here: ex2(-inf) = 0
     const float p0 = fast_exp2(s[tile][0] - st.m[0]);
     const float p1 = fast_exp2(s[tile][1] - st.m[1]);
@@ -424,65 +457,71 @@ __device__ __forceinline__ void process_group(WarpState &st, const LaneAddr &A, 
     const float p3 = fast_exp2(s[tile][3] - st.m[1]);
     st.l[0] += p0 + p2;
     st.l[1] += p1 + p3;
-    // P (anchor term) and P' = P * scale_v (code term) as B operands: in the
-    // operand layout a lane holds tokens 2t, 2t+1 (and 2t+8, 2t+9) of head g,
-    // whose V scales are one 32-bit word each
-    const uint32_t bP0 = ptx::movmatrix_trans(ptx::pack_half2(p0, p1));
-    const uint32_t bP1 = ptx::movmatrix_trans(ptx::pack_half2(p2, p3));
-    uint32_t sw0 = ptx::lds_u32(A.scV + tb * 2), sw1 = ptx::lds_u32(A.scV + (tb + 8) * 2);
+    bp[tile] = make_uint2(ptx::movmatrix_trans(ptx::pack_half2(p0, p1)), ptx::movmatrix_trans(ptx::pack_half2(p2, p3)));
+  }
+  return moved;
+}
+
+// Output of the 16-token tile at chunk-local token tb with its P (bP0, bP1).
+template <class G, bool MASK>
+__device__ __forceinline__ void v_tile(WarpState &st, const VAddr &A, int tb, uint32_t bP0, uint32_t bP1, int nvalid,
+                                       int lane) {
+  constexpr int lsv = G::LSV;
+  // P' = P * scale_v: in the operand layout a lane holds tokens 2t, 2t+1 (and
+  // 2t+8, 2t+9) of head g, whose V scales are one 32-bit word each
+  uint32_t sw0 = ptx::lds_u32(A.scV + tb * 2), sw1 = ptx::lds_u32(A.scV + (tb + 8) * 2);
+  if (MASK) {
+    // scales past the end are stale bytes (P is 0 there, but 0 * inf is not)
+    const int t2 = tb + 2 * (lane & 3);
+    if (t2 >= nvalid) sw0 = 0u;
+    else if (t2 + 1 >= nvalid) sw0 &= 0xffffu;
+    if (t2 + 8 >= nvalid) sw1 = 0u;
+    else if (t2 + 9 >= nvalid) sw1 &= 0xffffu;
+  }
+  const uint32_t bS0 = ptx::h22u(__hmul2(ptx::u2h2(bP0), ptx::u2h2(sw0)));
+  const uint32_t bS1 = ptx::h22u(__hmul2(ptx::u2h2(bP1), ptx::u2h2(sw1)));
+  // V anchors: O += A_v^T P, ldmatrix.trans gathers each token's anchor row
+  {
+    uint32_t base = A.kfV + (uint32_t)((tb >> lsv) * (HD * 2));
     if (MASK) {
-      // scales past the end are stale bytes (P is 0 there, but 0 * inf is not)
-      const int t2 = tb + 2 * (lane & 3);
-      if (t2 >= nvalid) sw0 = 0u;
-      else if (t2 + 1 >= nvalid) sw0 &= 0xffffu;
-      if (t2 + 8 >= nvalid) sw1 = 0u;
-      else if (t2 + 9 >= nvalid) sw1 &= 0xffffu;
+      // rows past the copied anchors hold stale bytes: use anchor 0 (P is 0 there)
+      const int mi = lane >> 3, r = lane & 7;
+      if (tb + r + ((mi & 2) ? 8 : 0) >= nvalid) base = A.kfV0;
     }
-    const uint32_t bS0 = ptx::h22u(__hmul2(ptx::u2h2(bP0), ptx::u2h2(sw0)));
-    const uint32_t bS1 = ptx::h22u(__hmul2(ptx::u2h2(bP1), ptx::u2h2(sw1)));
-    // V anchors: O += A_v^T P, ldmatrix.trans gathers each token's anchor row
-    {
-      uint32_t base = A.kfV + (uint32_t)((tb >> lsv) * (HD * 2));
-      if (MASK) {
-        // rows past the copied anchors hold stale bytes: use anchor 0 (P is 0 there)
-        const int mi = lane >> 3, r = lane & 7;
-        if (tb + r + ((mi & 2) ? 8 : 0) >= nvalid) base = A.kfV0;
-      }
 #pragma unroll
-      for (int i = 0; i < 8; ++i) {
-        uint32_t a0, a1, a2, a3;
-        ptx::ldmatrix_x4_trans(a0, a1, a2, a3, base + i * 32);
-        ptx::mma_f16_16816(st.o[i], a0, a1, a2, a3, bP0, bP1);
+    for (int i = 0; i < 8; ++i) {
+      uint32_t a0, a1, a2, a3;
+      ptx::ldmatrix_x4_trans(a0, a1, a2, a3, base + i * 32);
+      ptx::mma_f16_16816(st.o[i], a0, a1, a2, a3, bP0, bP1);
+    }
+  }
+  // V codes: O += C_v^T P'  (tokens 2t,2t+1 | 2t+8,2t+9; words 2g, 2g+1)
+  {
+    // V rows of tokens tb+2t, +1, +8, +9 (stride 8: the I-frame at tb+8 sits between)
+    const uint32_t rv = A.cdV + (uint32_t)((tb - (tb >> lsv)) * 64);
+    const uint32_t rv8 = rv + (uint32_t)A.dv8 * 64;
+    const uint2 va = ptx::lds_u64(rv);
+    const uint2 vb = ptx::lds_u64(rv + 64);
+    const uint2 vc = ptx::lds_u64(rv8);
+    const uint2 vd = ptx::lds_u64(rv8 + 64);
+#pragma unroll
+    for (int q = 0; q < 2; ++q) {
+      const uint32_t wa = q ? va.y : va.x, wb = q ? vb.y : vb.x;
+      const uint32_t wc = q ? vc.y : vc.x, wd = q ? vd.y : vd.x;
+#pragma unroll
+      for (int half = 0; half < 2; ++half) {
+        const uint32_t sel = half ? 0x7632u : 0x5410u;
+        uint32_t xa[4], xc[4];
+        ptx::nibbles_to_half2_64(__byte_perm(wa, wb, sel), xa);  // nibbles 4*half + 0..3 of tokens (a, b)
+        ptx::nibbles_to_half2_64(__byte_perm(wc, wd, sel), xc);
+        // nibble j of word q <-> m-tile 4q + j/2, row g (+8 when j is odd)
+        const int i0 = 4 * q + 2 * half;
+        ptx::mma_f16_16816(st.o[i0], xa[0], xa[1], xc[0], xc[1], bS0, bS1);
+        ptx::mma_f16_16816(st.o[i0 + 1], xa[2], xa[3], xc[2], xc[3], bS0, bS1);
       }
     }
-    // V codes: O += C_v^T P'  (tokens 2t,2t+1 | 2t+8,2t+9; words 2g, 2g+1)
-    {
-      // V rows of tokens tb+2t, +1, +8, +9 (stride 8: the I-frame at tb+8 sits between)
-      const uint32_t rv = A.cdV + (uint32_t)((tb - (tb >> lsv)) * 64);
-      const uint32_t rv8 = rv + (uint32_t)A.dv8 * 64;
-      const uint2 va = ptx::lds_u64(rv);
-      const uint2 vb = ptx::lds_u64(rv + 64);
-      const uint2 vc = ptx::lds_u64(rv8);
-      const uint2 vd = ptx::lds_u64(rv8 + 64);
-#pragma unroll
-      for (int q = 0; q < 2; ++q) {
-        const uint32_t wa = q ? va.y : va.x, wb = q ? vb.y : vb.x;
-        const uint32_t wc = q ? vc.y : vc.x, wd = q ? vd.y : vd.x;
-#pragma unroll
-        for (int half = 0; half < 2; ++half) {
-          const uint32_t sel = half ? 0x7632u : 0x5410u;
-          uint32_t xa[4], xc[4];
-          ptx::nibbles_to_half2_64(__byte_perm(wa, wb, sel), xa);  // nibbles 4*half + 0..3 of tokens (a, b)
-          ptx::nibbles_to_half2_64(__byte_perm(wc, wd, sel), xc);
-          // nibble j of word q <-> m-tile 4q + j/2, row g (+8 when j is odd)
-          const int i0 = 4 * q + 2 * half;
-          ptx::mma_f16_16816(st.o[i0], xa[0], xa[1], xc[0], xc[1], bS0, bS1);
-          ptx::mma_f16_16816(st.o[i0 + 1], xa[2], xa[3], xc[2], xc[3], bS0, bS1);
-        }
-      }
-      // the offset 72 of every code value: 72 * sum_t P'_t, exactly as the MMAs above weight it
-      ptx::mma_f16_16816(st.vb, ptx::HALF2_72, ptx::HALF2_72, ptx::HALF2_72, ptx::HALF2_72, bS0, bS1);
-    }
+    // the offset 72 of every code value: 72 * sum_t P'_t, exactly as the MMAs above weight it
+    ptx::mma_f16_16816(st.vb, ptx::HALF2_72, ptx::HALF2_72, ptx::HALF2_72, ptx::HALF2_72, bS0, bS1);
   }
 }
 
@@ -549,58 +588,137 @@ __device__ __forceinline__ int cta_first_unit(const Params &p, const Len &L, int
   return unit_of(L, first_chunk(p, L, cta * p.nwc));
 }
 
-// In-step encode of token tnew of unit (b, h) by one warp, into the chunk's
-// slot (already holding the block copied from the cache) and into the cache
-// block itself (physical page pg).  The same codec as the append kernel.
-template <class G, int DTYPE>
-__device__ void encode_new_token(const Params &p, unsigned char *slot, int64_t pg, int b, int h, int64_t tnew,
+// In-step encode of component COMP of token tnew of unit (b, h) by one warp,
+// into the chunk's part in shared memory (already holding the part copied
+// from the cache) and into the cache block itself (physical page pg).  The
+// same codec as the append kernel.
+template <class G, int DTYPE, int COMP>
+__device__ void encode_new_token(const Params &p, unsigned char *part, int64_t pg, int b, int h, int64_t tnew,
                                  uint32_t *sw, int lane) {
   const int tl = (int)(tnew % p.cv.P);
   const int x = tl % G::C, j = tl / G::C;
   unsigned char *blk = const_cast<unsigned char *>((const unsigned char *)p.blk) + (pg * p.cv.H + h) * p.phs +
-                       (int64_t)j * G::SLOT;
+                       (int64_t)j * G::SLOT + (COMP ? G::O_KF1 : 0);
+  const CompView &c = p.cv.c[COMP];
+  constexpr int s = COMP ? G::SV : G::SK;
+  constexpr int ocd = COMP ? G::V_CD : G::O_CD0, osc = COMP ? G::V_SC : G::O_SC0;  // offsets inside the part
+  const int a = x / s, phase = x - a * s;
+  const int64_t xb = b * p.x_sb[COMP] + h * p.x_sh[COMP];
+  float xv[kMaxDimsPerLane];
 #pragma unroll
-  for (int comp = 0; comp < 2; ++comp) {
-    const CompView &c = p.cv.c[comp];
-    const int s = comp ? G::SV : G::SK;
-    const int okf = comp ? G::O_KF1 : G::O_KF0, ocd = comp ? G::O_CD1 : G::O_CD0, osc = comp ? G::O_SC1 : G::O_SC0;
-    const int a = x / s, phase = x - a * s;
-    const int64_t xb = b * p.x_sb[comp] + h * p.x_sh[comp];
-    float xv[kMaxDimsPerLane];
-#pragma unroll
-    for (int i = 0; i < kMaxDimsPerLane; ++i) {
-      const int d = lane + 32 * i;
-      xv[i] = (d < HD) ? load_as_float(p.x[comp], xb + d, DTYPE) : 0.f;
-    }
-    __half *arow_s = (__half *)(slot + okf + a * HD * 2), *arow_g = (__half *)(blk + okf + a * HD * 2);
-    if (phase == 0) {  // I-frame: token.astype(float16) (cache.py:103-105), scale slot 0
-#pragma unroll
-      for (int i = 0; i < HD / 32; ++i) {
-        const __half v = __float2half_rn(xv[i]);
-        arow_s[lane + 32 * i] = v;
-        arow_g[lane + 32 * i] = v;
-      }
-      if (lane == 0) {
-        *(__half *)(slot + osc + x * 2) = __float2half_rn(0.f);
-        *(__half *)(blk + osc + x * 2) = __float2half_rn(0.f);
-      }
-    } else {
-      float av[kMaxDimsPerLane];
-#pragma unroll
-      for (int i = 0; i < kMaxDimsPerLane; ++i) av[i] = (i < HD / 32) ? __half2float(arow_s[lane + 32 * i]) : 0.f;
-      const float scale = encode_residual<DTYPE>(xv, av, HD, c.bits, c.dead_zone, c.order, sw, lane);
-      const int pf = x - a - 1;
-      if (lane < HD / 8) {
-        ((uint32_t *)(slot + ocd + pf * (HD / 2)))[lane] = sw[lane];
-        ((uint32_t *)(blk + ocd + pf * (HD / 2)))[lane] = sw[lane];
-      }
-      if (lane == 0) {
-        *(__half *)(slot + osc + x * 2) = __float2half_rn(scale);
-        *(__half *)(blk + osc + x * 2) = __float2half_rn(scale);
-      }
-    }
-    __syncwarp();
+  for (int i = 0; i < kMaxDimsPerLane; ++i) {
+    const int d = lane + 32 * i;
+    xv[i] = (d < HD) ? load_as_float(p.x[COMP], xb + d, DTYPE) : 0.f;
   }
+  __half *arow_s = (__half *)(part + a * HD * 2), *arow_g = (__half *)(blk + a * HD * 2);
+  if (phase == 0) {  // I-frame: token.astype(float16) (cache.py:103-105), scale slot 0
+#pragma unroll
+    for (int i = 0; i < HD / 32; ++i) {
+      const __half v = __float2half_rn(xv[i]);
+      arow_s[lane + 32 * i] = v;
+      arow_g[lane + 32 * i] = v;
+    }
+    if (lane == 0) {
+      *(__half *)(part + osc + x * 2) = __float2half_rn(0.f);
+      *(__half *)(blk + osc + x * 2) = __float2half_rn(0.f);
+    }
+  } else {
+    float av[kMaxDimsPerLane];
+#pragma unroll
+    for (int i = 0; i < kMaxDimsPerLane; ++i) av[i] = (i < HD / 32) ? __half2float(arow_s[lane + 32 * i]) : 0.f;
+    const float scale = encode_residual<DTYPE>(xv, av, HD, c.bits, c.dead_zone, c.order, sw, lane);
+    const int pf = x - a - 1;
+    if (lane < HD / 8) {
+      ((uint32_t *)(part + ocd + pf * (HD / 2)))[lane] = sw[lane];
+      ((uint32_t *)(blk + ocd + pf * (HD / 2)))[lane] = sw[lane];
+    }
+    if (lane == 0) {
+      *(__half *)(part + osc + x * 2) = __float2half_rn(scale);
+      *(__half *)(blk + osc + x * 2) = __float2half_rn(scale);
+    }
+  }
+  __syncwarp();
+}
+
+template <class G, int COMP>
+__device__ __forceinline__ void encode_if_last(const Params &p, const Len &L, const Cursor &cc, unsigned char *part,
+                                               uint32_t *sw, int lane) {
+  if (!(p.fuse && cc.cu == L.cpu - 1)) return;  // this step's new token lies in the unit's last chunk
+  const int64_t pg = table_page(p.cv, cc.b, cc.lp);
+  if (p.x_dtype == CQ_BF16)
+    encode_new_token<G, CQ_BF16, COMP>(p, part, pg, cc.b, cc.h, L.T - 1, sw, lane);
+  else
+    encode_new_token<G, CQ_F16, COMP>(p, part, pg, cc.b, cc.h, L.T - 1, sw, lane);
+}
+
+// One chunk: the K phase (scores and softmax of every 32-token group, P kept
+// in registers), then the V phase (output of every tile).  With SPLIT the K
+// buffer is refilled between the two phases and the V buffer after them;
+// otherwise the whole slot is refilled at the end.  Returns false when a wait
+// gave up.
+template <class G, bool MASK>
+__device__ __forceinline__ bool do_chunk(const Params &p, const Len &L, WarpState &st, const QFrag &f,
+                                         const Cursor &cc, int nvalid, unsigned char *region, uint64_t *bar, int sk,
+                                         uint32_t ph, Cursor &ci, int64_t pg_next, float *qa, const uint2 *qn,
+                                         int lane) {
+  constexpr int NG = G::NT / 2;  // 32-token groups per chunk
+  const uint32_t ra = ptx::smem_u32(region);
+  // K and V parts: separate buffers (SPLIT) or the two halves of slot sk
+  const int koff = G::SPLIT ? 0 : sk * G::SLOT, voff = G::SPLIT ? G::KB : sk * G::SLOT + G::O_KF1;
+  const uint32_t kb = ra + koff, vbuf = ra + voff;
+  // ---- K phase
+  if (!ptx::mbar_wait_bounded(&bar[sk], ph, WAIT_BUDGET)) return false;
+  encode_if_last<G, 0>(p, L, cc, region + koff, (uint32_t *)qa, lane);
+  compute_qa(kb + G::O_KF0, qa, MASK ? ((nvalid - 1) >> G::LSK) + 1 : G::AK, qn, lane);
+  __syncwarp();
+  uint2 bp[NG][2];
+  {
+    const KAddr A(G(), kb, ptx::smem_u32(qa), lane);
+#pragma unroll
+    for (int grp = 0; grp < NG; ++grp) {
+      if (MASK && grp * 32 >= nvalid) break;
+      __half2 fh;
+      if (k_group<G, MASK>(st, A, f, grp * 32, nvalid, lane, bp[grp], fh)) {
+        // this chunk's earlier P into the new frame
+#pragma unroll
+        for (int k = 0; k < grp; ++k)
+#pragma unroll
+          for (int tile = 0; tile < 2; ++tile) {
+            bp[k][tile].x = ptx::h22u(__hmul2(ptx::u2h2(bp[k][tile].x), fh));
+            bp[k][tile].y = ptx::h22u(__hmul2(ptx::u2h2(bp[k][tile].y), fh));
+          }
+      }
+    }
+  }
+  if (G::SPLIT) {
+    // every lane's reads of the K buffer (and of the q.anchor table) are done before the refill
+    __syncwarp();
+    ptx::fence_proxy_async_smem();
+    if (ci.valid()) issue_part<G, 0>(p, kb, &bar[sk], ci, pg_next, lane);
+    // ---- V phase: its own buffer
+    if (!ptx::mbar_wait_bounded(&bar[G::NSK + sk], ph, WAIT_BUDGET)) return false;
+  }
+  encode_if_last<G, 1>(p, L, cc, region + voff, (uint32_t *)qa, lane);
+  {
+    const VAddr A(G(), vbuf, lane);
+#pragma unroll
+    for (int grp = 0; grp < NG; ++grp)
+#pragma unroll
+      for (int tile = 0; tile < 2; ++tile)
+        if (!MASK || grp * 32 + tile * 16 < nvalid)
+          v_tile<G, MASK>(st, A, grp * 32 + tile * 16, bp[grp][tile].x, bp[grp][tile].y, nvalid, lane);
+  }
+  // every lane's reads of the V part are done before the refill
+  __syncwarp();
+  ptx::fence_proxy_async_smem();
+  if (ci.valid()) {
+    if (G::SPLIT)
+      issue_part<G, 1>(p, vbuf, &bar[G::NSK + sk], ci, pg_next, lane);
+    else
+      issue_part<G, 2>(p, kb, &bar[sk], ci, pg_next, lane);
+    ci.next(p, L);
+  }
+  return true;
 }
 
 template <class G>
@@ -611,25 +729,30 @@ __device__ __forceinline__ void warp_main(const Params &p, const Len &L, unsigne
   unsigned char *region = smem + p.off_warp + warp * p.warp_bytes;
   const uint32_t region_a = ptx::smem_u32(region);
   const int u0 = cta_first_unit(p, L, blockIdx.x);
-  float *qa = (float *)(region + kNS * G::SLOT);
+  float *qa = (float *)(region + G::BUF);
+  uint2 *qn = (uint2 *)(region + G::BUF + kQaBytes);
 
+  // the issue cursor runs NSK chunks ahead: a chunk's slot (or K and V
+  // buffers) is refilled with the chunk NSK positions later
   Cursor ci, cc;
   cc.init(p, L, first, last);
   ci = cc;
-  for (int s = 0; s < kNS && ci.valid(); ++s) {
+  for (int s = 0; s < G::NSK && ci.valid(); ++s) {
     const int64_t pg = table_page(p.cv, ci.b, ci.lp);
-    issue_chunk<G>(p, region_a + s * G::SLOT, &bar[s], ci, pg, lane);
+    if (G::SPLIT) {
+      issue_part<G, 0>(p, region_a, &bar[s], ci, pg, lane);
+      issue_part<G, 1>(p, region_a + G::KB, &bar[G::NSK + s], ci, pg, lane);
+    } else {
+      issue_part<G, 2>(p, region_a + s * G::SLOT, &bar[s], ci, pg, lane);
+    }
     ci.next(p, L);
   }
-
-  uint2 *qn = (uint2 *)(region + kNS * G::SLOT + kQaBytes);
-  const uint32_t qa_a = ptx::smem_u32(qa);
 
   WarpState st;
   reset(st);
   QFrag f;
   int cur_unit = -1;
-  int s = 0;
+  int sk = 0;  // slot (or buffer pair) of this chunk and its barrier phase
   uint32_t ph = 0;
   for (; cc.valid(); cc.next(p, L)) {
     // page of the next chunk to issue, loaded early so its latency hides under this chunk
@@ -648,42 +771,17 @@ __device__ __forceinline__ void warp_main(const Params &p, const Len &L, unsigne
       load_q(p, cc.b, cc.h, lane, f, qn);
       __syncwarp();
     }
-    if (!ptx::mbar_wait_bounded(&bar[s], ph, WAIT_BUDGET)) {
+    const int nvalid = cc.nvalid(p, L);
+    const bool ok = (nvalid == G::C)
+                        ? do_chunk<G, false>(p, L, st, f, cc, nvalid, region, bar, sk, ph, ci, pg_next, qa, qn, lane)
+                        : do_chunk<G, true>(p, L, st, f, cc, nvalid, region, bar, sk, ph, ci, pg_next, qa, qn, lane);
+    if (!ok) {
       // a copy never landed: record it and stop this warp (no hang, results invalid)
       atomicExch(&g_fast_error, ERR_TIMEOUT_FULL);
       return;
     }
-    const uint32_t sa = region_a + s * G::SLOT;
-    const int nvalid = cc.nvalid(p, L);
-    if (p.fuse && cc.cu == L.cpu - 1) {  // this step's new token lies in the unit's last chunk
-      const int64_t pg = table_page(p.cv, cc.b, cc.lp);
-      unsigned char *slot = region + s * G::SLOT;
-      if (p.x_dtype == CQ_BF16)
-        encode_new_token<G, CQ_BF16>(p, slot, pg, cc.b, cc.h, L.T - 1, (uint32_t *)qa, lane);
-      else
-        encode_new_token<G, CQ_F16>(p, slot, pg, cc.b, cc.h, L.T - 1, (uint32_t *)qa, lane);
-    }
-    const LaneAddr A(G(), sa, qa_a, lane);
-    // tiles in groups of two (one softmax update per 32 tokens)
-    if (nvalid == G::C) {
-      compute_qa(sa + G::O_KF0, qa, G::AK, qn, lane);
-      __syncwarp();
-#pragma unroll
-      for (int grp = 0; grp < G::NT / 2; ++grp) process_group<G, false>(st, A, f, grp * 32, nvalid, lane);
-    } else {
-      compute_qa(sa + G::O_KF0, qa, ((nvalid - 1) >> G::LSK) + 1, qn, lane);
-      __syncwarp();
-      for (int grp = 0; grp * 32 < nvalid; ++grp) process_group<G, true>(st, A, f, grp * 32, nvalid, lane);
-    }
-    // every lane's reads of this slot are done before the refill is issued
-    __syncwarp();
-    ptx::fence_proxy_async_smem();
-    if (ci.valid()) {
-      issue_chunk<G>(p, sa, &bar[s], ci, pg_next, lane);
-      ci.next(p, L);
-    }
-    if (++s == kNS) {
-      s = 0;
+    if (++sk == G::NSK) {
+      sk = 0;
       ph ^= 1u;
     }
   }
@@ -925,9 +1023,9 @@ __global__ void __launch_bounds__(kMaxWarps * 32, 1) decode_kernel(const __grid_
   extern __shared__ __align__(128) unsigned char smem[];
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int nwc = blockDim.x >> 5;
-  uint64_t *bar = (uint64_t *)smem + warp * kNS;
+  uint64_t *bar = (uint64_t *)smem + warp * kBarsPerWarp;
   if (lane == 0) {
-    for (int s = 0; s < kNS; ++s) ptx::mbar_init(&bar[s], 1);
+    for (int s = 0; s < kBarsPerWarp; ++s) ptx::mbar_init(&bar[s], 1);
     ptx::fence_mbar_init();
     ((int *)(smem + p.off_fin))[warp] = -1;  // warps without work contribute nothing
   }
@@ -982,7 +1080,7 @@ using KernelFn = void (*)(Params);
 
 // One supported (stride_k, stride_v) pair: its geometry and kernel.
 struct GeoInfo {
-  int sk, sv, C, slot;
+  int sk, sv, C, slot, buf;
   int off[6];  // K anchors, K codes, K scales, V anchors, V codes, V scales
   KernelFn fn;
 };
@@ -990,7 +1088,7 @@ struct GeoInfo {
 template <int SK, int SV>
 static GeoInfo geo_info() {
   using G = Geo<SK, SV>;
-  return GeoInfo{SK, SV, G::C, G::SLOT, {G::O_KF0, G::O_CD0, G::O_SC0, G::O_KF1, G::O_CD1, G::O_SC1},
+  return GeoInfo{SK, SV, G::C, G::SLOT, G::BUF, {G::O_KF0, G::O_CD0, G::O_SC0, G::O_KF1, G::O_CD1, G::O_SC1},
                  decode_kernel<G>};
 }
 
@@ -1049,9 +1147,9 @@ static bool make_layout(const cq_paged_cache &c, Layout &L) {
   }
   if ((L.phs & 15) || L.phs < cs * (c.page_tokens / L.C)) return false;
   // a warp's copy slots later hold its on-chip partial; warp 0's also the unit list
-  L.warp_bytes = std::max(kNS * (int)cs, 8192 + 4 * kMaxWarps * 32) + kQaBytes + kQnBytes;
+  L.warp_bytes = std::max(L.geo->buf, 8192 + 4 * kMaxWarps * 32) + kQaBytes + kQnBytes;
   static_assert(kFinFloats * 4 <= 8192, "on-chip partial must fit below the unit list");
-  L.off_fin = kMaxWarps * 4 * 8;  // after the mbarriers [warp][slot]: each warp's last unit
+  L.off_fin = kMaxWarps * kBarsPerWarp * 8;  // after the mbarriers [warp][slot]: each warp's last unit
   L.off_strad = up128(L.off_fin + kMaxWarps * 4);
   L.off_warp = up128(L.off_strad + kStrad * kFinFloats * 4);
   if (L.warp_bytes & 15) return false;  // on-chip partials are read as float4
