@@ -2,15 +2,17 @@
 
     python bench.py [--gpus N] [--steps K] [--warmup W] [--config 2|3|4|5] [--impl ours|reference]
 
-Workload (bench config 2 by default): one attention layer, B=8 sequences,
-32 query / 8 KV heads, head_dim 128, a compressed context of T=16384 tokens
-per sequence in the Standard preset (stride_k 32, stride_v 8, INT4 residuals,
-dead zone 0).  One step = append one new token per sequence (the streaming
-encode kernel) + decode attention of a bf16 query against everything cached
-(the split-KV decode kernel, which also merges its splits), issued as one
-replay of a CUDA graph (``DecodeGraph``) after one copy of the step's K/V/q
-from a device-resident pool into the graph's flat input buffer.  Synthetic AR(1) K/V
-(fp16), seeded.
+Workload (bench config 3 by default, the metric's 32k-context case): one
+attention layer, B=16 sequences, 32 query / 8 KV heads, head_dim 128, a
+compressed context of T=32768 tokens per sequence in the Full-Throttle V3
+preset (stride_k 64, stride_v 32, INT4 K / 3-bit V residuals in INT4 lanes,
+dead zones 0 / 0.05).  ``--config 2`` selects B=8, T=16384, Standard
+(stride_k 32, stride_v 8, INT4, dead zone 0).  One step = append one new
+token per sequence (the streaming encode) + decode attention of a bf16 query
+against everything cached (the split-KV decode kernel, which also merges its
+splits), issued as one replay of a CUDA graph (``DecodeGraph``) after one
+copy of the step's K/V/q from a device-resident pool into the graph's flat
+input buffer.  Synthetic AR(1) K/V (fp16), seeded.
 
 value: compressed bytes the step must move (the cache's active bytes, the
 reference accounting, plus query/output and the encode's own bytes) divided
@@ -18,12 +20,18 @@ by the device time per step (CUDA events, max over ranks).  The cache (~170 MB
 per GPU) exceeds the 126 MB L2, so no flush is needed between steps.
 e2e: the same metric through the public API with pinned host buffers: the new
 token's K/V and the query copied host->device and the output device->host
-inside every timed step.
+inside every timed step (double-buffered: step k+1's inputs are copied in on a
+copy stream while step k runs, step k's output is copied out while step k+1
+runs).
 roofline: the decode kernel alone, a graph of the attention launch replayed
 back to back (it only reads the cache), CUDA events around the batch.
 
---gpus N (under torchrun): weak scaling, each rank owns a full config-2 shard
-(its own 8 sequences x 8 KV heads); no collective on the data path.
+--gpus N (under torchrun, N dividing the 8 KV heads): weak scaling by KV-head
+shards.  The job decodes N x B sequences; rank r holds KV heads
+[r*8/N, (r+1)*8/N) (and their query heads) of every sequence, so each rank
+holds as many (sequence, kv-head) units and compressed bytes as one GPU at
+N=1 (591 MB for config 3, above the 126 MB L2).  No collective on the data
+path: heads are independent.
 --impl reference: the reference's CPU path (restated in oracle/, the
 reference itself needs MLX/Metal) timed on the host cores.
 """
@@ -154,7 +162,7 @@ class ClockSampler:
                         self.reasons.add(name)
             except Exception:
                 pass
-            time.sleep(0.05)
+            time.sleep(0.002)
 
     def __enter__(self):
         if self.ok:
@@ -199,6 +207,35 @@ def load_traffic(cfg_name):
 # ----------------------------------------------------------------------------- GPU arm
 
 
+def shard_of(cfg, world, rank):
+    """KV-head shard of rank `rank` among `world` ranks (weak scaling): the
+    job decodes world x B sequences and each rank holds Hkv/world KV heads of
+    all of them, so every rank has the units and bytes of the one-GPU
+    workload.  Returns (local batch, local kv heads, local q heads, first
+    kv head)."""
+    B, H, Hq = cfg["B"], cfg["Hkv"], cfg["Hq"]
+    if world <= 1:
+        return B, H, Hq, 0
+    if H % world:
+        raise SystemExit(f"--gpus {world} must divide the {H} KV heads")
+    return B * world, H // world, Hq // world, rank * (H // world)
+
+
+def decode_config(cfg, world, T_start):
+    """The `config` object of a decode line (the same for both arms)."""
+    B, H, Hq, D = cfg["B"], cfg["Hkv"], cfg["Hq"], cfg["D"]
+    Bl, Hl, _, _ = shard_of(cfg, world, 0)
+    return {"workload": cfg["name"], "batch": B * max(world, 1), "q_heads": Hq, "kv_heads": H, "head_dim": D,
+            "context_tokens_start": T_start, "stride_k": cfg["stride_k"], "stride_v": cfg["stride_v"],
+            "bits_k": cfg["bits_k"], "bits_v": cfg["bits_v"], "dead_zone_k": cfg["dz_k"], "dead_zone_v": cfg["dz_v"],
+            "step": "append 1 token per (sequence, kv-head) (encode) + decode attention of one query per head",
+            "l2": "cache active bytes %.0f MB per GPU > 126 MB L2; no flush" %
+                  (active_bytes(Bl, Hl, T_start, D, cfg["stride_k"], cfg["stride_v"]) / 1e6),
+            "parallelism": (f"one shard: all {B} sequences x {H} kv-heads" if world <= 1 else
+                            f"kv-head shards over {world} GPUs: each rank holds {Hl} of {H} kv-heads of all "
+                            f"{Bl} sequences (weak scaling; no collective)")}
+
+
 def run_ours(args, cfg):
     import torch
     import torch.distributed as dist
@@ -217,7 +254,9 @@ def run_ours(args, cfg):
     sys.path.insert(0, HERE)
     from chronoquant_mlx_b200 import ChronoQuantCache, DecodeGraph
 
-    B, H, Hq, D, T0 = cfg["B"], cfg["Hkv"], cfg["Hq"], cfg["D"], cfg["T"]
+    B, H, Hq, h0 = shard_of(cfg, world, rank)
+    D, T0 = cfg["D"], cfg["T"]
+    lcfg = dict(cfg, B=B, Hkv=H, Hq=Hq)  # this rank's shard
     n_new = args.warmup + args.steps + 2  # tokens appended by warm-up, timed and e2e steps
     K, V = ar1_host(B, H, T0 + 2 * n_new, D, cfg["rho_k"], cfg["rho_v"], seed=1000 + rank)
     cache = ChronoQuantCache(stride_k=cfg["stride_k"], stride_v=cfg["stride_v"], delta_bits_k=cfg["bits_k"],
@@ -230,11 +269,13 @@ def run_ours(args, cfg):
                                torch.from_numpy(V[:, :, t:t + n]).to(device))
     newK = torch.from_numpy(np.ascontiguousarray(K[:, :, T0:])).to(device)
     newV = torch.from_numpy(np.ascontiguousarray(V[:, :, T0:])).to(device)
+    del K, V
     g = torch.Generator(device="cpu").manual_seed(7 + rank)
     qs = (torch.randn((2 * n_new, B, Hq, 1, D), generator=g) / math.sqrt(D)).to(torch.bfloat16).to(device)
     scale = 1.0 / math.sqrt(D)
-    # one decode step = one CUDA-graph replay: encode the new token, attend over the cache
-    dg = DecodeGraph(cache, Hq, scale, q_dtype=torch.bfloat16, max_len=T0 + 2 * n_new + 4)
+    # one decode step = one CUDA-graph replay: encode the new token, attend over the cache;
+    # two buffer sets so the e2e loop can copy step k+1's inputs while step k runs
+    dg = DecodeGraph(cache, Hq, scale, q_dtype=torch.bfloat16, max_len=T0 + 2 * n_new + 4, buffers=2)
     torch.cuda.synchronize()
 
     # every step's K/V/q packed in the layout of the graph's flat input buffer:
@@ -279,7 +320,7 @@ def run_ours(args, cfg):
     T_end = cache.offset
     tot_bytes = 0
     for T in range(T_start + 1, T_end + 1):
-        a, e = step_bytes(cfg, T)
+        a, e = step_bytes(lcfg, T)
         tot_bytes += a + e
     ms_per_step = elapsed_ms / args.steps
     value = world * tot_bytes / (elapsed_ms * 1e-3) / 1e9
@@ -301,25 +342,54 @@ def run_ours(args, cfg):
     a1.record(stream)
     torch.cuda.synchronize()
     mean_attn_ms = a0.elapsed_time(a1) / reps
-    mean_attn_bytes = step_bytes(cfg, cache.offset)[0]
+    mean_attn_bytes = step_bytes(lcfg, cache.offset)[0]
     del attn_graph
 
-    # e2e: the same step through the public API with host buffers -- pinned
-    # host K/V/q copied in and the output copied out inside every timed step
+    # e2e: the same step through the public API with host buffers -- every
+    # step's K/V/q copied in from pinned host memory and its output copied
+    # back to pinned host memory.  Double-buffered on a copy stream: step
+    # k+1's inputs go in while step k runs, step k's output comes out while
+    # step k+1 runs; the timed region ends after the last output is home.
     hin = pool[n_new:].cpu().pin_memory()  # each row: one step's K, V and q bytes
     hout = torch.empty((B, Hq, 1, D), dtype=torch.bfloat16).pin_memory()
     e_steps = min(args.steps, n_new - 2)
+    copy = torch.cuda.Stream(device)
+    ev_in = [torch.cuda.Event(), torch.cuda.Event()]
+    ev_done = [torch.cuda.Event(), torch.cuda.Event()]
+    ev_out = [torch.cuda.Event(), torch.cuda.Event()]
     torch.cuda.synchronize()
     if world > 1:
         dist.barrier()
     e0 = torch.cuda.Event(enable_timing=True)
     e1 = torch.cuda.Event(enable_timing=True)
     Te0 = cache.offset
+    first_set = dg._cur  # buffer set of step 0
     e0.record(stream)
+    copy.wait_event(e0)
+
+    def h2d(k):  # step k's inputs into its buffer set, once step k-2 (same set) has run
+        s = (first_set + k) % 2
+        with torch.cuda.stream(copy):
+            if k >= 2:
+                copy.wait_event(ev_done[s])
+            dg.inputs_of(s).copy_(hin[k], non_blocking=True)
+            ev_in[s].record(copy)
+
+    h2d(0)
     for k in range(e_steps):
-        dg.inputs.copy_(hin[k], non_blocking=True)
+        s = (first_set + k) % 2
+        if k + 1 < e_steps:
+            h2d(k + 1)
+        stream.wait_event(ev_in[s])
+        if k >= 2:
+            stream.wait_event(ev_out[s])  # step k-2's output (same set) is home
         out = dg.replay()
-        hout.copy_(out, non_blocking=True)
+        ev_done[s].record(stream)
+        with torch.cuda.stream(copy):
+            copy.wait_event(ev_done[s])
+            hout.copy_(out, non_blocking=True)
+            ev_out[s].record(copy)
+    stream.wait_stream(copy)
     e1.record(stream)
     torch.cuda.synchronize()
     e_ms = e0.elapsed_time(e1)
@@ -327,10 +397,10 @@ def run_ours(args, cfg):
         tt = torch.tensor([e_ms], device=device)
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e_ms = float(tt.item())
-    e_bytes = sum(sum(step_bytes(cfg, T)) for T in range(Te0 + 1, cache.offset + 1))
+    e_bytes = sum(sum(step_bytes(lcfg, T)) for T in range(Te0 + 1, cache.offset + 1))
     e2e_value = world * e_bytes / (e_ms * 1e-3) / 1e9
-    h2d = hin[0].numel()
-    d2h = hout.numel() * 2
+    h2d_bytes = hin[0].numel()
+    d2h_bytes = hout.numel() * 2
 
     fp16_base = fp16_decode_baseline(cfg, cache.offset, device, reps) if world == 1 else None
 
@@ -355,17 +425,14 @@ def run_ours(args, cfg):
             "vs_baseline": None,
             "dtype": "int4-residual/f16-anchor, bf16 q, f32 accumulate",
             "data": "synthetic AR(1) K/V (seeded), random bf16 queries",
-            "config": {"workload": cfg["name"], "batch": B, "q_heads": Hq, "kv_heads": H, "head_dim": D,
-                       "context_tokens_start": T_start, "stride_k": cfg["stride_k"], "stride_v": cfg["stride_v"],
-                       "bits_k": cfg["bits_k"], "bits_v": cfg["bits_v"], "dead_zone_v": cfg["dz_v"],
-                       "page_tokens": cache.page_tokens,
-                       "step": "append 1 token (encode) + decode attention, one CUDA-graph replay",
-                       "l2": "cache active bytes %.0f MB per GPU > 126 MB L2; no flush" %
-                             (active_bytes(B, H, T_start, D, cfg["stride_k"], cfg["stride_v"]) / 1e6),
-                       "parallelism": f"dp{world} (batch/head shards, no collective)"},
-            "tokens_per_s": round(world * B * args.steps / (elapsed_ms * 1e-3), 1),
-            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d,
-                    "d2h_bytes_per_step": d2h, "steps": e_steps},
+            "config": decode_config(cfg, world, T_start),
+            "cache_layout": {"page_tokens": cache.page_tokens, "chunk_tokens": cache.store.chunk},
+            # every rank holds a head slice of all B local sequences: B tokens per step for the job
+            "tokens_per_s": round(B * args.steps / (elapsed_ms * 1e-3), 1),
+            "bytes_per_step_per_gpu": round(tot_bytes / args.steps),
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s", "h2d_bytes_per_step": h2d_bytes,
+                    "d2h_bytes_per_step": d2h_bytes, "steps": e_steps,
+                    "copies": "pinned host <-> device on a copy stream, double-buffered (overlapping the steps)"},
             "roofline": {"bound": "hbm", "kernel": "decode_kernel (split-KV decode with in-kernel merge)",
                          "achieved": round(achieved, 1), "peak": peak, "unit": "GB/s",
                          "frac": round(achieved / peak, 4), "peak_source": peak_kind,
@@ -881,6 +948,11 @@ def cpu_baseline(cfg, budget_s=20.0):
 
 
 def run_reference(args, cfg):
+    """The reference's CPU path (oracle restatement) on the host cores: one
+    process per core, each stepping one (sequence, kv-head) unit of the
+    workload.  A step of this arm is one decode step of `workers` units in
+    parallel (a bounded sample of the workload's units); `ms_per_step` and
+    `value` are that sample's own measured time and throughput."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     if rank != 0:
@@ -896,34 +968,36 @@ def run_reference(args, cfg):
     _ref_unit_step(c, K, V, q, 1.0 / math.sqrt(cfg["D"]))
     t_unit = time.perf_counter() - t0
     total_steps = args.steps + args.warmup
-    units = cfg["B"] * cfg["Hkv"]
+    units = cfg["B"] * cfg["Hkv"] * max(world, 1)
     workers = min(cores, units)
     # steps per worker so that the whole timed run stays near 90 s of wall time
-    per_worker_steps = max(1, min(total_steps, int(90.0 / max(t_unit, 1e-3))))
+    per_worker_steps = max(2, min(total_steps, 60, int(90.0 / max(t_unit, 1e-3))))  # K/V hold T + 64 tokens
     ctx = mp.get_context("spawn")
+    t_wall = time.perf_counter()
     with ctx.Pool(workers) as pool:
         res = pool.map(_ref_worker, [(cfg, 100 + i, per_worker_steps) for i in range(workers)])
+    t_wall = time.perf_counter() - t_wall
     w = min(args.warmup, per_worker_steps - 1)
-    step_times = []
-    for times, _ in res:
-        step_times.extend(times[w:])
-    # each worker processes one unit per step in parallel; throughput = bytes of all units / wall per step
-    mean_t = sum(step_times) / len(step_times)
+    timed = per_worker_steps - w
+    # step i of the sample = every worker's i-th unit step, run in parallel: its time is the slowest worker's
+    step_ms = [1e3 * max(times[w + i] for times, _ in res) for i in range(timed)]
+    ms = sum(step_ms) / timed
     unit_cfg = dict(cfg, B=1, Hkv=1, Hq=rep)
-    a, e = step_bytes(unit_cfg, cfg["T"] + 1)
-    value = workers * (a + e) / mean_t / 1e9
-    ms_per_step_full = mean_t * 1e3 * units / workers
+    byts = sum(step_bytes(unit_cfg, cfg["T"] + w + i + 1)[0] + step_bytes(unit_cfg, cfg["T"] + w + i + 1)[1]
+               for i in range(timed)) / timed
+    value = workers * byts / (ms * 1e-3) / 1e9
+    sample = (f"each step: one decode step (encode the new token, fp16 reconstruct, fallback SDPA) on each of "
+              f"{workers} of the workload's {units} (sequence, kv-head) units, one host process per unit "
+              f"(oracle restatement of the reference's CPU path; MLX/Metal is unavailable here); {timed} timed "
+              f"steps after {w} warm-up, wall {t_wall:.1f} s")
     out = {
         "impl": "reference", "metric": METRIC, "value": round(value, 4), "unit": "GB/s", "n_gpus": world,
-        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(ms_per_step_full, 3),
+        "steps": timed, "warmup": w, "ms_per_step": round(ms, 3),
         "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
         "dtype": "int4-residual/f16-anchor, fp16 fallback SDPA", "data": "synthetic AR(1) K/V (seeded)",
-        "config": {"workload": cfg["name"], "batch": cfg["B"], "q_heads": cfg["Hq"], "kv_heads": cfg["Hkv"],
-                   "head_dim": cfg["D"], "context_tokens_start": cfg["T"], "parallelism": f"{workers} host processes"},
+        "config": decode_config(cfg, world, cfg["T"] + w),
         "cpu_baseline": {"value": round(value, 4), "unit": "GB/s", "cores": workers, "kind": "port",
-                         "sample": f"{per_worker_steps} decode steps on each of {workers} of {units} (sequence, "
-                                   f"kv-head) units at T={cfg['T']} (oracle restatement of the reference's "
-                                   "encode + fp16 reconstruct + fallback SDPA; MLX/Metal is unavailable here)"},
+                         "sample": sample},
         "e2e": {"value": round(value, 4), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
     }
     print(json.dumps(out))
@@ -934,7 +1008,7 @@ def main():
     ap.add_argument("--gpus", type=int, default=1)
     ap.add_argument("--steps", type=int, default=200)
     ap.add_argument("--warmup", type=int, default=10)
-    ap.add_argument("--config", type=int, default=2, choices=sorted(CONFIGS))
+    ap.add_argument("--config", type=int, default=3, choices=sorted(CONFIGS))
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--cpu-budget", type=float, default=15.0)

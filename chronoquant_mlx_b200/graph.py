@@ -26,6 +26,13 @@ and call ``replay``),
 replays the graph and advances ``cache.offset`` like ``update_and_fetch``.
 The returned tensor is the graph's output buffer: it is overwritten by the
 next step.
+
+``buffers=2`` captures two graphs over two sets of input and output buffers
+(they share the cache, its device-resident length and the workspace).  The
+sets alternate: ``keys``/``values``/``queries``/``inputs``/``out`` name the
+set the next ``replay`` uses, and ``inputs_of(k)`` / ``out_of(k)`` name set
+``k % buffers``, so a caller can copy step k+1's inputs in (on another stream)
+while step k runs and read step k's output while step k+1 runs.
 """
 
 from __future__ import annotations
@@ -41,7 +48,7 @@ from ._tensors import cq_dtype, require_cuda, stream_ptr
 
 class DecodeGraph:
     def __init__(self, cache, num_q_heads: int, scale: float, *, q_dtype=torch.bfloat16, max_len: int | None = None,
-                 tokens: int = 1, kv_dtype=torch.float16, out_dtype=None):
+                 tokens: int = 1, kv_dtype=torch.float16, out_dtype=None, buffers: int = 1):
         st = cache.store
         if st is None or cache.offset == 0:
             raise ValueError("DecodeGraph needs a cache that already holds tokens (prefill first)")
@@ -61,14 +68,20 @@ class DecodeGraph:
         self.len = torch.zeros(2, dtype=torch.int64, device=dev)  # {tokens cached, arrival counter}
         self.len[0] = cache.offset
         self._synced = cache.offset
-        # the step's inputs live in one flat buffer (one copy fills all three)
+        if buffers not in (1, 2):
+            raise ValueError("buffers must be 1 or 2")
+        # a step's inputs live in one flat buffer (one copy fills all three); one set per buffer
         nk = B * H * self.S * D * torch.empty((), dtype=kv_dtype).element_size()
         nq = B * self.Hq * D * torch.empty((), dtype=q_dtype).element_size()
-        self.inputs = torch.zeros(2 * nk + nq, dtype=torch.uint8, device=dev)
-        self.keys = self.inputs[:nk].view(kv_dtype).view(B, H, self.S, D)
-        self.values = self.inputs[nk:2 * nk].view(kv_dtype).view(B, H, self.S, D)
-        self.queries = self.inputs[2 * nk:].view(q_dtype).view(B, self.Hq, 1, D)
-        self.out = torch.empty((B, self.Hq, 1, D), dtype=out_dtype or q_dtype, device=dev)
+        self._sets = []
+        for _ in range(buffers):
+            inputs = torch.zeros(2 * nk + nq, dtype=torch.uint8, device=dev)
+            self._sets.append(dict(
+                inputs=inputs, keys=inputs[:nk].view(kv_dtype).view(B, H, self.S, D),
+                values=inputs[nk:2 * nk].view(kv_dtype).view(B, H, self.S, D),
+                queries=inputs[2 * nk:].view(q_dtype).view(B, self.Hq, 1, D),
+                out=torch.empty((B, self.Hq, 1, D), dtype=out_dtype or q_dtype, device=dev), graph=None))
+        self._cur = 0
         self._desc = st.descriptor()
         L = _lib.lib()
         need = ctypes.c_size_t(0)
@@ -79,14 +92,55 @@ class DecodeGraph:
         torch.cuda.synchronize(dev)
         self._attend()
         torch.cuda.synchronize(dev)
-        self.graph = torch.cuda.CUDAGraph()
-        with torch.cuda.graph(self.graph):
-            if self.S == 1:
-                self._step_fused()  # one kernel: encode each unit's token, then attend
-            else:
-                self._append()
-                self._attend()
+        for i, st_ in enumerate(self._sets):
+            self._cur = i
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                if self.S == 1:
+                    self._step_fused()  # one kernel: encode each unit's token, then attend
+                else:
+                    self._append()
+                    self._attend()
+            st_["graph"] = g
+        self._cur = 0
         torch.cuda.synchronize(dev)
+
+    # the buffer set the next replay uses
+    @property
+    def inputs(self):
+        return self._sets[self._cur]["inputs"]
+
+    @property
+    def keys(self):
+        return self._sets[self._cur]["keys"]
+
+    @property
+    def values(self):
+        return self._sets[self._cur]["values"]
+
+    @property
+    def queries(self):
+        return self._sets[self._cur]["queries"]
+
+    @property
+    def out(self):
+        return self._sets[self._cur]["out"]
+
+    @property
+    def graph(self):
+        return self._sets[self._cur]["graph"]
+
+    @property
+    def buffers(self) -> int:
+        return len(self._sets)
+
+    def inputs_of(self, k: int) -> torch.Tensor:
+        """Flat input buffer of buffer set ``k % buffers``."""
+        return self._sets[k % len(self._sets)]["inputs"]
+
+    def out_of(self, k: int) -> torch.Tensor:
+        """Output buffer of buffer set ``k % buffers``."""
+        return self._sets[k % len(self._sets)]["out"]
 
     def _append(self):
         k, v = self.keys, self.values
@@ -124,10 +178,12 @@ class DecodeGraph:
             self.len[0] = c.offset
         if c.offset + self.S > self.max_len:
             raise ValueError(f"step past max_len {self.max_len}")
-        self.graph.replay()
+        cur = self._sets[self._cur]
+        cur["graph"].replay()
         c.offset += self.S
         self._synced = c.offset
-        return self.out
+        self._cur = (self._cur + 1) % len(self._sets)
+        return cur["out"]
 
     @traced("cq.graph_step")
     def step(self, keys: torch.Tensor, values: torch.Tensor, queries: torch.Tensor) -> torch.Tensor:

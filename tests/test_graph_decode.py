@@ -66,3 +66,74 @@ def test_graph_step_matches_eager(B, Hkv, Hq, T, sk, sv, steps, headroom):
         k1, v1 = K[:, :, :1], V[:, :, :1]
         with pytest.raises(ValueError):
             g.step(k1, v1, torch.zeros((B, Hq, 1, 128), dtype=torch.bfloat16, device=dev))  # past max_len
+
+
+@pytest.mark.gpu
+def test_double_buffered_graph_matches_single():
+    """buffers=2: two captured graphs over alternating input/output sets, fed
+    from pinned host memory on a copy stream while the previous step runs
+    (the serving loop of bench.py's e2e), give bit-identical outputs and
+    cache bytes to the one-buffer graph stepping the same tokens."""
+    if not torch.cuda.is_available():
+        pytest.skip("no CUDA device")
+    from chronoquant_mlx_b200 import ChronoQuantCache, DecodeGraph
+    dev = torch.device("cuda")
+    B, Hkv, Hq, T, steps = 2, 2, 8, 700, 24
+    K, V = O.ar1_kv(B, Hkv, T + steps, 128, seed=11)
+    K = torch.from_numpy(K).to(dev).half()
+    V = torch.from_numpy(V).to(dev).half()
+    kw = dict(stride_k=64, stride_v=32, delta_bits_v=3, max_tokens=T + steps + 8)
+    one, two = ChronoQuantCache(**kw), ChronoQuantCache(**kw)
+    for c in (one, two):
+        c.update_and_fetch(K[:, :, :T], V[:, :, :T])
+    scale = 1.0 / math.sqrt(128)
+    g1 = DecodeGraph(one, Hq, scale, q_dtype=torch.bfloat16, max_len=T + steps)
+    g2 = DecodeGraph(two, Hq, scale, q_dtype=torch.bfloat16, max_len=T + steps, buffers=2)
+    assert g2.buffers == 2 and g2.inputs_of(0).data_ptr() != g2.inputs_of(1).data_ptr()
+    gen = torch.Generator(device="cpu").manual_seed(3)
+    qs = [(torch.randn((B, Hq, 1, 128), generator=gen) / math.sqrt(128)).to(torch.bfloat16) for _ in range(steps)]
+    # each step's flat input row (K | V | q bytes), pinned on the host
+    rows = []
+    for i in range(steps):
+        g1.keys.copy_(K[:, :, T + i:T + i + 1])
+        g1.values.copy_(V[:, :, T + i:T + i + 1])
+        g1.queries.copy_(qs[i].to(dev))
+        rows.append(g1.inputs.cpu().clone())
+    hin = torch.stack(rows).pin_memory()
+    ref = []
+    for i in range(steps):
+        g1.inputs.copy_(hin[i].to(dev))
+        ref.append(g1.replay().clone())
+    copy = torch.cuda.Stream(dev)
+    main = torch.cuda.current_stream()
+    ev_in, ev_done, ev_out = ([torch.cuda.Event() for _ in range(2)] for _ in range(3))
+    houts = [torch.empty((B, Hq, 1, 128), dtype=torch.bfloat16).pin_memory() for _ in range(steps)]
+
+    def h2d(k):
+        s = k % 2
+        with torch.cuda.stream(copy):
+            if k >= 2:
+                copy.wait_event(ev_done[s])
+            g2.inputs_of(s).copy_(hin[k], non_blocking=True)
+            ev_in[s].record(copy)
+
+    h2d(0)
+    for k in range(steps):
+        s = k % 2
+        if k + 1 < steps:
+            h2d(k + 1)
+        main.wait_event(ev_in[s])
+        if k >= 2:
+            main.wait_event(ev_out[s])
+        out = g2.replay()
+        assert out.data_ptr() == g2.out_of(s).data_ptr()
+        ev_done[s].record(main)
+        with torch.cuda.stream(copy):
+            copy.wait_event(ev_done[s])
+            houts[k].copy_(out, non_blocking=True)
+            ev_out[s].record(copy)
+    torch.cuda.synchronize()
+    for k in range(steps):
+        assert torch.equal(houts[k], ref[k].cpu()), k
+    for a, b in zip(one.state, two.state):
+        assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
