@@ -28,7 +28,9 @@
 //             it exceeds the running one by 8, so p <= 256);
 //   output    O += anchor_v(t) * p_t + codes_v(t) * (p_t * scale_t), both as
 //             MMAs with tokens as the reduction axis: V anchors are gathered
-//             per token with ldmatrix.trans; V codes (MMA nibble order) enter
+//             per token with ldmatrix.trans (32-token chunks), or P is summed
+//             per anchor by an indicator MMA and the chunk's anchors applied
+//             once (64-token chunks); V codes (MMA nibble order) enter
 //             as the fp16 values 64 + n = code + 72 made by bit operations
 //             alone, and 72 * sum_t(p_t * scale_t) -- one more MMA with the
 //             same fp16 weights -- is subtracted when the partial is written;
@@ -308,12 +310,14 @@ struct WarpState {
   float l[2];     // this thread's partial sums
   float o[8][4];  // O^T fragments: [m-tile i][c0..c3]
   float vb[4];    // 72 * sum of the fp16 code weights P' (same fragment layout): the V code offset
+  float ps[4];    // P summed per V anchor slot of the chunk (rows) and head
 };
 
 __device__ __forceinline__ void reset(WarpState &st) {
   st.m[0] = st.m[1] = -INFINITY;
   st.l[0] = st.l[1] = 0.f;
   st.vb[0] = st.vb[1] = st.vb[2] = st.vb[3] = 0.f;
+  st.ps[0] = st.ps[1] = st.ps[2] = st.ps[3] = 0.f;
 #pragma unroll
   for (int i = 0; i < 8; ++i)
 #pragma unroll
@@ -480,6 +484,17 @@ __device__ __forceinline__ void v_tile(WarpState &st, const VAddr &A, int tb, ui
   }
   const uint32_t bS0 = ptx::h22u(__hmul2(ptx::u2h2(bP0), ptx::u2h2(sw0)));
   const uint32_t bS1 = ptx::h22u(__hmul2(ptx::u2h2(bP1), ptx::u2h2(sw1)));
+  if (G::SPLIT) {
+    // 64-token chunks have few V anchors (2 for stride 32): P is summed per
+    // anchor slot of the chunk (rows of ps) by one MMA with an indicator
+    // matrix (row a, token k: 1 when token k belongs to anchor a), and the
+    // anchors are applied once per chunk (see do_chunk) instead of gathered
+    // for every token
+    constexpr uint32_t ONE2 = 0x3C003C00u;
+    const int gg = lane >> 2, t2 = 2 * (lane & 3);
+    const int s0 = (tb + t2) >> lsv, s1 = (tb + t2 + 8) >> lsv;
+    ptx::mma_f16_16816(st.ps, gg == s0 ? ONE2 : 0u, 0u, gg == s1 ? ONE2 : 0u, 0u, bP0, bP1);
+  } else
   // V anchors: O += A_v^T P, ldmatrix.trans gathers each token's anchor row
   {
     uint32_t base = A.kfV + (uint32_t)((tb >> lsv) * (HD * 2));
@@ -707,6 +722,20 @@ __device__ __forceinline__ bool do_chunk(const Params &p, const Len &L, WarpStat
       for (int tile = 0; tile < 2; ++tile)
         if (!MASK || grp * 32 + tile * 16 < nvalid)
           v_tile<G, MASK>(st, A, grp * 32 + tile * 16, bp[grp][tile].x, bp[grp][tile].y, nvalid, lane);
+    if (G::SPLIT) {
+      // O += A_v^T PS: the chunk's V anchors (rows = slots; past the valid ones, the last valid one, weight 0)
+      const int nA = MASK ? ((nvalid - 1) >> G::LSV) + 1 : G::AV;
+      const uint32_t b0 = ptx::movmatrix_trans(ptx::pack_half2(st.ps[0], st.ps[1]));
+      st.ps[0] = st.ps[1] = st.ps[2] = st.ps[3] = 0.f;
+      const uint32_t base = vbuf + min(lane & 7, nA - 1) * (HD * 2) + (lane >> 3) * 16;
+#pragma unroll
+      for (int i = 0; i < 4; ++i) {
+        uint32_t a0, a1, a2, a3;
+        ptx::ldmatrix_x4_trans(a0, a1, a2, a3, base + i * 64);
+        ptx::mma_f16_16816(st.o[2 * i], a0, a1, 0u, 0u, b0, 0u);
+        ptx::mma_f16_16816(st.o[2 * i + 1], a2, a3, 0u, 0u, b0, 0u);
+      }
+    }
   }
   // every lane's reads of the V part are done before the refill
   __syncwarp();
