@@ -18,11 +18,15 @@ the protocol tests) brings every rank's partials to every rank
 
     out = sum_i exp(lse_i - M) o_i / sum_i exp(lse_i - M),   M = max_i lse_i
 
-For a query chunk (q_len > 1) the chunk's own tokens sit in the tail shard,
-so the causal mask (anchored at the end of the keys, attention.py:8-20)
-applies there; every other shard's keys precede all queries and are attended
-without a mask.  The messages are small (B*Hq*q_len*(D+1) floats per rank),
-so the exchange is latency-bound rather than bandwidth-bound.
+For a query chunk (q_len > 1) the chunk's own tokens must sit in the tail
+shard: the causal mask (anchored at the end of the keys, attention.py:8-20)
+applies there, and every other shard's keys precede all queries and are
+attended without a mask.  ``sequence_parallel_attention`` checks this on
+every rank (one tiny all-reduce of the tail shard's length) and raises on all
+of them when the tail shard holds fewer than q_len tokens (short sequences,
+where ``shard_bounds`` can leave the tail short or empty).  The messages are
+small (B*Hq*q_len*(D+1) floats per rank), so the exchange is latency-bound
+rather than bandwidth-bound.
 """
 
 from __future__ import annotations
@@ -107,6 +111,16 @@ def sequence_parallel_attention(queries: torch.Tensor, cache, scale: float, grou
     rank."""
     import torch.distributed as dist
     rank, world = dist.get_rank(group), dist.get_world_size(group)
+    q_len = queries.shape[2]
+    if q_len > 1:
+        # the chunk's own tokens must all be in the tail shard (it alone is masked); every
+        # rank learns the tail's length and all raise together, before any partial exchange
+        n = torch.tensor([cache.offset if rank == world - 1 else 0], dtype=torch.int64,
+                         device=queries.device if dist.get_backend(group) == "nccl" else "cpu")
+        dist.all_reduce(n, op=dist.ReduceOp.MAX, group=group)
+        if int(n.item()) < q_len:
+            raise ValueError(f"sequence_parallel_attention: the tail shard holds {int(n.item())} tokens, fewer than "
+                             f"the {q_len} queries of the chunk; use fewer ranks or a longer sequence")
     o, lse = local_partials(queries, cache, scale, tail=rank == world - 1)
     o_all, lse_all = exchange_partials(o, lse, group)
     return merge_partials(o_all, lse_all, out_dtype=queries.dtype)

@@ -185,3 +185,29 @@ def seq_decoder_worker(rank, world, port, steps, queue):
         queue.put((rank, rels, lens, None))
     except Exception as e:
         queue.put((rank, None, None, repr(e)))
+
+
+class _ShardStub:
+    """The part of a cache the tail check reads: its token count."""
+
+    def __init__(self, n):
+        self.offset = n
+
+
+def short_tail_worker(rank, world, port, T, q_len, stride_k, stride_v, queue):
+    """sequence_parallel_attention on a sequence whose tail shard is shorter
+    than the query chunk: every rank must raise ValueError before any partial
+    is computed or exchanged."""
+    from chronoquant_mlx_b200.distributed import sequence_parallel_attention, shard_bounds
+    try:
+        _init(rank, world, port, 30)
+        lo, hi = shard_bounds(T, world, stride_k, stride_v)[rank]
+        q = torch.zeros((1, 4, q_len, 128), dtype=torch.float16)
+        try:
+            sequence_parallel_attention(q, _ShardStub(hi - lo), 0.1)
+            queue.put((rank, "no error", hi - lo))
+        except ValueError as e:
+            queue.put((rank, "raised: " + str(e), hi - lo))
+        dist.destroy_process_group()
+    except Exception as e:  # pragma: no cover - reported to the test
+        queue.put((rank, "error: " + repr(e), None))

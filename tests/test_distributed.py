@@ -97,6 +97,21 @@ def test_gloo_exchange_and_merge(q_len):
         assert np.abs(merged - ref).max() < 1e-12
 
 
+@pytest.mark.parametrize("T,world,q_len", [(64, 3, 8), (100, 2, 48)])
+def test_gloo_short_tail_shard_raises_on_every_rank(T, world, q_len):
+    """A query chunk longer than the tail shard (T=64 over 3 ranks leaves the
+    tail empty; T=100 over 2 leaves 4 tokens for 48 queries) would put some of
+    the chunk's own tokens in an unmasked shard: every rank raises instead."""
+    from chronoquant_mlx_b200.distributed import shard_bounds
+    tail = shard_bounds(T, world, 32, 8)[-1]
+    assert tail[1] - tail[0] < q_len
+    port = _free_port()
+    res, codes = _run(W.short_tail_worker, lambda r: (r, world, port, T, q_len, 32, 8), world)
+    assert codes == [0] * world
+    for rank, msg, n in res:
+        assert msg.startswith("raised:") and "tail shard" in msg, (rank, msg)
+
+
 def test_gloo_rank_failure_is_detected():
     """A rank that leaves before the exchange (a host-side failure: no GPU is
     involved) makes the other rank's collective raise instead of hanging."""
