@@ -13,6 +13,10 @@ namespace fast {
 int fast_chunk_tokens(int stride_k, int stride_v, int page_tokens);
 }
 size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len, int splits_req);
+// Offset and size in bytes of the fast kernel's per-unit completion words in
+// its workspace for this shape (size 0 when the kernel does not take it).
+size_t fast_decode_done_words(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len, int splits_req,
+                              size_t *offset);
 // A decode step's new token per (sequence, kv-head): K and V inputs at
 // b*sb + h*sh (unit dim stride), dtype f16/bf16, and the device length
 // {tokens cached, arrival counter} the step reads and advances.

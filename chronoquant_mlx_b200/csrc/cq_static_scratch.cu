@@ -14,9 +14,15 @@
 // Set-up: the first call on a device, made with that device current, looks up
 // the array's device address (cudaGetSymbolAddress) and keeps it; later calls
 // on that device reuse it.  Make that first call before any stream capture.
+// The kept address belongs to the device's primary context: resetting the
+// device (cudaDeviceReset) while the library stays loaded is not supported.
 //
-// Nothing in the scratch has to start at zero: the decode step writes every
-// partial slot that the combine step of the same call reads.
+// The array keeps the last call's contents.  The split partials are written
+// before they are read within each call, but the decode kernel counts its
+// finished CTAs in per-unit completion words whose position depends on the
+// shape, so an earlier call of another shape may have left partial values
+// there: each call first clears those words (cudaMemsetAsync on the caller's
+// stream, which allocates nothing).
 //
 // One array per device is shared by every call on it.  Two calls whose work
 // overlaps on the device (different streams, or different host threads on the
@@ -26,6 +32,7 @@
 #include <string>
 
 #include "cq_common.cuh"
+#include "cq_decode_fast.cuh"
 
 namespace cq {
 
@@ -75,6 +82,14 @@ extern "C" int cq_attention_static_scratch(const cq_paged_cache *cache, int64_t 
   void *ws = nullptr;
   r = scratch_pointer(&ws);
   if (r) return r;
+  size_t off = 0;
+  const size_t done = fast_decode_done_words(*cache, T, n_q_heads, q_len, num_splits, &off);
+  if (done) {  // the decode kernel's completion words start at zero (see above)
+    cudaError_t e = cudaMemsetAsync((char *)ws + off, 0, done, (cudaStream_t)stream);
+    if (e != cudaSuccess)
+      return set_error(CQ_ERR_CUDA, std::string("cq_attention_static_scratch: cudaMemsetAsync: ") +
+                                        cudaGetErrorString(e));
+  }
   return cq_attention(cache, T, q, q_dtype, n_q_heads, q_len, causal, q_sb, q_sh, q_sq, scale, out, out_dtype,
                       lse_out, ws, (size_t)CQ_STATIC_SCRATCH_BYTES, num_splits, stream);
 }

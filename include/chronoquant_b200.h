@@ -289,11 +289,13 @@ int cq_sdpa_reference_layout_workspace(int32_t n_q_heads, int32_t dim, int64_t s
  * allocates nothing.  A shape whose partials need more (cq_attention_workspace
  * reports the size) is rejected with CQ_ERR_WORKSPACE.  The first call on a
  * device, with that device current, looks up the array's address; make it
- * before any stream capture.  Nothing in the array needs to start at zero.
- * All calls on one device share the array: calls that overlap on the device
- * (other streams, other host threads) race and can corrupt each other's
- * results, so serialise them on one stream.  Arguments and results are those
- * of cq_attention. */
+ * before any stream capture (resetting the device afterwards is not
+ * supported).  Each call clears, on its stream, the few words of the array
+ * the decode kernel counts in (they must start at zero; the rest is written
+ * before it is read).  All calls on one device share the array: calls that
+ * overlap on the device (other streams, other host threads) race and can
+ * corrupt each other's results, so serialise them on one stream.  Arguments
+ * and results are those of cq_attention. */
 #define CQ_STATIC_SCRATCH_BYTES (8u << 20)
 int cq_attention_static_scratch(const cq_paged_cache *cache, int64_t T, const void *q, int q_dtype,
                                 int32_t n_q_heads, int32_t q_len, int32_t causal, int64_t q_sb, int64_t q_sh,

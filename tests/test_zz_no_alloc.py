@@ -4,7 +4,13 @@ library's fixed per-device scratch array instead of a caller workspace.
 Collected last (file name) so that it also runs after every other GPU test in
 the same process; it passes alone in a fresh process too.  Each case makes two
 calls in a row through the C ABI and compares both with cq_attention given a
-caller-allocated workspace, within max-abs 2e-3 / relative 1e-2."""
+caller-allocated workspace: the same kernels on the same inputs, so the
+outputs agree bit for bit (the tests' usual max-abs 2e-3 / relative 1e-2 bar
+is checked as well).  The calls must not allocate: device free memory and
+the caching allocator's counters stay unchanged across them.  Before the
+calls, the shared scratch is filled with the partials of a different shape,
+so stale contents (the decode kernel's completion words included) are
+exercised."""
 
 import ctypes
 import math
@@ -71,13 +77,29 @@ def test_static_scratch_matches_workspace_path(B, Hkv, Hq, T, q_len, stride_k, s
 
     outs = [(torch.empty((B, Hq, q_len, 128), dtype=torch.float32, device="cuda"),
              torch.empty((B, Hq, q_len), dtype=torch.float32, device="cuda")) for _ in qs]
+    # leave other partials in the shared scratch first: a decode of another shape
+    other = ChronoQuantCache(stride_k=32, stride_v=8)
+    Ko, Vo = O.ar1_kv(1, 8, 3000, 128, seed=5)
+    other.update_and_fetch(torch.from_numpy(Ko).cuda().half(), torch.from_numpy(Vo).cuda().half())
+    qo = torch.randn((1, 32, 1, 128), generator=gen).to(torch.bfloat16).cuda()
+    oo = torch.empty((1, 32, 1, 128), dtype=torch.float32, device="cuda")
+    lo = torch.empty((1, 32, 1), dtype=torch.float32, device="cuda")
+    _attention("cq_attention_static_scratch", other.store.descriptor(), 3000, qo, 0, oo, lo)
+    torch.cuda.synchronize()
+    free0 = torch.cuda.mem_get_info()[0]
+    stats0 = torch.cuda.memory_stats()
     for q, (o, lse) in zip(qs, outs):  # two calls in a row on the same scratch
         _attention("cq_attention_static_scratch", desc, T, q, causal, o, lse)
     torch.cuda.synchronize()
+    assert torch.cuda.mem_get_info()[0] == free0
+    stats1 = torch.cuda.memory_stats()
+    for k in ("allocation.all.allocated", "segment.all.allocated"):
+        assert stats1.get(k, 0) == stats0.get(k, 0), k
     for (o, lse), (ro, rlse) in zip(outs, ref):
         assert torch.isfinite(o).all()
         _close(o, ro)
         _close(lse, rlse)
+        assert torch.equal(o, ro) and torch.equal(lse, rlse)
 
 
 def test_static_scratch_rejects_oversized_shape():
