@@ -236,6 +236,39 @@ def decode_config(cfg, world, T_start):
                             f"{Bl} sequences (weak scaling; no collective)")}
 
 
+def unit_parity(cache, cfg, unit_kv):
+    """Unit (0, 0) of the benchmarked cache after all its steps, against the
+    oracle (the test checker) encoding the same fp16 tokens: its state
+    (anchors, packed codes, scales) bit for bit, and the halfway quotients
+    (rounded half to even, codec.py:50-51) counted and the device's codes
+    checked at each of them."""
+    import torch
+    sys.path.insert(0, HERE)
+    from oracle import cq_oracle as O
+    T = cache.offset
+    K, V = unit_kv
+    o = O.OracleCache(stride_k=cfg["stride_k"], stride_v=cfg["stride_v"], delta_bits_k=cfg["bits_k"],
+                      delta_bits_v=cfg["bits_v"], dead_zone_k=cfg["dz_k"], dead_zone_v=cfg["dz_v"])
+    sites = {}
+    o.update_and_fetch(K[:, :, :T], V[:, :, :T], tie_sites=sites)
+    dev = []
+    for a in cache.state:
+        a = a[0:1, 0:1].cpu()
+        dev.append(a.view(torch.int32).numpy().view(np.uint32) if a.dtype == torch.uint32 else a.numpy())
+    exact = len(dev) == len(o.state) and all(
+        np.array_equal(np.ascontiguousarray(a).view(np.uint8), np.ascontiguousarray(r).view(np.uint8))
+        for a, r in zip(dev, o.state))
+    ties, matched = {}, True
+    for comp, idx in (("k", 2), ("v", 4)):
+        mask = np.concatenate(sites[comp], axis=2)
+        dc = O.unpack_int4(np.ascontiguousarray(dev[idx]), cfg["D"])
+        oc = O.unpack_int4(np.ascontiguousarray(o.state[idx]), cfg["D"])
+        ties[comp] = int(mask.sum())
+        matched = matched and bool(np.array_equal(dc[mask], oc[mask]))
+    return {"unit": [0, 0], "tokens": T, "state_bit_exact_vs_oracle": bool(exact),
+            "halfway_quotients": ties, "halfway_codes_match": matched}
+
+
 def run_ours(args, cfg):
     import torch
     import torch.distributed as dist
@@ -269,6 +302,7 @@ def run_ours(args, cfg):
                                torch.from_numpy(V[:, :, t:t + n]).to(device))
     newK = torch.from_numpy(np.ascontiguousarray(K[:, :, T0:])).to(device)
     newV = torch.from_numpy(np.ascontiguousarray(V[:, :, T0:])).to(device)
+    unit_kv = (K[0:1, 0:1].copy(), V[0:1, 0:1].copy())  # the host copy of unit (0, 0), for the parity check
     del K, V
     g = torch.Generator(device="cpu").manual_seed(7 + rank)
     qs = (torch.randn((2 * n_new, B, Hq, 1, D), generator=g) / math.sqrt(D)).to(torch.bfloat16).to(device)
@@ -350,9 +384,10 @@ def run_ours(args, cfg):
     # back to pinned host memory.  Double-buffered on a copy stream: step
     # k+1's inputs go in while step k runs, step k's output comes out while
     # step k+1 runs; the timed region ends after the last output is home.
-    hin = pool[n_new:].cpu().pin_memory()  # each row: one step's K, V and q bytes
+    # each row: one step's K, V and q bytes, continuing the token sequence where the timed steps stopped
+    hin = pool[i_tok[0]:].cpu().pin_memory()
     hout = torch.empty((B, Hq, 1, D), dtype=torch.bfloat16).pin_memory()
-    e_steps = min(args.steps, n_new - 2)
+    e_steps = min(args.steps, hin.shape[0])
     copy = torch.cuda.Stream(device)
     ev_in = [torch.cuda.Event(), torch.cuda.Event()]
     ev_done = [torch.cuda.Event(), torch.cuda.Event()]
@@ -404,6 +439,8 @@ def run_ours(args, cfg):
 
     fp16_base = fp16_decode_baseline(cfg, cache.offset, device, reps) if world == 1 else None
 
+    parity = unit_parity(cache, cfg, unit_kv) if rank == 0 else None
+
     peak, peak_kind = load_peak()
     achieved = mean_attn_bytes / (mean_attn_ms * 1e-3) / 1e9
     traffic = None
@@ -440,6 +477,7 @@ def run_ours(args, cfg):
                          "algorithmic_bytes_per_launch": round(mean_attn_bytes),
                          "launch_ms": round(mean_attn_ms, 5), "launch_timing": "graph replays back to back"},
             "clocks": clk.summary(),
+            "parity": parity,
             "gpu_launches": args.steps,  # one fused encode+decode kernel per graph replay
             "fp16_baseline": None if fp16_base is None else dict(
                 fp16_base, compressed_bytes_per_token_kv_head=round(

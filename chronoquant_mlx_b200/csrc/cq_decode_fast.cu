@@ -459,8 +459,10 @@ __device__ __forceinline__ bool k_group(WarpState &st, const KAddr &A, const QFr
     const float p1 = fast_exp2(s[tile][1] - st.m[1]);
     const float p2 = fast_exp2(s[tile][2] - st.m[0]);
     const float p3 = fast_exp2(s[tile][3] - st.m[1]);
-    st.l[0] += p0 + p2;
-    st.l[1] += p1 + p3;
+    if (!G::SPLIT) {  // 64-token chunks sum P through the indicator MMA's all-ones row instead
+      st.l[0] += p0 + p2;
+      st.l[1] += p1 + p3;
+    }
     bp[tile] = make_uint2(ptx::movmatrix_trans(ptx::pack_half2(p0, p1)), ptx::movmatrix_trans(ptx::pack_half2(p2, p3)));
   }
   return moved;
@@ -493,7 +495,8 @@ __device__ __forceinline__ void v_tile(WarpState &st, const VAddr &A, int tb, ui
     constexpr uint32_t ONE2 = 0x3C003C00u;
     const int gg = lane >> 2, t2 = 2 * (lane & 3);
     const int s0 = (tb + t2) >> lsv, s1 = (tb + t2 + 8) >> lsv;
-    ptx::mma_f16_16816(st.ps, gg == s0 ? ONE2 : 0u, 0u, gg == s1 ? ONE2 : 0u, 0u, bP0, bP1);
+    const uint32_t r15 = gg == 7 ? ONE2 : 0u;  // row 15: every token (the softmax denominator)
+    ptx::mma_f16_16816(st.ps, gg == s0 ? ONE2 : 0u, r15, gg == s1 ? ONE2 : 0u, r15, bP0, bP1);
   } else
   // V anchors: O += A_v^T P, ldmatrix.trans gathers each token's anchor row
   {
@@ -726,6 +729,8 @@ __device__ __forceinline__ bool do_chunk(const Params &p, const Len &L, WarpStat
       // O += A_v^T PS: the chunk's V anchors (rows = slots; past the valid ones, the last valid one, weight 0)
       const int nA = MASK ? ((nvalid - 1) >> G::LSV) + 1 : G::AV;
       const uint32_t b0 = ptx::movmatrix_trans(ptx::pack_half2(st.ps[0], st.ps[1]));
+      st.l[0] += st.ps[2];  // row 15 (lanes g == 7): this chunk's sum of P per head
+      st.l[1] += st.ps[3];
       st.ps[0] = st.ps[1] = st.ps[2] = st.ps[3] = 0.f;
       const uint32_t base = vbuf + min(lane & 7, nA - 1) * (HD * 2) + (lane >> 3) * 16;
 #pragma unroll
@@ -1241,6 +1246,20 @@ size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, 
          (size_t)pl.units * sizeof(unsigned long long);
 }
 
+// Byte range of the per-unit completion words inside the workspace of
+// run_fast_decode for this shape (0 bytes when the fast kernel does not take
+// it).  A caller that reuses one workspace across shapes clears it so that
+// stale partials cannot be read as this call's counts.
+size_t fast_decode_done_words(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len, int splits_req,
+                              size_t *offset) {
+  *offset = 0;
+  if (!fast_decode_supported(c, n_q_heads, q_len)) return 0;
+  const Plan pl = make_plan(c, T, splits_req);
+  const int G = n_q_heads / c.kv_heads;
+  *offset = (size_t)(pl.nwarps + pl.grid + 2 * pl.units) * G * (2 + HD) * sizeof(float);
+  return (size_t)pl.units * sizeof(unsigned long long);
+}
+
 int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, const void *q, int q_dtype,
                     int n_q_heads, int64_t q_sb, int64_t q_sh, float scale, void *out, int out_dtype, float *lse_out,
                     void *ws, size_t ws_bytes, int splits_req, cudaStream_t st, const int64_t *T_dev,
@@ -1335,6 +1354,10 @@ bool fast_decode_supported(const cq_paged_cache &c, int n_q_heads, int q_len) {
 }
 size_t fast_decode_workspace(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len, int splits_req) {
   return fast::fast_decode_workspace(c, T, n_q_heads, q_len, splits_req);
+}
+size_t fast_decode_done_words(const cq_paged_cache &c, int64_t T, int n_q_heads, int q_len, int splits_req,
+                              size_t *offset) {
+  return fast::fast_decode_done_words(c, T, n_q_heads, q_len, splits_req, offset);
 }
 int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, const void *q, int q_dtype, int n_q_heads,
                     int64_t q_sb, int64_t q_sh, float scale, void *out, int out_dtype, float *lse_out, void *ws,

@@ -84,12 +84,15 @@ def _round_to(x64: np.ndarray, dtype: str) -> np.ndarray:
 
 
 def quantize_delta(delta: np.ndarray, bits: int, dead_zone: float = 0.0, dtype: str = "f16",
-                   tie_counter: list | None = None):
+                   tie_counter: list | None = None, tie_sites: list | None = None):
     """Restates ``ChronoQuantCodecMLX.quantize_delta`` (codec.py:23-65).
 
     ``delta``: [..., D] values of the token dtype (fp16, or bf16 held in
     float32).  Every arithmetic step is rounded to that dtype.  Returns
     ``codes`` int8 [..., D] and ``scale`` fp16 [..., 1] (codec.py:65).
+    ``tie_counter`` collects the number of quotients exactly halfway between
+    two integers (rounded half to even, codec.py:50-51); ``tie_sites`` their
+    boolean positions (same shape as ``codes``).
     """
     hl = half_levels(bits)
     d = np.asarray(delta)
@@ -112,9 +115,12 @@ def quantize_delta(delta: np.ndarray, bits: int, dead_zone: float = 0.0, dtype: 
         # codec.py:48-54
         scale_safe = np.where(scale < tiny, 1.0, scale)
         q = _round_to(d64 / scale_safe, dtype).astype(np.float64)
-        if tie_counter is not None:
+        if tie_counter is not None or tie_sites is not None:
             frac = np.abs(q - np.trunc(q))
-            tie_counter.append(int(np.count_nonzero(frac == 0.5)))
+            if tie_counter is not None:
+                tie_counter.append(int(np.count_nonzero(frac == 0.5)))
+            if tie_sites is not None:
+                tie_sites.append(frac == 0.5)
         r = np.rint(q)
         r = np.clip(r, -hl, hl - 1)
         r = np.where(scale < tiny, 0.0, r)
@@ -201,7 +207,7 @@ def _to_dtype_array(x: np.ndarray, dtype: str) -> np.ndarray:
 
 def encode_component(x: np.ndarray, t0: int, stride: int, bits: int, dead_zone: float,
                      existing_kf: np.ndarray | None, dtype: str = "f16",
-                     tie_counter: list | None = None):
+                     tie_counter: list | None = None, tie_sites: list | None = None):
     """Vectorised restatement of ``_append_component`` (cache.py:87-129).
 
     ``x``: [B, H, S, D] new tokens at absolute positions t0..t0+S-1 (fp16, or
@@ -229,7 +235,7 @@ def encode_component(x: np.ndarray, t0: int, stride: int, bits: int, dead_zone: 
     else:
         a_bf = round_bf16(anchors.astype(np.float32))
         delta = round_bf16((tok.astype(np.float64) - a_bf.astype(np.float64)).astype(np.float32))
-    codes, scale = quantize_delta(delta, bits, dead_zone, dtype, tie_counter)
+    codes, scale = quantize_delta(delta, bits, dead_zone, dtype, tie_counter, tie_sites)
     packed = pack_int4(codes)
     return kf_new, packed, scale[..., 0].astype(F16)
 
@@ -328,9 +334,9 @@ class OracleCache:
             return self.per_layer_v_bits[min(self.layer_idx, len(self.per_layer_v_bits) - 1)]
         return self.delta_bits_v
 
-    def _append(self, comp, x, stride, bits, dz, tie_counter=None):
-        kf_new, pk, sc = encode_component(x, self.offset, stride, bits, dz, self.kf.get(comp),
-                                          self.dtype, tie_counter)
+    def _append(self, comp, x, stride, bits, dz, tie_counter=None, tie_sites=None):
+        kf_new, pk, sc = encode_component(x, self.offset, stride, bits, dz, self.kf.get(comp), self.dtype,
+                                          tie_counter, None if tie_sites is None else tie_sites.setdefault(comp, []))
         if kf_new.shape[2]:
             self.kf[comp] = kf_new if comp not in self.kf else np.concatenate([self.kf[comp], kf_new], 2)
         if pk.shape[2]:
@@ -340,15 +346,17 @@ class OracleCache:
                 self.packed[comp] = np.concatenate([self.packed[comp], pk], 2)
                 self.scales[comp] = np.concatenate([self.scales[comp], sc], 2)
 
-    def update_and_fetch(self, keys, values, tie_counter=None):
-        """cache.py:198-215."""
+    def update_and_fetch(self, keys, values, tie_counter=None, tie_sites=None):
+        """cache.py:198-215.  ``tie_sites`` (a dict): per component ("k",
+        "v") a list of boolean [B, H, n_pframes, D] masks of the halfway
+        quotients of each call, in the order of the packed rows."""
         D = keys.shape[-1]
         if self.head_dim is None:
             self.head_dim = D
         elif D != self.head_dim:
             raise ValueError(f"ChronoQuantCache head_dim changed: {self.head_dim} -> {D}")
-        self._append("k", keys, self.stride_k, self.delta_bits_k, self.dead_zone_k, tie_counter)
-        self._append("v", values, self.stride_v, self.v_bits(), self.dead_zone_v, tie_counter)
+        self._append("k", keys, self.stride_k, self.delta_bits_k, self.dead_zone_k, tie_counter, tie_sites)
+        self._append("v", values, self.stride_v, self.v_bits(), self.dead_zone_v, tie_counter, tie_sites)
         self.offset += keys.shape[2]
         return keys, values
 

@@ -357,6 +357,23 @@ def test_prefill_chunk_causal_vs_exact():
     close(npy(out), O.fallback_sdpa(q, "f16", fk, fv, scale, "causal"))
 
 
+def assert_ties_match(dev_state, ora_state, tie_sites, D=128):
+    """The quotients the oracle found exactly halfway between two integers
+    (codec.py:50-51 rounds them half to even): check that the device's codes
+    equal the oracle's at every one of them.  Returns the tie count per
+    component ("k", "v").  States are the reference layout [kf_k, kf_v,
+    packed_k, scales_k, packed_v, scales_v] of one (sequence, kv-head)."""
+    counts = {}
+    for comp, idx in (("k", 2), ("v", 4)):
+        mask = np.concatenate(tie_sites[comp], axis=2)
+        dev = O.unpack_int4(np.ascontiguousarray(dev_state[idx]), D)
+        ora = O.unpack_int4(np.ascontiguousarray(ora_state[idx]), D)
+        assert mask.shape == dev.shape == ora.shape
+        assert np.array_equal(dev[mask], ora[mask])
+        counts[comp] = int(mask.sum())
+    return counts
+
+
 def test_full_size_config2_properties():
     """bench config 2 sizes (B8 Hkv8 Hq32 T16384): encode of two rows
     bit-exact against the oracle, export->import idempotent, decode of two
@@ -370,10 +387,13 @@ def test_full_size_config2_properties():
     st = c.state
     for (b, h) in ((0, 0), (7, 5)):
         o = O.OracleCache(stride_k=32, stride_v=8, dead_zone_v=0.0)
-        o.update_and_fetch(K[b:b + 1, h:h + 1], V[b:b + 1, h:h + 1])
-        for a, r in zip(st, o.state):
-            a = npy(a[b:b + 1, h:h + 1])
+        sites = {}
+        o.update_and_fetch(K[b:b + 1, h:h + 1], V[b:b + 1, h:h + 1], tie_sites=sites)
+        dev = [npy(a[b:b + 1, h:h + 1]) for a in st]
+        for a, r in zip(dev, o.state):
             assert np.array_equal(np.ascontiguousarray(a).view(np.uint8), np.ascontiguousarray(r).view(np.uint8))
+        ties = assert_ties_match(dev, o.state, sites)
+        print(f"config 2 unit ({b},{h}): {ties['k']} K and {ties['v']} V halfway quotients, all matched")
     c2 = ChronoQuantCache(stride_k=32, stride_v=8, dead_zone_v=0.0)
     c2.state = st
     for a, b in zip(st, c2.state):
@@ -469,3 +489,40 @@ def test_decode_fast_vs_generic_small_T(T):
     g.use_fused = False
     out2 = chronoquant_sdpa(cu(q), None, None, g, scale)
     close(npy(out2), npy(out))
+
+
+def test_full_size_config3_properties():
+    """bench config 3 sizes (B16 Hkv8 Hq32 T32768, Full-Throttle V3: strides
+    64/32, 4/3 bits, dead zones 0/0.05, AR(1) K/V with rho 0.97/0.85): the
+    state of three sampled (sequence, kv-head) units bit-exact against the
+    oracle (halfway quotients counted and matched), decode of their query
+    heads on the sm_100a kernel against exact float64 attention and against
+    the reference's fp16 fallback (B > 1), within 2e-3 / 1e-2."""
+    from chronoquant_mlx_b200 import ChronoQuantCache, chronoquant_sdpa
+    B, H, T, D = 16, 8, 32768, 128
+    kw = dict(stride_k=64, stride_v=32, delta_bits_k=4, delta_bits_v=3, dead_zone_k=0.0, dead_zone_v=0.05)
+    K, V = O.ar1_kv_fast(B, H, T, D, rho_k=0.97, rho_v=0.85, seed=3)
+    c = ChronoQuantCache(max_tokens=T + 64, **kw)
+    for t in range(0, T, 8192):  # prefill in chunks, as a serving loop would
+        c.update_and_fetch(cu(K[:, :, t:t + 8192]), cu(V[:, :, t:t + 8192]))
+    st = c.state
+    q = (np.random.default_rng(4).standard_normal((B, 32, 1, D)) / math.sqrt(D)).astype(np.float32)
+    qb = O.round_bf16(q)
+    scale = 1.0 / math.sqrt(D)
+    out = npy(chronoquant_sdpa(cu(qb, torch.bfloat16), None, None, c, scale))
+    qs = O.round_bf16(qb.astype(np.float64) * float(O.round_bf16(np.float32(scale))))
+    for (b, h) in ((0, 0), (9, 3), (15, 7)):
+        o = O.OracleCache(**kw)
+        sites = {}
+        for t in range(0, T, 8192):
+            o.update_and_fetch(K[b:b + 1, h:h + 1, t:t + 8192], V[b:b + 1, h:h + 1, t:t + 8192], tie_sites=sites)
+        dev = [npy(a[b:b + 1, h:h + 1]) for a in st]
+        for a, r in zip(dev, o.state):
+            assert np.array_equal(np.ascontiguousarray(a).view(np.uint8), np.ascontiguousarray(r).view(np.uint8))
+        ties = assert_ties_match(dev, o.state, sites)
+        print(f"config 3 unit ({b},{h}): {ties['k']} K and {ties['v']} V halfway quotients, all matched")
+        k32, v32 = o.reconstruct_history_f32()
+        rows = slice(4 * h, 4 * h + 4)
+        close(out[b:b + 1, rows], O.exact_sdpa(qs[b:b + 1, rows], k32, v32, False))
+        fk, fv = o.reconstruct_history()
+        close(out[b:b + 1, rows], O.fallback_sdpa(qb[b:b + 1, rows], "bf16", fk, fv, scale, None))

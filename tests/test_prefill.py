@@ -128,9 +128,12 @@ def test_prefill_lse_and_strided_queries():
 
 def test_prefill_config4_sampled_rows():
     """bench config 4: B1 Hq32 Hkv8 D128, 65536 compressed tokens then a
-    2048-token chunk (Standard strides), causal.  Sampled rows (query-tile
-    edges, first/last tokens, every GQA position) against exact float64
-    attention on the device's fp16 reconstruction."""
+    2048-token chunk (Standard strides), causal.  For the kv-heads of the
+    sampled rows (query-tile edges, first/last tokens, every GQA position) the
+    oracle encodes the same tokens on the CPU; its fp16 reconstruction
+    (cache.py:131-160, the reference's fallback input) must equal the
+    device's bit for bit, and the sampled rows must match exact float64
+    attention over the oracle's reconstruction."""
     from chronoquant_mlx_b200 import ChronoQuantCache, chronoquant_sdpa
     B, Hkv, Hq, ctx, chunk = 1, 8, 32, 65536, 2048
     T = ctx + chunk
@@ -138,21 +141,31 @@ def test_prefill_config4_sampled_rows():
     cache = ChronoQuantCache(stride_k=32, stride_v=8)
     cache.update_and_fetch(torch.from_numpy(K[:, :, :ctx]).cuda(), torch.from_numpy(V[:, :, :ctx]).cuda())
     cache.update_and_fetch(torch.from_numpy(K[:, :, ctx:]).cuda(), torch.from_numpy(V[:, :, ctx:]).cuda())
-    del K, V
     q = O.round_bf16((np.random.default_rng(7).standard_normal((B, Hq, chunk, 128)) / math.sqrt(128))
                      .astype(np.float32))
     scale = 1.0 / math.sqrt(128)
     out = npy(chronoquant_sdpa(torch.from_numpy(q).cuda().to(torch.bfloat16), None, None, cache, scale,
                                mask="causal"))
     assert np.isfinite(out).all()
-    fk, fv = (npy(t).astype(np.float64) for t in cache.reconstruct_history())
+    dk, dv = (npy(t) for t in cache.reconstruct_history())
     qs = scaled_q(q, "bf16", scale).astype(np.float64)
     toks = [0, 1, 31, 32, 63, 1000, 2015, 2016, 2047]
-    for hq in (0, 5, 10, 15, 20, 27, 31):
-        kh = hq // (Hq // Hkv)
+    heads = (0, 5, 10, 15, 20, 27, 31)
+    recon = {}
+    for kh in sorted({hq // (Hq // Hkv) for hq in heads}):
+        o = O.OracleCache(stride_k=32, stride_v=8)
+        o.update_and_fetch(K[:, kh:kh + 1, :ctx], V[:, kh:kh + 1, :ctx])
+        o.update_and_fetch(K[:, kh:kh + 1, ctx:], V[:, kh:kh + 1, ctx:])
+        fk, fv = o.reconstruct_history()
+        assert np.array_equal(dk[:, kh:kh + 1].astype(np.float16).view(np.uint16), fk.view(np.uint16))
+        assert np.array_equal(dv[:, kh:kh + 1].astype(np.float16).view(np.uint16), fv.view(np.uint16))
+        recon[kh] = (fk[0, 0].astype(np.float64), fv[0, 0].astype(np.float64))
+    del K, V
+    for hq in heads:
+        fk, fv = recon[hq // (Hq // Hkv)]
         for i in toks:
             lim = ctx + i + 1
-            s = fk[0, kh, :lim] @ qs[0, hq, i]
+            s = fk[:lim] @ qs[0, hq, i]
             p = np.exp(s - s.max())
-            ref = (p @ fv[0, kh, :lim]) / p.sum()
+            ref = (p @ fv[:lim]) / p.sum()
             close(out[0, hq, i], O.round_bf16(ref.astype(np.float32)), ATOL, RTOL)
