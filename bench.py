@@ -365,7 +365,7 @@ def run_ours(args, cfg):
     with torch.cuda.graph(attn_graph):
         dg._attend()
     torch.cuda.synchronize()
-    reps = max(20, args.steps)
+    reps = max(100, args.steps)
     a0 = torch.cuda.Event(enable_timing=True)
     a1 = torch.cuda.Event(enable_timing=True)
     attn_graph.replay()
