@@ -492,6 +492,77 @@ def run_ours(args, cfg):
         dist.destroy_process_group()
 
 
+def run_vpack3(args, cfg):
+    """The decode step over a cache with physical 3-bit V codes
+    (ChronoQuantCache(v_pack=3), opt-in; config 3's V codes are 3-bit),
+    stepped eagerly (update_and_fetch of one token + chronoquant_sdpa, which
+    runs the sm_100a decode kernel's bit-plane path), beside the same eager
+    steps over the INT4-lane store.  GB/s counts the bytes each store holds
+    (``physical_nbytes``: the reference's accounting cannot express 3-bit
+    rows).  One GPU."""
+    import torch
+    sys.path.insert(0, HERE)
+    from chronoquant_mlx_b200 import ChronoQuantCache, chronoquant_sdpa
+    device = torch.device("cuda", 0)
+    B, H, Hq, D, T0 = cfg["B"], cfg["Hkv"], cfg["Hq"], cfg["D"], cfg["T"]
+    n = args.warmup + args.steps
+    K, V = ar1_host(B, H, T0 + n, D, cfg["rho_k"], cfg["rho_v"], seed=1000)
+    caches = {}
+    for pack in (4, 3):
+        c = ChronoQuantCache(stride_k=cfg["stride_k"], stride_v=cfg["stride_v"], delta_bits_k=cfg["bits_k"],
+                             delta_bits_v=cfg["bits_v"], dead_zone_k=cfg["dz_k"], dead_zone_v=cfg["dz_v"],
+                             max_tokens=T0 + n + 8, v_pack=pack)
+        for t in range(0, T0, 4096):
+            c.update_and_fetch(torch.from_numpy(K[:, :, t:t + min(4096, T0 - t)]).to(device),
+                               torch.from_numpy(V[:, :, t:t + min(4096, T0 - t)]).to(device))
+        caches[pack] = c
+    newK = torch.from_numpy(np.ascontiguousarray(K[:, :, T0:])).to(device)
+    newV = torch.from_numpy(np.ascontiguousarray(V[:, :, T0:])).to(device)
+    del K, V
+    g = torch.Generator(device="cpu").manual_seed(7)
+    qs = (torch.randn((n, B, Hq, 1, D), generator=g) / math.sqrt(D)).to(torch.bfloat16).to(device)
+    scale = 1.0 / math.sqrt(D)
+    stream = torch.cuda.current_stream()
+    res = {}
+    for pack in (3, 4):
+        c = caches[pack]
+        for j in range(args.warmup):
+            c.update_and_fetch(newK[:, :, j:j + 1], newV[:, :, j:j + 1])
+            chronoquant_sdpa(qs[j], None, None, c, scale)
+        torch.cuda.synchronize()
+        T_start = c.offset
+        b0 = c.physical_nbytes
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        for j in range(args.warmup, n):
+            c.update_and_fetch(newK[:, :, j:j + 1], newV[:, :, j:j + 1])
+            out = chronoquant_sdpa(qs[j], None, None, c, scale)
+        e1.record(stream)
+        torch.cuda.synchronize()
+        ms = e0.elapsed_time(e1) / args.steps
+        byts = (b0 + c.physical_nbytes) / 2 + 2 * B * Hq * D * 2  # mean over the steps, plus q and out
+        res[pack] = dict(ms=ms, gbs=byts / (ms * 1e-3) / 1e9, T_start=T_start,
+                         bytes_per_token_kv_head=round(c.physical_nbytes / (B * H * c.offset), 2),
+                         reference_accounting_bytes_per_token_kv_head=round(c.nbytes / (B * H * c.offset), 2))
+    r3, r4 = res[3], res[4]
+    out = {
+        "metric": METRIC, "value": round(r3["gbs"], 2), "unit": "GB/s", "n_gpus": 1, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(r3["ms"], 5), "higher_is_better": True, "scaling": "weak",
+        "vs_baseline": None, "dtype": "3-bit residual V (bit planes), INT4 K, f16 anchors, bf16 q, f32 accumulate",
+        "data": "synthetic AR(1) K/V (seeded), random bf16 queries",
+        "config": dict(decode_config(cfg, 1, r3["T_start"]), v_pack=3,
+                       step="append 1 token per (sequence, kv-head) + decode attention, eager "
+                            "(update_and_fetch + chronoquant_sdpa): the decode kernel's bit-plane path"),
+        "bytes_per_token_kv_head": r3["bytes_per_token_kv_head"],
+        "reference_accounting_bytes_per_token_kv_head": r3["reference_accounting_bytes_per_token_kv_head"],
+        "int4_lanes_same_path": {"ms_per_step": round(r4["ms"], 5), "value": round(r4["gbs"], 2),
+                                 "bytes_per_token_kv_head": r4["bytes_per_token_kv_head"],
+                                 "note": "the same eager steps over the INT4-lane store"},
+        "gpu_launches": None,
+    }
+    print(json.dumps(out))
+
+
 def run_prefill(args, cfg):
     """Config 4: one step = encode a 2048-token chunk into the compressed cache
     (context 65536 tokens) and attend its 2048 causal queries over all 67584
@@ -1056,6 +1127,9 @@ def main():
     ap.add_argument("--seqsplit", action="store_true",
                     help="config 5: one sequence (batch 1, 524288-token context unless --context), split by "
                          "token ranges over the torchrun ranks")
+    ap.add_argument("--v-pack", type=int, default=4, choices=[3, 4],
+                    help="decode configs: 3 = physical 3-bit V codes (ChronoQuantCache(v_pack=3), opt-in; needs "
+                         "3-bit V codes, i.e. config 3), stepped eagerly beside the INT4-lane store")
     ap.add_argument("--context", type=int, default=None,
                     help="config 4: cached tokens before the chunk (default 65536; smaller for profiler "
                          "captures); config 5: context tokens")
@@ -1084,6 +1158,15 @@ def main():
             run_reference_prefill(args, cfg)
         else:
             run_prefill(args, cfg)
+        return
+    if args.v_pack == 3:
+        if cfg["bits_v"] > 3:
+            ap.error("--v-pack 3 needs 3-bit V codes (config 3)")
+        if args.impl == "reference":
+            print(json.dumps({"impl": "reference", "unavailable": "the reference has no physical 3-bit format "
+                              "(README.md:57); its arm is the INT4-lane config 3 line"}))
+        else:
+            run_vpack3(args, cfg)
         return
     if args.impl == "reference":
         run_reference(args, cfg)

@@ -13,7 +13,13 @@ rows and fp16 scales (``PagedStore``).  The anchors and code rows are exactly
 the reference's per-token bytes, so ``nbytes`` (the active-byte accounting of
 cache.py:274-287) is unchanged; scales are stored per token (2 bytes more per
 I-frame).  V code rows use the decode kernel's nibble order when head_dim is
-128; ``state`` converts to the reference layout.  Appending never copies
+128; ``state`` converts to the reference layout.  ``v_pack=3`` (opt-in, V
+codes of 3 bits or fewer) stores V code rows physically in 3 bits per value
+(two bit planes, 48 bytes per row at head_dim 128 instead of 64; the decode
+kernel reads them for the (64, 32) and (32, 8) stride pairs, the general
+kernel otherwise), ``state`` still exports INT4 lanes, and ``nbytes`` keeps
+the reference accounting while ``physical_nbytes`` reports what the store
+holds.  Appending never copies
 history except when the page pool grows (geometrically, or never with
 ``max_tokens``).
 """
@@ -62,6 +68,7 @@ def _num_keyframes(num_tokens: int, stride: int) -> int:
 class _Component:
     def __init__(self, stride: int, bits: int, dead_zone: float, page_tokens: int, head_dim: int, order: int):
         self.stride = stride
+        self.row_words = 12 if order == _lib.CQ_ORDER_PLANES3 else (head_dim + 7) // 8  # PLANES3: head_dim 128
         self.bits = bits
         self.dead_zone = float(dead_zone)
         self.apg = page_tokens // stride
@@ -104,7 +111,7 @@ class PagedStore:
             comp.off_kf = off
             off = _up16(off + a * head_dim * 2)
             comp.off_cd = off
-            off = _up16(off + (self.chunk - a) * self.W * 4)
+            off = _up16(off + (self.chunk - a) * comp.row_words * 4)
             comp.off_sc = off
             off = _up16(off + self.chunk * 2)
         self.chunk_bytes = off
@@ -177,12 +184,14 @@ class ChronoQuantCache:
 
     Arguments follow cache.py:21-31.  Keyword-only extras: ``page_tokens``
     (page size; default the multiple of lcm(stride_k, stride_v, 16) nearest
-    256 from below) and ``max_tokens`` (pre-size the page pool)."""
+    256 from below), ``max_tokens`` (pre-size the page pool) and ``v_pack``
+    (4: V codes in INT4 lanes as the reference stores them; 3: physically 3
+    bits per value, for V codes of 3 bits or fewer)."""
 
     def __init__(self, stride_k: int = 32, stride_v: int = 8, delta_bits_k: int = 4, delta_bits_v: int = 4,
                  dead_zone_k: float = 0.0, dead_zone_v: float = 0.05, use_fused: bool = True,
                  per_layer_v_bits: list = None, layer_idx: int = 0, *, page_tokens: int | None = None,
-                 max_tokens: int | None = None):
+                 max_tokens: int | None = None, v_pack: int = 4):
         if int(stride_k) < 1 or int(stride_v) < 1:
             raise ValueError("strides must be >= 1")
         self.stride_k = stride_k
@@ -203,6 +212,11 @@ class ChronoQuantCache:
             raise ValueError("page_tokens must be a multiple of stride_k and stride_v")
         self.page_tokens = int(page_tokens)
         self.max_tokens = max_tokens
+        if int(v_pack) not in (3, 4):
+            raise ValueError("v_pack must be 4 (INT4 lanes) or 3 (physical 3-bit codes)")
+        self.v_pack = int(v_pack)
+        if self.v_pack == 3 and self._get_codec_for_v().delta_bits > 3:
+            raise ValueError(f"v_pack=3 needs V codes of at most 3 bits, got {self._get_codec_for_v().delta_bits}")
         self._store: PagedStore | None = None
         self._workspace = None
 
@@ -229,6 +243,11 @@ class ChronoQuantCache:
             raise NotImplementedError(f"head_dim {D} unsupported (multiple of 8, <= 256)")
         cv = self._get_codec_for_v()
         v_order = _lib.CQ_ORDER_MMA if D == 128 else _lib.CQ_ORDER_NATURAL
+        if self.v_pack == 3:
+            if cv.delta_bits > 3 or D != 128:
+                raise ValueError(f"v_pack=3 needs V codes of at most 3 bits (got {cv.delta_bits}) and head_dim 128 "
+                                 f"(got {D})")
+            v_order = _lib.CQ_ORDER_PLANES3
         comps = [_Component(self.stride_k, self.delta_bits_k, self.dead_zone_k, self.page_tokens, D,
                             _lib.CQ_ORDER_NATURAL),
                  _Component(self.stride_v, cv.delta_bits, self.dead_zone_v, self.page_tokens, D, v_order)]
@@ -448,13 +467,13 @@ class ChronoQuantCache:
     # saved cache restores self-described; "" is still accepted.
     _META_TAG = "chronoquant/1"
     _META_KEYS = ("stride_k", "stride_v", "delta_bits_k", "delta_bits_v", "dead_zone_k", "dead_zone_v",
-                  "use_fused", "per_layer_v_bits", "layer_idx", "page_tokens")
+                  "use_fused", "per_layer_v_bits", "layer_idx", "page_tokens", "v_pack")
 
     @property
     def meta_state(self):
         vals = [self.stride_k, self.stride_v, self.delta_bits_k, self.delta_bits_v, repr(float(self.dead_zone_k)),
                 repr(float(self.dead_zone_v)), int(bool(self.use_fused)),
-                ",".join(str(int(b)) for b in self.per_layer_v_bits), self.layer_idx, self.page_tokens]
+                ",".join(str(int(b)) for b in self.per_layer_v_bits), self.layer_idx, self.page_tokens, self.v_pack]
         return (self._META_TAG,) + tuple(f"{k}={v}" for k, v in zip(self._META_KEYS, vals))
 
     @meta_state.setter
@@ -479,7 +498,8 @@ class ChronoQuantCache:
                       dead_zone_k=float(kv["dead_zone_k"]), dead_zone_v=float(kv["dead_zone_v"]),
                       use_fused=bool(int(kv["use_fused"])),
                       per_layer_v_bits=[int(b) for b in bits_v.split(",")] if bits_v else None,
-                      layer_idx=int(kv["layer_idx"]), page_tokens=int(kv["page_tokens"]), max_tokens=self.max_tokens)
+                      layer_idx=int(kv["layer_idx"]), page_tokens=int(kv["page_tokens"]), max_tokens=self.max_tokens,
+                      v_pack=int(kv.get("v_pack", 4)))
         self._codec_v = None  # V bits may have changed
 
     def is_trimmable(self):
@@ -504,4 +524,19 @@ class ChronoQuantCache:
             nkf = self._num_keyframes(self.offset, s)
             npf = self.offset - nkf
             total += st.B * st.H * (nkf * st.D * 2 + npf * st.W * 4 + npf * 2)
+        return total
+
+    @property
+    def physical_nbytes(self) -> int:
+        """The same active slices at the bytes the store holds them in: equal to
+        ``nbytes`` except with ``v_pack=3``, whose V code rows take 3 bits per
+        value."""
+        if self._store is None or self.offset == 0:
+            return 0
+        st = self._store
+        total = 0
+        for s, c in zip((self.stride_k, self.stride_v), st.comps):
+            nkf = self._num_keyframes(self.offset, s)
+            npf = self.offset - nkf
+            total += st.B * st.H * (nkf * st.D * 2 + npf * c.row_words * 4 + npf * 2)
         return total

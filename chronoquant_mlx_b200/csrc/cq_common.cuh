@@ -73,7 +73,7 @@ inline CacheView make_view(const cq_paged_cache &c) {
     v.c[i].bits = src[i]->bits;
     v.c[i].dead_zone = src[i]->dead_zone;
     const cq_component &k = *src[i];
-    const int W = (c.head_dim + 7) >> 3;
+    const int W = k.code_order == CQ_ORDER_PLANES3 ? 12 : (c.head_dim + 7) >> 3;  // row words
     const int ct = k.chunk_tokens > 0 ? k.chunk_tokens : c.page_tokens;
     v.c[i].ac = ct / k.stride;
     v.c[i].pc = ct - v.c[i].ac;
@@ -108,6 +108,10 @@ __host__ __device__ inline int64_t scale_index(const CompView &c, int H, int64_t
 int validate_cache(const cq_paged_cache *c);
 
 __host__ __device__ inline int words_of(int D) { return (D + 7) >> 3; }
+// Words of one code row in the cache's layout (the reference layout is words_of).
+__host__ __device__ inline int row_words(int D, int order) {
+  return order == CQ_ORDER_PLANES3 ? 12 : words_of(D);  // PLANES3: head_dim 128
+}
 
 // Position of dim d's nibble in a code row: word index and bit shift.
 // NATURAL: word d/8, nibble d%8 (kernels.py:15-19).  MMA (head_dim multiple of
@@ -206,16 +210,36 @@ __device__ __forceinline__ TokLoc locate(const CacheView &cv, int comp, int b, i
     L.scale = 0.f;
   } else {
     int pf = tl - a - 1;
-    L.codes = c.codes + code_index(c, cv.H, words_of(cv.D), pg, h, pf);
+    L.codes = c.codes + code_index(c, cv.H, row_words(cv.D, c.order), pg, h, pf);
     L.scale = __half2float(c.scales[scale_index(c, cv.H, pg, h, c.stok ? tl : pf)]);
   }
   return L;
 }
 
 __device__ __forceinline__ int nibble_at(const uint32_t *row, int d, int D, int order) {
+  if (order == CQ_ORDER_PLANES3) {  // code + 4 from two planes (head_dim 128), returned as code + 8
+    const int g = d & 7, k = d >> 3;
+    const uint32_t lo = (row[g] >> (2 * k)) & 3u, hi = (row[8 + (g >> 1)] >> (16 * (g & 1) + k)) & 1u;
+    return (int)(lo | (hi << 2)) + 4;
+  }
   int w, s;
   nibble_pos(d, D, order, w, s);
   return (int)((row[w] >> s) & 0xFu);
+}
+
+// ORs the stored value of dim d (nib = code + 8, the INT4-lane value) into a
+// code row being assembled in warp-shared words `sw` (zeroed beforehand).
+__device__ __forceinline__ void pack_code(uint32_t *sw, int d, int D, int order, uint32_t nib) {
+  if (order == CQ_ORDER_PLANES3) {  // head_dim 128
+    const uint32_t v = nib - 4u;  // code + 4, in [0, 8) for codes of 3 bits or fewer
+    const int g = d & 7, k = d >> 3;
+    atomicOr(&sw[g], (v & 3u) << (2 * k));
+    atomicOr(&sw[8 + (g >> 1)], (v >> 2) << (16 * (g & 1) + k));
+    return;
+  }
+  int w, s;
+  nibble_pos(d, D, order, w, s);
+  atomicOr(&sw[w], nib << s);
 }
 
 // ---------------------------------------------------------------------------

@@ -128,7 +128,7 @@ __device__ __forceinline__ void encode_token(const EncodeArgs &A, int64_t t0, ui
   }
 
   const float scale = encode_residual<DTYPE>(xv, av, D, c.bits, c.dead_zone, c.order, sw, lane);
-  const int W = words_of(D);
+  const int W = row_words(D, c.order);
   const int pf = tl - a - 1;
   uint32_t *code_row = const_cast<uint32_t *>(c.codes) + code_index(c, cv.H, W, pg, h, pf);
   if (lane < W) code_row[lane] = sw[lane];

@@ -23,7 +23,7 @@ __device__ __forceinline__ int quantise_code(float q, float hl, bool zero_scale)
 // Codes and scale of one P-frame token, computed by one warp.  xv: the
 // token's values (exact in DTYPE), av: its anchor's fp16 values, for dims
 // lane + 32 i.  Packs the nibbles (+8 bias, kernels.py:40) of the code row in
-// `order` into sw[0 .. words_of(D)) (warp-private shared memory) and returns
+// `order` into sw[0 .. row_words(D, order)) (warp-private shared memory) and returns
 // the scale in DTYPE precision (stored as fp16 by the caller, cache.py:116).
 template <int DTYPE>
 __device__ __forceinline__ float encode_residual(const float (&xv)[kMaxDimsPerLane],
@@ -70,9 +70,7 @@ __device__ __forceinline__ float encode_residual(const float (&xv)[kMaxDimsPerLa
       float q = round_dt(__fdiv_rn(dv[i], scale_safe), DTYPE);
       int code = quantise_code(q, hl, zero_scale);
       uint32_t nib = (uint32_t)min(max(code + 8, 0), 15);  // kernels.py:40
-      int w, sh;
-      nibble_pos(d, D, order, w, sh);
-      atomicOr(&sw[w], nib << sh);
+      pack_code(sw, d, D, order, nib);
     }
   }
   __syncwarp();

@@ -75,7 +75,7 @@ __global__ void export_kernel(CacheView cv, int comp, int64_t nkf, int64_t npf, 
   const int64_t pg = page_of(cv, b, lp);
   const int a = tl / c.stride;
   const int pf = tl - a - 1;
-  uint32_t *crow = const_cast<uint32_t *>(c.codes) + code_index(c, cv.H, W, pg, h, pf);
+  uint32_t *crow = const_cast<uint32_t *>(c.codes) + code_index(c, cv.H, row_words(D, c.order), pg, h, pf);
   __half *cscale = const_cast<__half *>(c.scales) + scale_index(c, cv.H, pg, h, c.stok ? tl : pf);
   uint32_t *rrow = pk_out + (bh * npf + j) * W;
   if (lane < W) {
@@ -97,12 +97,10 @@ __global__ void export_kernel(CacheView cv, int comp, int64_t nkf, int64_t npf, 
     __syncwarp();
     for (int d = lane; d < D; d += 32) {
       uint32_t nib = (rrow[d >> 3] >> ((d & 7) * 4)) & 0xFu;
-      int w, s;
-      nibble_pos(d, D, c.order, w, s);
-      atomicOr(&sw[w], nib << s);
+      pack_code(sw, d, D, c.order, nib);
     }
     __syncwarp();
-    if (lane < W) crow[lane] = sw[lane];
+    if (lane < row_words(D, c.order)) crow[lane] = sw[lane];
     if (lane == 0) *cscale = sc_out[bh * npf + j];
   } else if (lane == 0) {
     sc_out[bh * npf + j] = *cscale;

@@ -109,6 +109,11 @@ __device__ __forceinline__ uint32_t lds_u32(uint32_t a) {
   asm volatile("ld.shared.u32 %0, [%1];" : "=r"(v) : "r"(a));
   return v;
 }
+__device__ __forceinline__ uint32_t lds_u16(uint32_t a) {
+  unsigned short v;
+  asm volatile("ld.shared.u16 %0, [%1];" : "=h"(v) : "r"(a));
+  return (uint32_t)v;
+}
 __device__ __forceinline__ uint2 lds_u64(uint32_t a) {
   uint2 v;
   asm volatile("ld.shared.v2.u32 {%0,%1}, [%2];" : "=r"(v.x), "=r"(v.y) : "r"(a));
@@ -184,6 +189,7 @@ __device__ __forceinline__ void nibbles_to_half2_64(uint32_t x, uint32_t (&out)[
   out[3] = lop3_and_or(x >> 8, 0x00f000f0u, MAGIC);
 }
 constexpr uint32_t HALF2_72 = 0x54805480u;  // (72, 72)
+constexpr uint32_t HALF2_68 = 0x54405440u;  // (68, 68)
 
 // Raw nibble values under the fp16 exponent of 1024 (0x6400, one unit in the
 // last place = 1): out[0], out[2] hold 1024 + n (nibbles 0 and 2 of each

@@ -54,6 +54,13 @@ extern "C" {
 /* V-code nibble orders (the cache's own storage; the reference layout is order 0) */
 #define CQ_ORDER_NATURAL 0 /* word w holds dims 8w..8w+7, LSB first (kernels.py:15-19) */
 #define CQ_ORDER_MMA 1     /* word 2g+q, nibble j holds dim g + 64q + 8j (head_dim 128) */
+/* Physical 3-bit codes (opt-in; bits <= 3, head_dim 128): a code row is 12
+ * words, two bit planes holding v = code + 4 in [0, 8), in the decode
+ * kernel's lane order: with g = d%8, k = d/8, the low two bits of dim d at
+ * word g, bit 2k, the high bit at word 8 + g/2, bit 16*(g%2) + k.  No
+ * reference counterpart: the reference stores 3-bit codes in INT4 lanes
+ * (README.md:57); cq_export_state still produces that layout. */
+#define CQ_ORDER_PLANES3 2
 
 /*
  * One compressed component (K or V) of a paged cache.  Token t of sequence b

@@ -167,6 +167,35 @@ def unpack_int4(packed: np.ndarray, head_dim: int) -> np.ndarray:
     return (e[..., :head_dim] - 8).astype(np.int8)
 
 
+def pack_planes3(codes: np.ndarray) -> np.ndarray:
+    """Physical 3-bit rows of this build's opt-in ``v_pack=3`` format (no
+    reference counterpart: the reference keeps 3-bit codes in INT4 lanes,
+    README.md:57).  ``codes`` int8 [..., 128] in [-4, 3]; v = code + 4 in
+    [0, 8).  Returns uint32 [..., 12]: with g = d % 8 and k = d // 8, the low
+    two bits of dim d at word g, bit 2k; its high bit at word 8 + g // 2,
+    bit 16 (g % 2) + k."""
+    c = np.asarray(codes).astype(np.int32)
+    assert c.shape[-1] == 128 and c.min(initial=0) >= -4 and c.max(initial=0) <= 3
+    v = (c + 4).astype(np.uint32).reshape(*c.shape[:-1], 16, 8)  # [..., k, g]
+    k = np.arange(16, dtype=np.uint32)[:, None]
+    lo = np.bitwise_or.reduce((v & 3) << (2 * k), axis=-2)  # [..., g]
+    hi_g = np.bitwise_or.reduce((v >> 2) << k, axis=-2)     # [..., g]: 16 bits each
+    hi = hi_g[..., 0::2] | (hi_g[..., 1::2] << 16)
+    return np.concatenate([lo, hi], axis=-1).astype(np.uint32)
+
+
+def unpack_planes3(rows: np.ndarray, head_dim: int = 128) -> np.ndarray:
+    """Inverse of ``pack_planes3``: int8 codes [..., 128]."""
+    assert head_dim == 128
+    r = np.asarray(rows, dtype=np.uint32)
+    k = np.arange(16, dtype=np.uint32)[:, None]
+    lo = (r[..., None, :8] >> (2 * k)) & np.uint32(3)                       # [..., k, g]
+    hi_g = np.stack([r[..., 8:] & np.uint32(0xFFFF), r[..., 8:] >> np.uint32(16)], axis=-1).reshape(
+        *r.shape[:-1], 8)
+    hi = (hi_g[..., None, :] >> k) & np.uint32(1)
+    return ((lo | (hi << 2)).astype(np.int32) - 4).reshape(*r.shape[:-1], 128).astype(np.int8)
+
+
 # ---------------------------------------------------------------------------
 # Frame schedule -- cache.py:53-61, 99-116
 # ---------------------------------------------------------------------------

@@ -27,15 +27,18 @@ def test_decode_graph_is_exported():
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("B,Hkv,Hq,T,sk,sv,steps,headroom", [
-    (2, 2, 8, 500, 32, 8, 40, 0),     # crosses I-frames of both strides and a chunk boundary
-    (1, 4, 16, 1000, 64, 32, 70, 0),  # Full-Throttle strides, crosses a page boundary
+@pytest.mark.parametrize("B,Hkv,Hq,T,sk,sv,steps,headroom,v_pack", [
+    (2, 2, 8, 500, 32, 8, 40, 0, 4),     # crosses I-frames of both strides and a chunk boundary
+    (1, 4, 16, 1000, 64, 32, 70, 0, 4),  # Full-Throttle strides, crosses a page boundary
     # a graph sized for far more tokens than are cached: the launch has more warps than the
     # current length has chunks, and only as many as there are chunks take work
-    (1, 2, 8, 300, 64, 32, 12, 20000),
-    (2, 2, 8, 100, 32, 8, 8, 3000),
+    (1, 2, 8, 300, 64, 32, 12, 20000, 4),
+    (2, 2, 8, 100, 32, 8, 8, 3000, 4),
+    # physical 3-bit V codes: the step kernel encodes into bit-plane rows
+    (2, 2, 8, 700, 64, 32, 40, 0, 3),
+    (1, 2, 8, 300, 32, 8, 20, 0, 3),
 ])
-def test_graph_step_matches_eager(B, Hkv, Hq, T, sk, sv, steps, headroom):
+def test_graph_step_matches_eager(B, Hkv, Hq, T, sk, sv, steps, headroom, v_pack):
     if not torch.cuda.is_available():
         pytest.skip("no CUDA device")
     from chronoquant_mlx_b200 import ChronoQuantCache, DecodeGraph, chronoquant_sdpa
@@ -44,6 +47,8 @@ def test_graph_step_matches_eager(B, Hkv, Hq, T, sk, sv, steps, headroom):
     K = torch.from_numpy(K).to(dev).half()
     V = torch.from_numpy(V).to(dev).half()
     kw = dict(stride_k=sk, stride_v=sv, dead_zone_v=0.0, max_tokens=T + steps + headroom + 8)
+    if v_pack == 3:
+        kw.update(delta_bits_v=3, v_pack=3)
     eager, graphed = ChronoQuantCache(**kw), ChronoQuantCache(**kw)
     for c in (eager, graphed):
         c.update_and_fetch(K[:, :, :T], V[:, :, :T])
@@ -62,6 +67,7 @@ def test_graph_step_matches_eager(B, Hkv, Hq, T, sk, sv, steps, headroom):
     assert int(g.len[0]) == T + steps and int(g.len[1]) == 0
     for a, b in zip(eager.state, graphed.state):
         assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+    assert torch.equal(eager.store.buf, graphed.store.buf)  # the physical pages too
     if headroom == 0:
         k1, v1 = K[:, :, :1], V[:, :, :1]
         with pytest.raises(ValueError):
