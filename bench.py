@@ -53,6 +53,8 @@ HERE = os.path.dirname(os.path.abspath(__file__))
 METRIC = "fused dequant-SDPA decode GB/s vs 8 TB/s HBM; decode tokens/s at 32k ctx"
 
 CONFIGS = {
+    1: dict(name="cfg1-standard-codec", B=1, Hq=32, Hkv=8, D=128, T=4096, stride_k=32, stride_v=8,
+            bits_k=4, bits_v=4, dz_k=0.0, dz_v=0.0, rho_k=0.95, rho_v=0.8),
     2: dict(name="cfg2-standard-decode", B=8, Hq=32, Hkv=8, D=128, T=16384, stride_k=32, stride_v=8,
             bits_k=4, bits_v=4, dz_k=0.0, dz_v=0.0, rho_k=0.95, rho_v=0.8),
     3: dict(name="cfg3-ftv3-decode", B=16, Hq=32, Hkv=8, D=128, T=32768, stride_k=64, stride_v=32,
@@ -91,6 +93,19 @@ def step_bytes(cfg, T):
         else:
             enc += B * H * (D * 2 + D * 2 + (D // 8) * 4 + 2)
     return attn, enc
+
+
+def codec_bytes(cfg, B=None, H=None):
+    """Algorithmic bytes of the config-1 workload (encode the whole cache, then
+    one decode query): the encode reads the fp16 K and V tokens and writes the
+    compressed cache (its active bytes, cache.py:274-287); the decode reads
+    the compressed cache and the query and writes the output."""
+    B = cfg["B"] if B is None else B
+    H = cfg["Hkv"] if H is None else H
+    hq = H * (cfg["Hq"] // cfg["Hkv"])
+    T, D = cfg["T"], cfg["D"]
+    comp = active_bytes(B, H, T, D, cfg["stride_k"], cfg["stride_v"])
+    return 2 * B * H * T * D * 2 + comp + comp + 2 * B * hq * D * 2
 
 
 def prefill_flops(cfg, rows=None, kv_heads=None):
@@ -910,17 +925,333 @@ def _prefill_unit(cfg, seed, rows):
 
 
 def _prefill_worker(a):
-    os.environ.setdefault("OMP_NUM_THREADS", "1")
-    return _prefill_unit(*a)
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(1):  # one BLAS thread per process: the processes are the parallelism
+        return _prefill_unit(*a)
 
 
 def cpu_baseline_prefill(cfg, rows=128):
     sys.path.insert(0, HERE)
-    sec, fl = _prefill_unit(cfg, 0, rows)
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(1):
+        sec, fl = _prefill_unit(cfg, 0, rows)
     return {"value": round(fl / sec / 1e12, 6), "unit": "TFLOP/s", "cores": 1, "kind": "port",
             "sample": f"1 of {cfg['Hkv']} kv-heads, the last {rows} of {cfg['chunk']} queries: oracle chunk encode "
                       f"+ fp16 reconstruct of {cfg['T'] + cfg['chunk']} tokens + fallback SDPA (numpy)",
             "seconds": round(sec, 2), "host_cpus": os.cpu_count()}
+
+
+def _count_kernels(fn):
+    """Kernels one call of ``fn`` launches on the GPU (torch profiler, outside
+    any timed region; copies and memsets are not kernels)."""
+    import torch
+    from torch.profiler import ProfilerActivity, profile
+    torch.cuda.synchronize()
+    with profile(activities=[ProfilerActivity.CUDA]) as prof:
+        fn()
+        torch.cuda.synchronize()
+    names = [e.name for e in prof.events() if e.device_type.name == "CUDA"]
+    return [n for n in names if not n.lower().startswith(("memcpy", "memset"))]
+
+
+def run_codec(args, cfg):
+    """Config 1 on the GPU: encode the whole cache (B1, Hkv8, T4096, Standard)
+    through ``update_and_fetch``, then one decode query through
+    ``chronoquant_sdpa`` (the fused path of attention.py:44-59).  Both calls
+    are captured once as a CUDA graph over a preallocated cache; a replay
+    re-encodes every token into the same pages and decodes, so each step does
+    the whole workload.  The inputs and cache (~22 MB) fit in L2, so the L2 is
+    flushed (a 256 MB write) before every timed step and each step is timed
+    alone with CUDA events.  e2e: K, V and the query copied in from pinned
+    host memory and the output copied back inside every timed step."""
+    import torch
+    import torch.distributed as dist
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    sys.path.insert(0, HERE)
+    from chronoquant_mlx_b200 import ChronoQuantCache, chronoquant_sdpa
+
+    B, H, Hq, _ = shard_of(cfg, world, rank)
+    D, T = cfg["D"], cfg["T"]
+    K, V = ar1_host(B, H, T, D, cfg["rho_k"], cfg["rho_v"], seed=0 + rank)
+    g = np.random.default_rng(rank)
+    q_host = (g.standard_normal((B, Hq, 1, D)) / math.sqrt(D)).astype(np.float16)
+    k_dev = torch.from_numpy(K).to(device)
+    v_dev = torch.from_numpy(V).to(device)
+    q_dev = torch.from_numpy(q_host).to(device)
+    scale = 1.0 / math.sqrt(D)
+    cache = ChronoQuantCache(stride_k=cfg["stride_k"], stride_v=cfg["stride_v"], delta_bits_k=cfg["bits_k"],
+                             delta_bits_v=cfg["bits_v"], dead_zone_k=cfg["dz_k"], dead_zone_v=cfg["dz_v"],
+                             max_tokens=T, page_tokens=args.page_tokens)
+    out_box = [None]
+
+    def workload():
+        cache.offset = 0  # re-encode from the first token into the same pages
+        kk, vv = cache.update_and_fetch(k_dev, v_dev)
+        out_box[0] = chronoquant_sdpa(q_dev, kk, vv, cache, scale)
+
+    workload()  # allocates the store and the attention workspace
+    kernels = _count_kernels(workload)
+    torch.cuda.synchronize()
+    side = torch.cuda.Stream(device)
+    side.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(side):
+        workload()
+    torch.cuda.current_stream().wait_stream(side)
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        workload()
+    out = out_box[0]
+    stream = torch.cuda.current_stream()
+    flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
+
+    def timed_steps(n, before=None, after=None):
+        ms = []
+        for _ in range(n):
+            flush.fill_(1)
+            if before:
+                before()
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(stream)
+            if before is not None:
+                before(True)
+            graph.replay()
+            if after is not None:
+                after()
+            e1.record(stream)
+            ms.append((e0, e1))
+        torch.cuda.synchronize()
+        return [a.elapsed_time(b) for a, b in ms]
+
+    timed_steps(args.warmup)
+    if world > 1:
+        dist.barrier()
+    with ClockSampler(local) as clk:
+        ms = timed_steps(args.steps)
+    elapsed_ms = sum(ms)
+    if world > 1:
+        tt = torch.tensor([elapsed_ms], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        elapsed_ms = float(tt.item())
+    ms_per_step = elapsed_ms / args.steps
+    byts = codec_bytes(cfg, B, H)
+    value = world * byts / (ms_per_step * 1e-3) / 1e9
+
+    # the encode kernel alone (the larger share of the bytes), L2 flushed before each launch
+    enc_graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(enc_graph):
+        cache.offset = 0
+        cache.update_and_fetch(k_dev, v_dev)
+    cache.offset = T
+    enc = []
+    for _ in range(max(20, args.steps)):
+        flush.fill_(1)
+        e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        e0.record(stream)
+        enc_graph.replay()
+        e1.record(stream)
+        enc.append((e0, e1))
+    torch.cuda.synchronize()
+    enc_ms = statistics.mean(a.elapsed_time(b) for a, b in enc)
+    comp = active_bytes(B, H, T, D, cfg["stride_k"], cfg["stride_v"])
+    enc_bytes = 2 * B * H * T * D * 2 + comp
+
+    # e2e through the public API from pinned host memory
+    hk = torch.from_numpy(K).pin_memory()
+    hv = torch.from_numpy(V).pin_memory()
+    hq = torch.from_numpy(q_host).pin_memory()
+    hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
+
+    def h2d(_inside=False):
+        if _inside:
+            k_dev.copy_(hk, non_blocking=True)
+            v_dev.copy_(hv, non_blocking=True)
+            q_dev.copy_(hq, non_blocking=True)
+
+    def d2h():
+        hout.copy_(out, non_blocking=True)
+
+    e_ms = timed_steps(args.steps, before=h2d, after=d2h)
+    e_tot = sum(e_ms)
+    if world > 1:
+        tt = torch.tensor([e_tot], device=device)
+        dist.all_reduce(tt, op=dist.ReduceOp.MAX)
+        e_tot = float(tt.item())
+    e2e_value = world * byts / (e_tot / args.steps * 1e-3) / 1e9
+
+    # parity of this run's output and state against the oracle (the test checker)
+    parity = None
+    cpu = None
+    if rank == 0:
+        from oracle import cq_oracle as O
+        o = O.OracleCache(stride_k=cfg["stride_k"], stride_v=cfg["stride_v"], delta_bits_k=cfg["bits_k"],
+                          delta_bits_v=cfg["bits_v"], dead_zone_k=cfg["dz_k"], dead_zone_v=cfg["dz_v"])
+        sites = {}
+        o.update_and_fetch(K, V, tie_sites=sites)
+        dev = []
+        for a in cache.state:
+            a = a.cpu()
+            dev.append(a.view(torch.int32).numpy().view(np.uint32) if a.dtype == torch.uint32 else a.numpy())
+        exact = all(np.array_equal(np.ascontiguousarray(a).view(np.uint8), np.ascontiguousarray(r).view(np.uint8))
+                    for a, r in zip(dev, o.state))
+        # B=1, q_len=1 dispatches to the fused kernel (attention.py:44-59): q pre-scaled in fp16
+        qs = (q_host.astype(np.float64) * float(np.float16(scale))).astype(np.float16).astype(np.float32)
+        kk, kv, pk, sk, pv, sv = o.state
+        ref = O.fused_decode(qs[0, :, 0], kk[0], pk[0], sk[0], kv[0], pv[0], sv[0], T, cfg["stride_k"],
+                             cfg["stride_v"], D)[None, :, None, :]
+        got = out.float().cpu().numpy()
+        err = np.abs(got - ref)
+        ties = {c: int(np.concatenate(sites[c], axis=2).sum()) for c in ("k", "v")}
+        parity = {"state_bit_exact_vs_oracle": bool(exact), "halfway_quotients": ties,
+                  "attention_max_abs_err_vs_oracle": float(err.max()),
+                  "attention_within_2e-3_1e-2": bool((err <= 2e-3 + 1e-2 * np.abs(ref)).all())}
+        if not args.no_cpu_baseline:
+            cpu = cpu_baseline_codec(cfg, args.cpu_budget)
+
+    peak, peak_kind = load_peak()
+    achieved = enc_bytes / (enc_ms * 1e-3) / 1e9
+    if rank == 0:
+        res = {
+            "metric": METRIC, "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": round(ms_per_step, 5), "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "int4-residual/f16-anchor, fp16 K/V/q, f32 accumulate",
+            "data": "synthetic AR(1) K/V (seeded 0), q ~ N(0,1)/sqrt(128)",
+            "config": {"workload": cfg["name"], "batch": cfg["B"] * max(world, 1), "q_heads": cfg["Hq"],
+                       "kv_heads": cfg["Hkv"], "head_dim": D, "tokens": T, "stride_k": cfg["stride_k"],
+                       "stride_v": cfg["stride_v"], "bits_k": cfg["bits_k"], "bits_v": cfg["bits_v"],
+                       "dead_zone_k": cfg["dz_k"], "dead_zone_v": cfg["dz_v"],
+                       "step": "encode all T tokens of every (sequence, kv-head) + one decode query per q head "
+                               "(one CUDA-graph replay)",
+                       "l2": "inputs + cache ~%.0f MB < 126 MB L2: 256 MB L2 flush before every timed step"
+                             % ((2 * B * H * T * D * 2 + comp) / 1e6),
+                       "parallelism": "one GPU" if world <= 1 else f"kv-head shards over {world} GPUs (weak)"},
+            "bytes_per_step_per_gpu": byts,
+            "e2e": {"value": round(e2e_value, 2), "unit": "GB/s",
+                    "h2d_bytes_per_step": hk.numel() * 2 + hv.numel() * 2 + hq.numel() * 2,
+                    "d2h_bytes_per_step": hout.numel() * hout.element_size(),
+                    "copies": "pinned host -> device before, device -> host after each step, in the timed region"},
+            "roofline": {"bound": "hbm", "kernel": "append_block_kernel (encode of all tokens)", "achieved": round(achieved, 1),
+                         "peak": peak, "unit": "GB/s", "frac": round(achieved / peak, 4), "peak_source": peak_kind,
+                         "traffic": None, "algorithmic_bytes_per_launch": enc_bytes, "launch_ms": round(enc_ms, 5),
+                         "launch_timing": "one launch at a time, L2 flushed before each"},
+            "clocks": clk.summary(),
+            "parity": parity,
+            "gpu_launches": len(kernels) * args.steps,
+            "kernels_per_step": kernels,
+            "cpu_baseline": cpu,
+        }
+        print(json.dumps(res))
+    del graph, enc_graph
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+def _codec_unit(cfg, K, V, q, scale):
+    """The config-1 workload of one (sequence, kv-head) on the reference's CPU
+    path: encode all tokens (cache.py:87-129), reconstruct the fp16 history
+    (cache.py:131-160), the fallback SDPA of its query heads (attention.py:61-74)."""
+    from oracle import cq_oracle as O
+    c = O.OracleCache(stride_k=cfg["stride_k"], stride_v=cfg["stride_v"], delta_bits_k=cfg["bits_k"],
+                      delta_bits_v=cfg["bits_v"], dead_zone_k=cfg["dz_k"], dead_zone_v=cfg["dz_v"])
+    c.update_and_fetch(K, V)
+    fk, fv = c.reconstruct_history()
+    return O.fallback_sdpa(q, "f16", fk, fv, scale, None)
+
+
+def cpu_baseline_codec(cfg, budget_s=15.0):
+    """The whole config-1 workload on the oracle, one host thread."""
+    sys.path.insert(0, HERE)
+    from threadpoolctl import threadpool_limits
+    K, V = ar1_host(cfg["B"], cfg["Hkv"], cfg["T"], cfg["D"], cfg["rho_k"], cfg["rho_v"], seed=0)
+    q = (np.random.default_rng(0).standard_normal((cfg["B"], cfg["Hq"], 1, cfg["D"])) /
+         math.sqrt(cfg["D"])).astype(np.float16)
+    scale = 1.0 / math.sqrt(cfg["D"])
+    n, t_tot = 0, 0.0
+    with threadpool_limits(1):
+        _codec_unit(cfg, K, V, q, scale)
+        while t_tot < budget_s and n < 30:
+            t0 = time.perf_counter()
+            _codec_unit(cfg, K, V, q, scale)
+            t_tot += time.perf_counter() - t0
+            n += 1
+    return {"value": round(n * codec_bytes(cfg) / t_tot / 1e9, 5), "unit": "GB/s", "cores": 1, "kind": "port",
+            "sample": f"the whole workload {n} times: oracle encode of {cfg['T']} tokens x {cfg['Hkv']} kv-heads + "
+                      "fp16 reconstruct + fallback SDPA (numpy, 1 thread)",
+            "ms_per_step": round(1e3 * t_tot / n, 2), "host_cpus": os.cpu_count()}
+
+
+_CODEC_DATA = {}
+
+
+def _codec_init(cfg):
+    """Pool initializer: every worker generates the workload's inputs once."""
+    sys.path.insert(0, HERE)
+    K, V = ar1_host(cfg["B"], cfg["Hkv"], cfg["T"], cfg["D"], cfg["rho_k"], cfg["rho_v"], seed=0)
+    rep = cfg["Hq"] // cfg["Hkv"]
+    q = (np.random.default_rng(0).standard_normal((cfg["B"], cfg["Hq"], 1, cfg["D"])) /
+         math.sqrt(cfg["D"])).astype(np.float16)
+    for h in range(cfg["Hkv"]):
+        _CODEC_DATA[h] = (np.ascontiguousarray(K[:, h:h + 1]), np.ascontiguousarray(V[:, h:h + 1]),
+                          np.ascontiguousarray(q[:, h * rep:(h + 1) * rep]))
+
+
+def _codec_worker(a):
+    cfg, h = a
+    K, V, q = _CODEC_DATA[h]
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(1):  # one BLAS thread per process: the processes are the parallelism
+        t0 = time.perf_counter()
+        _codec_unit(cfg, K, V, q, 1.0 / math.sqrt(cfg["D"]))
+        return time.perf_counter() - t0
+
+
+def run_reference_codec(args, cfg):
+    """Config 1 on the reference's CPU path (oracle restatement) with the host
+    cores: one process per kv-head; a step is the whole workload (every
+    kv-head's encode, reconstruct and SDPA) and is timed by the wall clock."""
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    if rank != 0:
+        return
+    import multiprocessing as mp
+    workers = max(1, min(os.cpu_count() or 1, cfg["Hkv"]))
+    tasks = [(cfg, h) for h in range(cfg["Hkv"])]
+    ctx = mp.get_context("spawn")
+    with ctx.Pool(workers, initializer=_codec_init, initargs=(cfg,)) as pool:
+        for _ in range(args.warmup):
+            pool.map(_codec_worker, tasks, chunksize=1)
+        ms = []
+        for _ in range(args.steps):
+            t0 = time.perf_counter()
+            pool.map(_codec_worker, tasks, chunksize=1)
+            ms.append(1e3 * (time.perf_counter() - t0))
+    mean = sum(ms) / len(ms)
+    value = codec_bytes(cfg) / (mean * 1e-3) / 1e9
+    out = {
+        "impl": "reference", "metric": METRIC, "value": round(value, 5), "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup, "ms_per_step": round(mean, 3), "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "int4-residual/f16-anchor, fp16 fallback SDPA",
+        "data": "synthetic AR(1) K/V (seeded 0)",
+        "config": {"workload": cfg["name"], "batch": cfg["B"], "q_heads": cfg["Hq"], "kv_heads": cfg["Hkv"],
+                   "head_dim": cfg["D"], "tokens": cfg["T"], "stride_k": cfg["stride_k"],
+                   "stride_v": cfg["stride_v"], "bits_k": cfg["bits_k"], "bits_v": cfg["bits_v"],
+                   "dead_zone_k": cfg["dz_k"], "dead_zone_v": cfg["dz_v"],
+                   "parallelism": f"{workers} host processes, one kv-head each"},
+        "cpu_baseline": {"value": round(value, 5), "unit": "GB/s", "cores": workers, "kind": "port",
+                         "sample": "the whole workload each step (oracle restatement of the reference's encode + "
+                                   "fp16 reconstruct + fallback SDPA; MLX/Metal is unavailable here)"},
+        "e2e": {"value": round(value, 5), "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+    print(json.dumps(out))
 
 
 def run_reference_prefill(args, cfg):
@@ -1020,7 +1351,12 @@ def _ref_unit_step(c, K, V, q, scale):
 
 def _ref_worker(args):
     cfg, seed, n_steps = args
-    os.environ.setdefault("OMP_NUM_THREADS", "1")
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(1):  # one BLAS thread per process: the processes are the parallelism
+        return _ref_worker_steps(cfg, seed, n_steps)
+
+
+def _ref_worker_steps(cfg, seed, n_steps):
     c, K, V = _ref_unit_setup(cfg, seed)
     rep = cfg["Hq"] // cfg["Hkv"]
     q = (np.random.default_rng(seed).standard_normal((1, rep, 1, cfg["D"])) / math.sqrt(cfg["D"])).astype(np.float16)
@@ -1035,6 +1371,12 @@ def _ref_worker(args):
 def cpu_baseline(cfg, budget_s=20.0):
     """The oracle's reference-structured decode step on one (sequence,
     kv-head) unit, single thread, GB/s of that unit's compressed bytes."""
+    from threadpoolctl import threadpool_limits
+    with threadpool_limits(1):
+        return _cpu_baseline_1t(cfg, budget_s)
+
+
+def _cpu_baseline_1t(cfg, budget_s):
     sys.path.insert(0, HERE)
     c, K, V = _ref_unit_setup(cfg, 0)
     rep = cfg["Hq"] // cfg["Hkv"]
@@ -1152,6 +1494,12 @@ def main():
                               "CPU path (numpy oracle) cannot run it in a bounded sample"}))
         else:
             run_decoder(args, cfg)
+        return
+    if args.config == 1:
+        if args.impl == "reference":
+            run_reference_codec(args, cfg)
+        else:
+            run_codec(args, cfg)
         return
     if args.config == 4:
         if args.impl == "reference":

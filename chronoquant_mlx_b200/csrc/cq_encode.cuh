@@ -20,11 +20,43 @@ __device__ __forceinline__ int quantise_code(float q, float hl, bool zero_scale)
   return (int)r;
 }
 
+// The stored value (code + 8, kernels.py:40) of one residual: the quotient
+// delta / scale rounded to the token dtype, then half to even and clipped
+// (codec.py:48-54).
+template <int DTYPE>
+__device__ __forceinline__ uint32_t code_nibble(float dv, float scale_safe, float hl, bool zero_scale) {
+  const float q = round_dt(__fdiv_rn(dv, scale_safe), DTYPE);
+  const int code = quantise_code(q, hl, zero_scale);
+  return (uint32_t)min(max(code + 8, 0), 15);
+}
+
+// code_nibble without a division per value, for many values sharing one
+// scale: r is the correctly rounded 1/scale (finite; callers scale dv and
+// scale by a power of two where it is not).  rint(round_dt(q))
+// differs from rint(q) only when q rounds onto a half-integer m = k + 1/2;
+// those are representable with an even significand (|m| < 64), so that
+// happens exactly for q in [m - h, m + h], h half a dtype ulp at m.  q' = dv*r
+// is within 2^-19 of q (|q| < 16), far less than h, so m = floor(q') + 1/2 is
+// the only candidate, an FMA residual dv - (m -+ h) * scale (exact product,
+// exact sign) settles membership, and outside the interval rint(q') = rint(q).
+template <int DTYPE>
+__device__ __forceinline__ uint32_t code_nibble_rcp(float dv, float scale_safe, float r, float hl,
+                                                    bool zero_scale) {
+  const float q = dv * r;
+  const float m = floorf(q) + 0.5f;
+  constexpr int fb = (DTYPE == CQ_BF16) ? 8 : 11;  // h = 2^(e - fb) for |m| in [2^e, 2^(e+1))
+  const float h = __int_as_float((__float_as_int(m) & 0x7f800000) - (fb << 23));
+  const bool on_half = fmaf(-(m - h), scale_safe, dv) >= 0.f && fmaf(-(m + h), scale_safe, dv) <= 0.f;
+  const int code = quantise_code(on_half ? m : q, hl, zero_scale);  // rint(m): the even neighbour
+  return (uint32_t)min(max(code + 8, 0), 15);
+}
+
 // Codes and scale of one P-frame token, computed by one warp.  xv: the
 // token's values (exact in DTYPE), av: its anchor's fp16 values, for dims
 // lane + 32 i.  Packs the nibbles (+8 bias, kernels.py:40) of the code row in
-// `order` into sw[0 .. row_words(D, order)) (warp-private shared memory) and returns
-// the scale in DTYPE precision (stored as fp16 by the caller, cache.py:116).
+// `order` into sw[0 .. row_words(D, order)) (warp-private shared memory) and
+// returns the scale in DTYPE precision (stored as fp16 by the caller,
+// cache.py:116).
 template <int DTYPE>
 __device__ __forceinline__ float encode_residual(const float (&xv)[kMaxDimsPerLane],
                                                  const float (&av)[kMaxDimsPerLane], int D, int bits,
@@ -66,12 +98,7 @@ __device__ __forceinline__ float encode_residual(const float (&xv)[kMaxDimsPerLa
 #pragma unroll
   for (int i = 0; i < kMaxDimsPerLane; ++i) {
     int d = lane + 32 * i;
-    if (d < D) {
-      float q = round_dt(__fdiv_rn(dv[i], scale_safe), DTYPE);
-      int code = quantise_code(q, hl, zero_scale);
-      uint32_t nib = (uint32_t)min(max(code + 8, 0), 15);  // kernels.py:40
-      pack_code(sw, d, D, order, nib);
-    }
+    if (d < D) pack_code(sw, d, D, order, code_nibble<DTYPE>(dv[i], scale_safe, hl, zero_scale));
   }
   __syncwarp();
   return scale;

@@ -313,6 +313,41 @@ def test_bf16_tokens_vs_oracle():
     compare_states(g, o)
 
 
+@pytest.mark.parametrize("dtype", ["f16", "bf16"])
+@pytest.mark.parametrize("cfg", [
+    dict(stride_k=32, stride_v=8, dead_zone_v=0.0),
+    dict(stride_k=64, stride_v=32, delta_bits_v=3, dead_zone_v=0.05),
+    dict(stride_k=16, stride_v=4, delta_bits_k=2, delta_bits_v=2, dead_zone_k=0.2),
+])
+def test_bulk_append_matches_token_appends(dtype, cfg):
+    """A multi-token append (head_dim 128: the 8-token-block kernel, codes from
+    a reciprocal with an exact FMA check near rounding boundaries) against the
+    same tokens appended one call each (the one-token kernel, a division per
+    value) and against the oracle, bit for bit.  Token magnitudes span the
+    dtype's range (fp16: subnormal to 1e3 scales; bf16: down to 1e-38, where
+    1/scale overflows and the division is taken)."""
+    rng = np.random.default_rng(17 if dtype == "f16" else 18)
+    B, H, T, D = 1, 2, 320, 128
+    K, V = O.ar1_kv(B, H, T, D, seed=3)
+    lo, hi = (-7.0, 3.0) if dtype == "f16" else (-38.0, 3.0)
+    mag = 10.0 ** rng.uniform(lo, hi, size=(B, H, T, 1))
+    K = K.astype(np.float64) * mag
+    V = V.astype(np.float64) * mag[:, :, ::-1]
+    tdt = torch.float16 if dtype == "f16" else torch.bfloat16
+    if dtype == "f16":
+        K, V = K.astype(np.float16), V.astype(np.float16)
+    else:
+        K, V = O.round_bf16(K.astype(np.float32)), O.round_bf16(V.astype(np.float32))
+    bulk = build_cache(K, V, [5, 200, 115], dtype=tdt, **cfg)
+    single = build_cache(K, V, [1] * T, dtype=tdt, **cfg)
+    for a, b in zip(bulk.state, single.state):
+        assert torch.equal(a.view(torch.uint8), b.view(torch.uint8))
+    o = O.OracleCache(dtype=dtype, **cfg)
+    for t0, n in ((0, 5), (5, 200), (205, 115)):
+        o.update_and_fetch(K[:, :, t0:t0 + n], V[:, :, t0:t0 + n])
+    compare_states(bulk, o)
+
+
 @pytest.mark.parametrize("B,Hkv,Hq,T,cfg", [
     (1, 8, 32, 4096, dict(stride_k=32, stride_v=8, dead_zone_v=0.0)),
     (3, 2, 16, 1000, dict(stride_k=64, stride_v=32, delta_bits_v=3)),
