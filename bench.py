@@ -783,12 +783,24 @@ def run_decoder(args, cfg):
     dc = DecoderConfig()
     n_steps = args.warmup + args.steps + 4
     t_setup = time.perf_counter()
-    tp = world > 1 and args.tp
-    split = world > 1 and args.seqsplit and not tp
+    n_tp = n_seq = 1
+    if world > 1 and args.tp and args.seqsplit:
+        n_tp = args.tp_size or 2
+        if world % n_tp:
+            raise SystemExit(f"--tp-size {n_tp} must divide the {world} ranks")
+        n_seq = world // n_tp
+    elif world > 1 and args.tp:
+        n_tp = world
+    elif world > 1 and args.seqsplit:
+        n_seq = world
+    tp, split = n_tp > 1, n_seq > 1
     one_model = tp or split  # every rank runs the same sequences (else: independent replicas)
+    tp_group = seq_group = None
+    if one_model:
+        from chronoquant_mlx_b200.decoder import mesh_groups
+        tp_group, seq_group = mesh_groups(n_seq, n_tp)
     dec = Qwen3StyleDecoder(dc, B, T0 + n_steps + 4, kw, device=device, seed=100 if one_model else 100 + rank,
-                            tp_group=dist.group.WORLD if tp else None,
-                            seq_group=dist.group.WORLD if split else None)
+                            tp_group=tp_group, seq_group=seq_group)
     dec.fill_context(T0, seed=200 if one_model else 200 + rank)
     dec.ids.copy_(torch.arange(B, device=device) * 7 + 1)
     dec.capture()
@@ -837,6 +849,42 @@ def run_decoder(args, cfg):
     cache_bytes = sum(L["cache"].nbytes for L in dec.layers)
     del ag
 
+    # the collectives of a step alone, each set captured as a graph and replayed: the per-layer
+    # partial exchange + merge of the sequence split, the two all-reduces per layer of the
+    # tensor-parallel split (every rank runs the same captures in the same order)
+    comm = {}
+    if split:
+        cg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(cg):
+            for _ in dec.layers:
+                dec._merge_partials()
+        cg.replay()
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(reps):
+            cg.replay()
+        c1.record(stream)
+        torch.cuda.synchronize()
+        comm["seq_allgather_merge_ms_per_step"] = round(c0.elapsed_time(c1) / reps, 4)
+        del cg
+    if tp:
+        xr = torch.zeros((B, dc.hidden), device=device, dtype=torch.bfloat16)
+        cg = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(cg):
+            for _ in range(2 * dc.layers):
+                dec._reduce(xr)
+        cg.replay()
+        torch.cuda.synchronize()
+        c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        c0.record(stream)
+        for _ in range(reps):
+            cg.replay()
+        c1.record(stream)
+        torch.cuda.synchronize()
+        comm["tp_allreduce_ms_per_step"] = round(c0.elapsed_time(c1) / reps, 4)
+        del cg
+
     # e2e: a host-driven serving loop -- every step's input ids copied in from pinned host
     # memory, the sampled ids copied back and waited for, so the host holds each token before
     # it feeds the next step
@@ -873,13 +921,18 @@ def run_decoder(args, cfg):
                        "ffn": dc.ffn, "vocab": dc.vocab, "caches": "FT-V3 (64/32, 4/3 bits, dz 0/0.05)",
                        "step": "one CUDA-graph replay: 36 x (RMSNorm, QKV, q/k norm, RoPE, fused append+decode "
                                "attention, o_proj, SwiGLU) + lm_head + argmax",
-                       "parallelism": (f"tp{world} (kv-head tensor parallel, NCCL all-reduce after o_proj and "
+                       "parallelism": (f"seq{n_seq} x tp{n_tp} ({n_seq} token ranges of the context, each over "
+                                       f"{n_tp} kv-head tensor-parallel ranks: NCCL all-reduce after o_proj and the "
+                                       "down projection within a range, all-gather of partial attention + "
+                                       "log-sum-exp merge per layer across ranges)") if tp and split else
+                                      (f"tp{world} (kv-head tensor parallel, NCCL all-reduce after o_proj and "
                                        "the down projection)") if tp else
                                       (f"seq{world} (token ranges of one sequence per rank, NCCL all-gather of "
                                        "partial attention + log-sum-exp merge per layer)") if split else
                                       f"dp{world} (independent replicas)",
                        "setup_seconds": round(setup_s, 1)},
             "attention_ms_per_step": round(attn_ms, 4),
+            "collectives": comm or None,
             "compressed_cache_bytes": cache_bytes,
             "e2e": {"value": round((1 if one_model else world) * B / (e_ms * 1e-3), 1), "unit": "tokens/s",
                     "h2d_bytes_per_step": hin.numel() * hin.element_size(),
@@ -1466,6 +1519,9 @@ def main():
     ap.add_argument("--page-tokens", type=int, default=None, help="cache page size (default: the cache's choice)")
     ap.add_argument("--cpu-rows", type=int, default=128, help="config 4 CPU sample: query rows per kv-head")
     ap.add_argument("--tp", action="store_true", help="config 5 under torchrun: kv-head tensor parallel")
+    ap.add_argument("--tp-size", type=int, default=None,
+                    help="config 5 with --tp and --seqsplit: tensor-parallel ranks per token range (the mesh is "
+                         "(N / tp-size) token ranges x tp-size; default 2)")
     ap.add_argument("--seqsplit", action="store_true",
                     help="config 5: one sequence (batch 1, 524288-token context unless --context), split by "
                          "token ranges over the torchrun ranks")
@@ -1481,8 +1537,6 @@ def main():
     cfg = CONFIGS[args.config]
     if args.config == 4 and args.context is not None:
         cfg = dict(cfg, T=args.context, name=f"{cfg['name']}-ctx{args.context}")
-    if args.tp and args.seqsplit:
-        ap.error("--tp and --seqsplit are separate config-5 modes; pick one")
     if args.config == 5 and args.seqsplit:
         T = args.context or 524288
         cfg = dict(cfg, B=1, T=T, name=f"cfg5-qwen3-8b-shape-ftv3-seqsplit-{T}")

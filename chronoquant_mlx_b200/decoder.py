@@ -21,11 +21,13 @@ length lives on the device and advances inside the kernel, the RoPE position
 is a device counter, and the sampled ids are written back in-graph, so a
 replay needs no host synchronisation.
 
-Two multi-GPU modes, each inside the captured step: kv-head tensor
-parallelism (``tp_group``: NCCL all-reduce after o_proj and the down
-projection) and a sequence split of one long context (``seq_group``: each
-rank's range of every layer's cache, partial attention with log-sum-exp,
-one NCCL all-gather per layer, cq_lse_merge_packed).
+Two multi-GPU modes, each inside the captured step, alone or combined on a
+mesh of seq x tp ranks (``mesh_groups``): kv-head tensor parallelism
+(``tp_group``: NCCL all-reduce after o_proj and the down projection) and a
+sequence split of one long context (``seq_group``: each rank's range of
+every layer's cache, partial attention with log-sum-exp, one NCCL all-gather
+per layer, cq_lse_merge_packed).  Combined, a rank keeps its tensor-parallel
+share of the weights and, for its kv-heads, its token range of the context.
 
 ``fill_context`` writes a synthetic context (seeded random K/V per layer,
 encoded by the cache's own append kernel) instead of running a 32k-token
@@ -59,6 +61,29 @@ class DecoderConfig:
     eps: float = 1.0e-6
 
 
+def mesh_groups(seq: int, tp: int):
+    """Process groups of a seq x tp mesh over the default group's ranks
+    r = s * tp + p (seq index s, tensor-parallel index p): the tensor-parallel
+    group of this rank (ranks with its s) and its sequence group (ranks with
+    its p).  Every rank creates every group, in the same order, as
+    torch.distributed requires.  Returns (tp_group, seq_group); a size-1
+    dimension gives None."""
+    import torch.distributed as dist
+    world, rank = dist.get_world_size(), dist.get_rank()
+    if seq < 1 or tp < 1 or seq * tp != world:
+        raise ValueError(f"mesh {seq} x {tp} does not cover the {world} ranks")
+    tp_group = seq_group = None
+    for s in range(seq):
+        g = dist.new_group([s * tp + p for p in range(tp)])
+        if rank // tp == s:
+            tp_group = g
+    for p in range(tp):
+        g = dist.new_group([s * tp + p for s in range(seq)])
+        if rank % tp == p:
+            seq_group = g
+    return (tp_group if tp > 1 else None), (seq_group if seq > 1 else None)
+
+
 def _rmsnorm(x: torch.Tensor, w: torch.Tensor, eps: float) -> torch.Tensor:
     """RMSNorm as the torch expression that cq_rmsnorm reproduces (the tests'
     reference for the fused kernel)."""
@@ -90,11 +115,14 @@ class Qwen3StyleDecoder:
         whole model and, per layer, the compressed cache of its range; the
         last rank owns the tail and encodes the new tokens.  Each layer's
         attention is a partial (output, log-sum-exp) per rank, all-gathered
-        (NCCL) and merged by cq_lse_merge_packed, all inside the captured step."""
+        (NCCL) and merged by cq_lse_merge_packed, all inside the captured step.
+
+        Both together (``mesh_groups``): the layers are tensor-parallel over
+        ``tp_group`` and each rank's kv-heads hold its token range of the
+        context; the tail ranks (the last of every sequence group) encode the
+        new tokens."""
         self.cfg, self.B, self.max_len = cfg, batch, max_len
         self.device, self.dtype = torch.device(device), dtype
-        if tp_group is not None and seq_group is not None:
-            raise ValueError("tensor parallel and sequence split are separate modes")
         self.group, self.seq_group = tp_group, seq_group
         self.seq_rank, self.seq_world = 0, 1
         if seq_group is not None:

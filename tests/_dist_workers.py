@@ -187,6 +187,74 @@ def seq_decoder_worker(rank, world, port, steps, queue):
         queue.put((rank, None, None, repr(e)))
 
 
+def mesh_decoder_worker(rank, world, port, n_seq, steps, queue):
+    """The decoder on a seq x tp mesh of `world` GPUs (``mesh_groups``: n_seq
+    token ranges, each over world / n_seq tensor-parallel ranks) against the
+    same decoder on one GPU (rank 0): same weights, context and input ids
+    every step."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        from chronoquant_mlx_b200.decoder import DecoderConfig, Qwen3StyleDecoder, mesh_groups
+        tp_group, seq_group = mesh_groups(n_seq, world // n_seq)
+        cfg = DecoderConfig(layers=2, hidden=512, heads=8, kv_heads=2, head_dim=128, ffn=1024, vocab=1000)
+        kw = dict(stride_k=64, stride_v=32, delta_bits_v=3, dead_zone_v=0.05)
+        m = Qwen3StyleDecoder(cfg, 1, 1100, kw, device=dev, seed=9, tp_group=tp_group, seq_group=seq_group)
+        m.fill_context(1000)
+        m.capture()
+        one = None
+        if rank == 0:
+            one = Qwen3StyleDecoder(cfg, 1, 1100, kw, device=dev, seed=9)
+            one.fill_context(1000)
+            one.capture()
+        rels = []
+        for s in range(steps):
+            ids = torch.tensor([3 + 7 * s], device=dev)
+            m.ids.copy_(ids)
+            lm = m.decode(1).float().clone()
+            if one is not None:
+                one.ids.copy_(ids)
+                lo = one.decode(1).float()
+                rels.append(float((lm - lo).norm() / lo.norm()))
+        torch.cuda.synchronize()
+        lens = [int(L["len"][0]) for L in m.layers]
+        del m.graph  # graphs holding NCCL work go before the process group
+        if one is not None:
+            del one.graph
+        dist.barrier()
+        dist.destroy_process_group()
+        queue.put((rank, rels, lens, None))
+    except Exception as e:
+        queue.put((rank, None, None, repr(e)))
+
+
+def mesh_groups_worker(rank, world, port, n_seq, queue):
+    """The ranks of this rank's tensor-parallel and sequence groups on a
+    n_seq x (world / n_seq) mesh (gloo, CPU)."""
+    try:
+        _init(rank, world, port, 60)
+        from chronoquant_mlx_b200.decoder import mesh_groups
+        tp_group, seq_group = mesh_groups(n_seq, world // n_seq)
+        tp_ranks = dist.get_process_group_ranks(tp_group) if tp_group is not None else None
+        seq_ranks = dist.get_process_group_ranks(seq_group) if seq_group is not None else None
+        if seq_group is not None:  # the group carries a collective among exactly those ranks
+            t = torch.tensor([rank], dtype=torch.int64)
+            dist.all_reduce(t, group=seq_group)
+            seq_sum = int(t.item())
+        else:
+            seq_sum = None
+        dist.barrier()
+        dist.destroy_process_group()
+        queue.put((rank, tp_ranks, seq_ranks, seq_sum, None))
+    except Exception as e:
+        queue.put((rank, None, None, None, repr(e)))
+
+
 class _ShardStub:
     """The part of a cache the tail check reads: its token count."""
 

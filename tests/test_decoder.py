@@ -189,6 +189,37 @@ def test_sequence_split_matches_one_gpu():
     assert res[0][2] == [512, 512] and res[1][2] == [491, 491], (res[0][2], res[1][2])
 
 
+def test_sequence_split_times_tensor_parallel_matches_one_gpu():
+    """Four GPUs as a 2 x 2 mesh: two token ranges of one 1000-token context,
+    each over two kv-head tensor-parallel ranks (per layer an all-reduce pair
+    within a range and a partial all-gather + log-sum-exp merge across the
+    ranges, all in the captured step): logits within 2e-2 relative of the
+    one-GPU decoder with the same weights, context and ids; only the tail
+    ranks' caches grow."""
+    if not torch.cuda.is_available() or torch.cuda.device_count() < 4:
+        pytest.skip("needs four GPUs")
+    import multiprocessing as mp
+    import socket
+    import _dist_workers as W
+    sk = socket.socket()
+    sk.bind(("127.0.0.1", 0))
+    port = sk.getsockname()[1]
+    sk.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=W.mesh_decoder_worker, args=(r, 4, port, 2, 3, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=300) for _ in range(4)], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=60)
+    for rank, rels, lens, err in res:
+        assert err is None, err
+    assert len(res[0][1]) == 3 and all(r < 2e-2 for r in res[0][1]), res[0][1]
+    # ranks 0, 1: tokens 0-511 (fixed); ranks 2, 3: the tail 512-999 plus three new tokens
+    assert [r[2] for r in res] == [[512, 512], [512, 512], [491, 491], [491, 491]], [r[2] for r in res]
+
+
 def test_sequence_split_on_one_gpu_matches_unsplit():
     """The sequence-split decoder's logic on one GPU: two decoders hold the
     two token ranges of one 1000-token context (rank 0: tokens 0-511; the

@@ -181,3 +181,33 @@ def test_nccl_sequence_split_two_gpus(q_len):
         e = np.abs(out - ref)
         assert (e <= 2e-3 + 1e-2 * np.abs(ref)).all(), (rank, e.max())
     assert codes == [0, 0]
+
+
+@pytest.mark.parametrize("n_seq", [1, 2, 4])
+def test_mesh_groups(n_seq):
+    """mesh_groups on 4 gloo ranks: rank r = s * tp + p sits in the
+    tensor-parallel group of its s and the sequence group of its p, and a
+    collective over the sequence group sums exactly those ranks."""
+    import multiprocessing as mp
+    import socket
+    import _dist_workers as W
+    sk = socket.socket()
+    sk.bind(("127.0.0.1", 0))
+    port = sk.getsockname()[1]
+    sk.close()
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    procs = [ctx.Process(target=W.mesh_groups_worker, args=(r, 4, port, n_seq, q)) for r in range(4)]
+    for p in procs:
+        p.start()
+    res = sorted([q.get(timeout=120) for _ in range(4)], key=lambda x: x[0])
+    for p in procs:
+        p.join(timeout=60)
+    tp = 4 // n_seq
+    for rank, tp_ranks, seq_ranks, seq_sum, err in res:
+        assert err is None, err
+        s, p = divmod(rank, tp)
+        assert tp_ranks == (None if tp == 1 else [s * tp + i for i in range(tp)])
+        want_seq = [i * tp + p for i in range(n_seq)]
+        assert seq_ranks == (None if n_seq == 1 else want_seq)
+        assert seq_sum == (None if n_seq == 1 else sum(want_seq))
