@@ -10,7 +10,7 @@ is checked as well).  The calls must not allocate: device free memory and
 the caching allocator's counters stay unchanged across them.  Before the
 calls, the shared scratch is filled with the partials of a different shape,
 so stale contents (the decode kernel's completion words included) are
-exercised."""
+exercised.  Finally one call is captured in a CUDA graph and replayed twice."""
 
 import ctypes
 import math
@@ -100,6 +100,24 @@ def test_static_scratch_matches_workspace_path(B, Hkv, Hq, T, q_len, stride_k, s
         _close(o, ro)
         _close(lse, rlse)
         assert torch.equal(o, ro) and torch.equal(lse, rlse)
+
+    # after the first call the entry point is capture-safe: one call captured in a CUDA graph
+    # (the completion-word clear and the kernels), replayed twice, gives the same bits
+    go = torch.zeros_like(outs[0][0])
+    gl = torch.zeros_like(outs[0][1])
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        _attention("cq_attention_static_scratch", desc, T, qs[0], causal, go, gl)
+    torch.cuda.synchronize()
+    free1 = torch.cuda.mem_get_info()[0]
+    for _ in range(2):
+        go.zero_()
+        gl.zero_()
+        graph.replay()
+        torch.cuda.synchronize()
+        assert torch.equal(go, ref[0][0]) and torch.equal(gl, ref[0][1])
+    assert torch.cuda.mem_get_info()[0] == free1
+    del graph
 
 
 def test_static_scratch_rejects_oversized_shape():
