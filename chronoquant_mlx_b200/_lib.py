@@ -24,7 +24,7 @@ CQ_ERR_WORKSPACE = -4
 
 CQ_ABI_VERSION = 3  # CQ_ABI_VERSION of include/chronoquant_b200.h
 CQ_F16, CQ_BF16, CQ_F32 = 0, 1, 2
-CQ_ORDER_NATURAL, CQ_ORDER_MMA, CQ_ORDER_PLANES3 = 0, 1, 2
+CQ_ORDER_NATURAL, CQ_ORDER_MMA, CQ_ORDER_PLANES3, CQ_ORDER_PLANES2 = 0, 1, 2, 3
 CQ_SCALE_BY_PFRAME, CQ_SCALE_BY_TOKEN = 0, 1
 CQ_STATIC_SCRATCH_BYTES = 8 << 20  # cq_attention_static_scratch's fixed per-device scratch
 

@@ -17,7 +17,8 @@ I-frame).  V code rows use the decode kernel's nibble order when head_dim is
 codes of 3 bits or fewer) stores V code rows physically in 3 bits per value
 (two bit planes, 48 bytes per row at head_dim 128 instead of 64; the decode
 kernel reads them for the (64, 32) and (32, 8) stride pairs, the general
-kernel otherwise), ``state`` still exports INT4 lanes, and ``nbytes`` keeps
+kernel otherwise); ``v_pack=2`` (V codes of 2 bits) likewise in one plane of
+32 bytes per row.  ``state`` still exports INT4 lanes, and ``nbytes`` keeps
 the reference accounting while ``physical_nbytes`` reports what the store
 holds.  Appending never copies
 history except when the page pool grows (geometrically, or never with
@@ -68,7 +69,8 @@ def _num_keyframes(num_tokens: int, stride: int) -> int:
 class _Component:
     def __init__(self, stride: int, bits: int, dead_zone: float, page_tokens: int, head_dim: int, order: int):
         self.stride = stride
-        self.row_words = 12 if order == _lib.CQ_ORDER_PLANES3 else (head_dim + 7) // 8  # PLANES3: head_dim 128
+        # bit-plane rows (head_dim 128): 12 words for 3-bit codes, 8 for 2-bit codes
+        self.row_words = {_lib.CQ_ORDER_PLANES3: 12, _lib.CQ_ORDER_PLANES2: 8}.get(order, (head_dim + 7) // 8)
         self.bits = bits
         self.dead_zone = float(dead_zone)
         self.apg = page_tokens // stride
@@ -185,8 +187,9 @@ class ChronoQuantCache:
     Arguments follow cache.py:21-31.  Keyword-only extras: ``page_tokens``
     (page size; default the multiple of lcm(stride_k, stride_v, 16) nearest
     256 from below), ``max_tokens`` (pre-size the page pool) and ``v_pack``
-    (4: V codes in INT4 lanes as the reference stores them; 3: physically 3
-    bits per value, for V codes of 3 bits or fewer)."""
+    (4: V codes in INT4 lanes as the reference stores them; 3 or 2:
+    physically 3 or 2 bits per value, for V codes of at most that many
+    bits)."""
 
     def __init__(self, stride_k: int = 32, stride_v: int = 8, delta_bits_k: int = 4, delta_bits_v: int = 4,
                  dead_zone_k: float = 0.0, dead_zone_v: float = 0.05, use_fused: bool = True,
@@ -212,11 +215,14 @@ class ChronoQuantCache:
             raise ValueError("page_tokens must be a multiple of stride_k and stride_v")
         self.page_tokens = int(page_tokens)
         self.max_tokens = max_tokens
-        if int(v_pack) not in (3, 4):
-            raise ValueError("v_pack must be 4 (INT4 lanes) or 3 (physical 3-bit codes)")
+        if int(v_pack) not in (2, 3, 4):
+            raise ValueError("v_pack must be 4 (INT4 lanes), 3 or 2 (physical 3-bit or 2-bit codes)")
         self.v_pack = int(v_pack)
-        if self.v_pack == 3 and self._get_codec_for_v().delta_bits > 3:
-            raise ValueError(f"v_pack=3 needs V codes of at most 3 bits, got {self._get_codec_for_v().delta_bits}")
+        if self.v_pack < 4:  # (the V codec itself is made lazily: a factory may set layer_idx later)
+            v_bits = (self.per_layer_v_bits[min(self.layer_idx, len(self.per_layer_v_bits) - 1)]
+                      if self.per_layer_v_bits else self.delta_bits_v)
+            if v_bits > self.v_pack:
+                raise ValueError(f"v_pack={self.v_pack} needs V codes of at most {self.v_pack} bits, got {v_bits}")
         self._store: PagedStore | None = None
         self._workspace = None
 
@@ -243,11 +249,11 @@ class ChronoQuantCache:
             raise NotImplementedError(f"head_dim {D} unsupported (multiple of 8, <= 256)")
         cv = self._get_codec_for_v()
         v_order = _lib.CQ_ORDER_MMA if D == 128 else _lib.CQ_ORDER_NATURAL
-        if self.v_pack == 3:
-            if cv.delta_bits > 3 or D != 128:
-                raise ValueError(f"v_pack=3 needs V codes of at most 3 bits (got {cv.delta_bits}) and head_dim 128 "
-                                 f"(got {D})")
-            v_order = _lib.CQ_ORDER_PLANES3
+        if self.v_pack < 4:
+            if cv.delta_bits > self.v_pack or D != 128:
+                raise ValueError(f"v_pack={self.v_pack} needs V codes of at most {self.v_pack} bits (got "
+                                 f"{cv.delta_bits}) and head_dim 128 (got {D})")
+            v_order = _lib.CQ_ORDER_PLANES3 if self.v_pack == 3 else _lib.CQ_ORDER_PLANES2
         comps = [_Component(self.stride_k, self.delta_bits_k, self.dead_zone_k, self.page_tokens, D,
                             _lib.CQ_ORDER_NATURAL),
                  _Component(self.stride_v, cv.delta_bits, self.dead_zone_v, self.page_tokens, D, v_order)]
@@ -529,8 +535,8 @@ class ChronoQuantCache:
     @property
     def physical_nbytes(self) -> int:
         """The same active slices at the bytes the store holds them in: equal to
-        ``nbytes`` except with ``v_pack=3``, whose V code rows take 3 bits per
-        value."""
+        ``nbytes`` except with ``v_pack`` 3 or 2, whose V code rows take 3 or 2
+        bits per value."""
         if self._store is None or self.offset == 0:
             return 0
         st = self._store

@@ -33,9 +33,10 @@ static int validate_component(const cq_paged_cache *c, const cq_component &k, co
              CQ_ERR_INVALID, n + ": scale_row too small");
   CQ_REQUIRE(k.bits >= 2 && k.bits <= 8, CQ_ERR_INVALID, n + ": bits must be in [2, 8]");
   CQ_REQUIRE(k.code_order == CQ_ORDER_NATURAL || (k.code_order == CQ_ORDER_MMA && c->head_dim % 64 == 0) ||
-                 (k.code_order == CQ_ORDER_PLANES3 && c->head_dim == 128 && k.bits <= 3),
-             CQ_ERR_INVALID, n + ": code_order MMA needs head_dim % 64 == 0; PLANES3 needs head_dim 128 and "
-                                 "bits <= 3");
+                 (k.code_order == CQ_ORDER_PLANES3 && c->head_dim == 128 && k.bits <= 3) ||
+                 (k.code_order == CQ_ORDER_PLANES2 && c->head_dim == 128 && k.bits <= 2),
+             CQ_ERR_INVALID, n + ": code_order MMA needs head_dim % 64 == 0; PLANES3 (PLANES2) needs head_dim "
+                                 "128 and bits <= 3 (<= 2)");
   if (k.chunk_tokens > 0 && k.chunk_tokens != c->page_tokens) {
     CQ_REQUIRE(c->page_tokens % k.chunk_tokens == 0 && k.chunk_tokens % k.stride == 0, CQ_ERR_INVALID,
                n + ": chunk_tokens must divide page_tokens and be a multiple of the stride");

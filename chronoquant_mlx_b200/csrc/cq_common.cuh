@@ -73,7 +73,9 @@ inline CacheView make_view(const cq_paged_cache &c) {
     v.c[i].bits = src[i]->bits;
     v.c[i].dead_zone = src[i]->dead_zone;
     const cq_component &k = *src[i];
-    const int W = k.code_order == CQ_ORDER_PLANES3 ? 12 : (c.head_dim + 7) >> 3;  // row words
+    const int W = k.code_order == CQ_ORDER_PLANES3   ? 12
+                  : k.code_order == CQ_ORDER_PLANES2 ? 8
+                                                     : (c.head_dim + 7) >> 3;  // row words
     const int ct = k.chunk_tokens > 0 ? k.chunk_tokens : c.page_tokens;
     v.c[i].ac = ct / k.stride;
     v.c[i].pc = ct - v.c[i].ac;
@@ -110,7 +112,7 @@ int validate_cache(const cq_paged_cache *c);
 __host__ __device__ inline int words_of(int D) { return (D + 7) >> 3; }
 // Words of one code row in the cache's layout (the reference layout is words_of).
 __host__ __device__ inline int row_words(int D, int order) {
-  return order == CQ_ORDER_PLANES3 ? 12 : words_of(D);  // PLANES3: head_dim 128
+  return order == CQ_ORDER_PLANES3 ? 12 : order == CQ_ORDER_PLANES2 ? 8 : words_of(D);  // planes: head_dim 128
 }
 
 // Position of dim d's nibble in a code row: word index and bit shift.
@@ -222,6 +224,7 @@ __device__ __forceinline__ int nibble_at(const uint32_t *row, int d, int D, int 
     const uint32_t lo = (row[g] >> (2 * k)) & 3u, hi = (row[8 + (g >> 1)] >> (16 * (g & 1) + k)) & 1u;
     return (int)(lo | (hi << 2)) + 4;
   }
+  if (order == CQ_ORDER_PLANES2) return (int)((row[d & 7] >> (2 * (d >> 3))) & 3u) + 6;  // code + 2
   int w, s;
   nibble_pos(d, D, order, w, s);
   return (int)((row[w] >> s) & 0xFu);
@@ -235,6 +238,10 @@ __device__ __forceinline__ void pack_code(uint32_t *sw, int d, int D, int order,
     const int g = d & 7, k = d >> 3;
     atomicOr(&sw[g], (v & 3u) << (2 * k));
     atomicOr(&sw[8 + (g >> 1)], (v >> 2) << (16 * (g & 1) + k));
+    return;
+  }
+  if (order == CQ_ORDER_PLANES2) {  // head_dim 128: code + 2, in [0, 4) for codes of 2 bits
+    atomicOr(&sw[d & 7], ((nib - 6u) & 3u) << (2 * (d >> 3)));
     return;
   }
   int w, s;

@@ -84,12 +84,14 @@ constexpr int cx_max(int a, int b) { return a > b ? a : b; }
 // per chunk, anchors per chunk and the byte offsets of a chunk block's six
 // segments [K anchors][K codes][K scales][V anchors][V codes][V scales]
 // (each 16-byte aligned) -- the layout the cache stores and a slot mirrors.
-template <int SK_, int SV_, bool V3_ = false>
+template <int SK_, int SV_, int VP_ = 4>
 struct Geo {
   static constexpr int SK = SK_, SV = SV_;
-  // V3: V code rows of physical 3-bit codes (CQ_ORDER_PLANES3, 48 bytes) instead of INT4 lanes (64 bytes)
-  static constexpr bool V3 = V3_;
-  static constexpr int VR = V3 ? 48 : HD / 2;
+  // VP: bits per stored V code -- 4 (INT4 lanes, 64-byte rows), or bit planes of physical 3-bit
+  // (CQ_ORDER_PLANES3, 48 bytes) or 2-bit codes (CQ_ORDER_PLANES2, 32 bytes)
+  static constexpr int VP = VP_;
+  static constexpr bool V3 = VP == 3, PL = VP < 4;
+  static constexpr int VR = VP == 3 ? 48 : VP == 2 ? 32 : HD / 2;
   static constexpr int LSK = cx_log2(SK), LSV = cx_log2(SV);
   static constexpr int C = cx_max(32, cx_max(SK, SV));
   static constexpr int NT = C / 16;
@@ -356,7 +358,7 @@ struct VAddr {
   __device__ __forceinline__ VAddr(G, uint32_t vb, int lane) {
     const int g = lane >> 2, t = lane & 3, mi = lane >> 3;
     constexpr bool v8 = G::LSV == 3;
-    cdV = vb + G::V_CD + (2 * t - 1) * G::VR + (G::V3 ? 0 : g * 8);  // 3-bit rows: lane offsets at use
+    cdV = vb + G::V_CD + (2 * t - 1) * G::VR + (G::PL ? 0 : g * 8);  // bit-plane rows: lane offsets at use
     dv8 = v8 ? 7 : 8;
     scV = vb + G::V_SC + t * 4;
     kfV0 = vb + ((mi & 1) ? 16 : 0);
@@ -516,18 +518,23 @@ __device__ __forceinline__ void v_tile(WarpState &st, const VAddr &A, int tb, ui
       ptx::mma_f16_16816(st.o[i], a0, a1, a2, a3, bP0, bP1);
     }
   }
-  if constexpr (G::V3) {
-    // 3-bit V codes: a row's low bit plane word g holds dims 8k + g (k = 0..15) at bits 2k, its high
-    // plane half-word g the same dims' third bits at bit k (CQ_ORDER_PLANES3); the fp16 operand
-    // 64 + v = code + 68 gets the low bits at bits 4-5 and the high bit at bit 6 of each half
+  if constexpr (G::PL) {
+    // bit-plane V codes: a row's low plane word g holds dims 8k + g (k = 0..15) at bits 2k; with
+    // 3-bit codes a high plane half-word g holds the same dims' third bits at bit k
+    // (CQ_ORDER_PLANES3, CQ_ORDER_PLANES2).  The fp16 operand 64 + v (v = code + 4, or code + 2)
+    // gets the low bits at bits 4-5 and the high bit at bit 6 of each half
+    constexpr uint32_t R = G::VR;  // bytes per row
     const int g = lane >> 2;
-    const uint32_t r0 = A.cdV + (uint32_t)((tb - (tb >> lsv)) * 48);
-    const uint32_t r2 = r0 + (uint32_t)A.dv8 * 48;
+    const uint32_t r0 = A.cdV + (uint32_t)((tb - (tb >> lsv)) * R);
+    const uint32_t r2 = r0 + (uint32_t)A.dv8 * R;
     const uint32_t lo = 4 * g, hi = 32 + 2 * g;
-    const uint32_t la = ptx::lds_u32(r0 + lo), lb = ptx::lds_u32(r0 + 48 + lo);
-    const uint32_t lc = ptx::lds_u32(r2 + lo), ld = ptx::lds_u32(r2 + 48 + lo);
-    const uint32_t hab = __byte_perm(ptx::lds_u16(r0 + hi), ptx::lds_u16(r0 + 48 + hi), 0x5410u);
-    const uint32_t hcd = __byte_perm(ptx::lds_u16(r2 + hi), ptx::lds_u16(r2 + 48 + hi), 0x5410u);
+    const uint32_t la = ptx::lds_u32(r0 + lo), lb = ptx::lds_u32(r0 + R + lo);
+    const uint32_t lc = ptx::lds_u32(r2 + lo), ld = ptx::lds_u32(r2 + R + lo);
+    uint32_t hab = 0u, hcd = 0u;
+    if constexpr (G::V3) {
+      hab = __byte_perm(ptx::lds_u16(r0 + hi), ptx::lds_u16(r0 + R + hi), 0x5410u);
+      hcd = __byte_perm(ptx::lds_u16(r2 + hi), ptx::lds_u16(r2 + R + hi), 0x5410u);
+    }
 #pragma unroll
     for (int q = 0; q < 2; ++q) {
 #pragma unroll
@@ -535,14 +542,18 @@ __device__ __forceinline__ void v_tile(WarpState &st, const VAddr &A, int tb, ui
         const int bi = 2 * q + half;  // byte of the low plane (4 dims), nibble of the high plane
         const uint32_t sel = bi | (bi << 4) | ((4 + bi) << 8) | ((4 + bi) << 12);
         const uint32_t xab = __byte_perm(la, lb, sel), xcd = __byte_perm(lc, ld, sel);
-        const uint32_t yab = hab >> (4 * bi), ycd = hcd >> (4 * bi);
         uint32_t xa[4], xc[4];
 #pragma unroll
         for (int kk = 0; kk < 4; ++kk) {
           const int sl = 4 - 2 * kk;  // low bits 2kk..2kk+1 -> 4..5; high bit kk -> 6
           const uint32_t pa = sl >= 0 ? xab << sl : xab >> -sl, pc = sl >= 0 ? xcd << sl : xcd >> -sl;
-          xa[kk] = ptx::lop3_and_or(yab << (6 - kk), 0x00400040u, ptx::lop3_and_or(pa, 0x00300030u, 0x54005400u));
-          xc[kk] = ptx::lop3_and_or(ycd << (6 - kk), 0x00400040u, ptx::lop3_and_or(pc, 0x00300030u, 0x54005400u));
+          xa[kk] = ptx::lop3_and_or(pa, 0x00300030u, 0x54005400u);
+          xc[kk] = ptx::lop3_and_or(pc, 0x00300030u, 0x54005400u);
+          if constexpr (G::V3) {
+            const uint32_t yab = hab >> (4 * bi), ycd = hcd >> (4 * bi);
+            xa[kk] = ptx::lop3_and_or(yab << (6 - kk), 0x00400040u, xa[kk]);
+            xc[kk] = ptx::lop3_and_or(ycd << (6 - kk), 0x00400040u, xc[kk]);
+          }
         }
         // dim index k = 8q + 4 half + kk <-> m-tile 4q + (4 half + kk)/2, row g (+8 when kk is odd)
         const int i0 = 4 * q + 2 * half;
@@ -550,8 +561,9 @@ __device__ __forceinline__ void v_tile(WarpState &st, const VAddr &A, int tb, ui
         ptx::mma_f16_16816(st.o[i0 + 1], xa[2], xa[3], xc[2], xc[3], bS0, bS1);
       }
     }
-    // the offset 68 of every code value: 68 * sum_t P'_t, exactly as the MMAs above weight it
-    ptx::mma_f16_16816(st.vb, ptx::HALF2_68, ptx::HALF2_68, ptx::HALF2_68, ptx::HALF2_68, bS0, bS1);
+    // the offset of every code value (68 or 66): offset * sum_t P'_t, exactly as the MMAs above weight it
+    constexpr uint32_t OFF = G::V3 ? ptx::HALF2_68 : ptx::HALF2_66;
+    ptx::mma_f16_16816(st.vb, OFF, OFF, OFF, OFF, bS0, bS1);
   } else
   // V codes: O += C_v^T P'  (tokens 2t,2t+1 | 2t+8,2t+9; words 2g, 2g+1)
   {
@@ -685,10 +697,11 @@ __device__ void encode_new_token(const Params &p, unsigned char *part, int64_t p
 #pragma unroll
     for (int i = 0; i < kMaxDimsPerLane; ++i) av[i] = (i < HD / 32) ? __half2float(arow_s[lane + 32 * i]) : 0.f;
     // the fast kernel's layouts: K codes in natural order, V codes in the MMA nibble order or bit planes
-    constexpr int order = COMP ? (G::V3 ? CQ_ORDER_PLANES3 : CQ_ORDER_MMA) : CQ_ORDER_NATURAL;
+    constexpr int order =
+        COMP ? (G::VP == 3 ? CQ_ORDER_PLANES3 : G::VP == 2 ? CQ_ORDER_PLANES2 : CQ_ORDER_MMA) : CQ_ORDER_NATURAL;
     const float scale = encode_residual<DTYPE>(xv, av, HD, c.bits, c.dead_zone, order, sw, lane);
     const int pf = x - a - 1;
-    constexpr int rw = (COMP && G::V3) ? 12 : HD / 8;  // words of a code row
+    constexpr int rw = COMP ? G::VR / 4 : HD / 8;  // words of a code row
     if (lane < rw) {
       ((uint32_t *)(part + ocd + pf * rw * 4))[lane] = sw[lane];
       ((uint32_t *)(blk + ocd + pf * rw * 4))[lane] = sw[lane];
@@ -1157,30 +1170,31 @@ using KernelFn = void (*)(Params);
 
 // One supported (stride_k, stride_v) pair: its geometry and kernel.
 struct GeoInfo {
-  int sk, sv, v3, C, slot, buf;
+  int sk, sv, vp, C, slot, buf;
   int off[6];  // K anchors, K codes, K scales, V anchors, V codes, V scales
   KernelFn fn;
 };
 
-template <int SK, int SV, bool V3 = false>
+template <int SK, int SV, int VP = 4>
 static GeoInfo geo_info() {
-  using G = Geo<SK, SV, V3>;
-  return GeoInfo{SK, SV, V3, G::C, G::SLOT, G::BUF, {G::O_KF0, G::O_CD0, G::O_SC0, G::O_KF1, G::O_CD1, G::O_SC1},
+  using G = Geo<SK, SV, VP>;
+  return GeoInfo{SK, SV, VP, G::C, G::SLOT, G::BUF, {G::O_KF0, G::O_CD0, G::O_SC0, G::O_KF1, G::O_CD1, G::O_SC1},
                  decode_kernel<G>};
 }
 
 // Every pair the kernel takes: power-of-two strides, stride_k in {16, 32, 64}
 // (one K anchor per 16-token tile), stride_v in {8, .., 64}; with physical
-// 3-bit V rows (v3), the Full-Throttle (64, 32) and Standard (32, 8) pairs.
-static const GeoInfo *find_geo(int sk, int sv, int *index = nullptr, bool v3 = false) {
+// 3-bit or 2-bit V rows (vp 3, 2), the Full-Throttle (64, 32) and Standard
+// (32, 8) pairs.
+static const GeoInfo *find_geo(int sk, int sv, int *index = nullptr, int vp = 4) {
   static const GeoInfo table[] = {
       geo_info<16, 8>(),  geo_info<16, 16>(), geo_info<16, 32>(), geo_info<16, 64>(),
       geo_info<32, 8>(),  geo_info<32, 16>(), geo_info<32, 32>(), geo_info<32, 64>(),
       geo_info<64, 8>(),  geo_info<64, 16>(), geo_info<64, 32>(), geo_info<64, 64>(),
-      geo_info<64, 32, true>(), geo_info<32, 8, true>(),
+      geo_info<64, 32, 3>(), geo_info<32, 8, 3>(), geo_info<64, 32, 2>(), geo_info<32, 8, 2>(),
   };
   for (int i = 0; i < (int)(sizeof(table) / sizeof(table[0])); ++i)
-    if (table[i].sk == sk && table[i].sv == sv && table[i].v3 == (int)v3) {
+    if (table[i].sk == sk && table[i].sv == sv && table[i].vp == vp) {
       if (index) *index = i;
       return &table[i];
     }
@@ -1206,7 +1220,8 @@ struct Layout {
 // kernel's geometry, the six arrays' base pointers pointing into the first
 // block.  A slot is a byte image of one block.
 static bool make_layout(const cq_paged_cache &c, Layout &L) {
-  L.geo = find_geo(c.k.stride, c.v.stride, &L.gi, c.v.code_order == CQ_ORDER_PLANES3);
+  const int vp = c.v.code_order == CQ_ORDER_PLANES3 ? 3 : c.v.code_order == CQ_ORDER_PLANES2 ? 2 : 4;
+  L.geo = find_geo(c.k.stride, c.v.stride, &L.gi, vp);
   if (!L.geo) return false;
   L.C = L.geo->C;
   if (c.page_tokens % L.C || c.k.chunk_tokens != L.C || c.v.chunk_tokens != L.C) return false;
@@ -1243,7 +1258,8 @@ bool fast_decode_supported(const cq_paged_cache &c, int n_q_heads, int q_len) {
   const int gqa = n_q_heads / c.kv_heads;
   if (gqa < 1 || gqa > 8) return false;
   if (c.k.code_order != CQ_ORDER_NATURAL) return false;
-  if (c.v.code_order != CQ_ORDER_MMA && c.v.code_order != CQ_ORDER_PLANES3) return false;
+  if (c.v.code_order != CQ_ORDER_MMA && c.v.code_order != CQ_ORDER_PLANES3 && c.v.code_order != CQ_ORDER_PLANES2)
+    return false;
   if (c.k.scale_index != CQ_SCALE_BY_TOKEN || c.v.scale_index != CQ_SCALE_BY_TOKEN) return false;
   if (!aligned16(c.k.keyframes)) return false;
   Layout L;

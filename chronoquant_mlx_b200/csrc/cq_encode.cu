@@ -329,6 +329,28 @@ __global__ void __launch_bounds__(kEncodeWarps * 32) append_block_kernel(EncodeA
         row[3 * j + q] = o;
       }
     }
+  } else if (c.order == CQ_ORDER_PLANES2) {
+    // v = code + 2: dim g + 8 k' in word g at bits 2 k', with k' = 4 j + k
+    uint32_t w[8];
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      uint32_t v = 0u;
+#pragma unroll
+      for (int k = 0; k < 4; ++k) v |= ((nib[k][g] - 6u) & 3u) << (2 * (4 * j + k));
+      v |= __shfl_xor_sync(0xffffffffu, v, 1);
+      w[g] = v | __shfl_xor_sync(0xffffffffu, v, 2);
+    }
+    if (pframe) {
+#pragma unroll
+      for (int q = 0; q < 2; ++q) {
+        // word 2 j + q of the row, selected without local memory
+        uint32_t o = w[q];
+#pragma unroll
+        for (int jj = 1; jj < 4; ++jj)
+          if (j == jj) o = w[2 * jj + q];
+        row[2 * j + q] = o;
+      }
+    }
   } else if (pframe) {  // natural: word 4 j + k holds dims 32 j + 8 k .. + 7, nibble g at bit 4 g
     uint32_t wd[4];
 #pragma unroll

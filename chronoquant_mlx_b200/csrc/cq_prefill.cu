@@ -610,8 +610,9 @@ using namespace prefill;
 
 bool prefill_supported(const cq_paged_cache &c, int n_q_heads, int q_len) {
   if (c.head_dim != kTile || q_len < kMinRows) return false;
-  // the tile images are built from INT4-lane code rows; physical 3-bit rows take the general kernel
-  if (c.k.code_order == CQ_ORDER_PLANES3 || c.v.code_order == CQ_ORDER_PLANES3) return false;
+  // the tile images are built from INT4-lane code rows; bit-plane rows take the general kernel
+  for (int o : {c.k.code_order, c.v.code_order})
+    if (o == CQ_ORDER_PLANES3 || o == CQ_ORDER_PLANES2) return false;
   const int G = n_q_heads / c.kv_heads;
   return G >= 1 && G <= 16 && (G & (G - 1)) == 0;
 }

@@ -190,6 +190,7 @@ __device__ __forceinline__ void nibbles_to_half2_64(uint32_t x, uint32_t (&out)[
 }
 constexpr uint32_t HALF2_72 = 0x54805480u;  // (72, 72)
 constexpr uint32_t HALF2_68 = 0x54405440u;  // (68, 68)
+constexpr uint32_t HALF2_66 = 0x54205420u;  // (66, 66)
 
 // Raw nibble values under the fp16 exponent of 1024 (0x6400, one unit in the
 // last place = 1): out[0], out[2] hold 1024 + n (nibbles 0 and 2 of each

@@ -61,6 +61,10 @@ extern "C" {
  * reference counterpart: the reference stores 3-bit codes in INT4 lanes
  * (README.md:57); cq_export_state still produces that layout. */
 #define CQ_ORDER_PLANES3 2
+/* Physical 2-bit codes (opt-in; bits <= 2, head_dim 128): a code row is 8
+ * words, v = code + 2 in [0, 4) at word g, bits 2k..2k+1 (the low plane of
+ * CQ_ORDER_PLANES3). */
+#define CQ_ORDER_PLANES2 3
 
 /*
  * One compressed component (K or V) of a paged cache.  Token t of sequence b

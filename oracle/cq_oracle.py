@@ -184,6 +184,27 @@ def pack_planes3(codes: np.ndarray) -> np.ndarray:
     return np.concatenate([lo, hi], axis=-1).astype(np.uint32)
 
 
+def pack_planes2(codes: np.ndarray) -> np.ndarray:
+    """Physical 2-bit rows of this build's opt-in ``v_pack=2`` format (no
+    reference counterpart).  ``codes`` int8 [..., 128] in [-2, 1]; v = code +
+    2 in [0, 4).  Returns uint32 [..., 8]: with g = d % 8 and k = d // 8, dim d
+    at word g, bits 2k..2k+1 (the low plane of ``pack_planes3``)."""
+    c = np.asarray(codes).astype(np.int32)
+    assert c.shape[-1] == 128 and c.min(initial=0) >= -2 and c.max(initial=0) <= 1
+    v = (c + 2).astype(np.uint32).reshape(*c.shape[:-1], 16, 8)  # [..., k, g]
+    k = np.arange(16, dtype=np.uint32)[:, None]
+    return np.bitwise_or.reduce(v << (2 * k), axis=-2).astype(np.uint32)
+
+
+def unpack_planes2(rows: np.ndarray, head_dim: int = 128) -> np.ndarray:
+    """Inverse of ``pack_planes2``: int8 codes [..., 128]."""
+    assert head_dim == 128
+    r = np.asarray(rows, dtype=np.uint32)
+    k = np.arange(16, dtype=np.uint32)[:, None]
+    v = (r[..., None, :] >> (2 * k)) & np.uint32(3)  # [..., k, g]
+    return (v.astype(np.int32) - 2).reshape(*r.shape[:-1], 128).astype(np.int8)
+
+
 def unpack_planes3(rows: np.ndarray, head_dim: int = 128) -> np.ndarray:
     """Inverse of ``pack_planes3``: int8 codes [..., 128]."""
     assert head_dim == 128

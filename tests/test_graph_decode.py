@@ -37,6 +37,9 @@ def test_decode_graph_is_exported():
     # physical 3-bit V codes: the step kernel encodes into bit-plane rows
     (2, 2, 8, 700, 64, 32, 40, 0, 3),
     (1, 2, 8, 300, 32, 8, 20, 0, 3),
+    # physical 2-bit V codes
+    (2, 2, 8, 700, 64, 32, 40, 0, 2),
+    (1, 2, 8, 300, 32, 8, 20, 0, 2),
 ])
 def test_graph_step_matches_eager(B, Hkv, Hq, T, sk, sv, steps, headroom, v_pack):
     if not torch.cuda.is_available():
@@ -47,8 +50,8 @@ def test_graph_step_matches_eager(B, Hkv, Hq, T, sk, sv, steps, headroom, v_pack
     K = torch.from_numpy(K).to(dev).half()
     V = torch.from_numpy(V).to(dev).half()
     kw = dict(stride_k=sk, stride_v=sv, dead_zone_v=0.0, max_tokens=T + steps + headroom + 8)
-    if v_pack == 3:
-        kw.update(delta_bits_v=3, v_pack=3)
+    if v_pack < 4:
+        kw.update(delta_bits_v=v_pack, v_pack=v_pack)
     eager, graphed = ChronoQuantCache(**kw), ChronoQuantCache(**kw)
     for c in (eager, graphed):
         c.update_and_fetch(K[:, :, :T], V[:, :, :T])
