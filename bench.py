@@ -800,7 +800,7 @@ def run_decoder(args, cfg):
         from chronoquant_mlx_b200.decoder import mesh_groups
         tp_group, seq_group = mesh_groups(n_seq, n_tp)
     dec = Qwen3StyleDecoder(dc, B, T0 + n_steps + 4, kw, device=device, seed=100 if one_model else 100 + rank,
-                            tp_group=tp_group, seq_group=seq_group)
+                            tp_group=tp_group, seq_group=seq_group, peer_sum=not args.nccl_allreduce)
     dec.fill_context(T0, seed=200 if one_model else 200 + rank)
     dec.ids.copy_(torch.arange(B, device=device) * 7 + 1)
     dec.capture()
@@ -870,10 +870,15 @@ def run_decoder(args, cfg):
         del cg
     if tp:
         xr = torch.zeros((B, dc.hidden), device=device, dtype=torch.bfloat16)
+        yr = torch.empty_like(xr)
+        ln = dec.layers[0]["ln2"]
         cg = torch.cuda.CUDAGraph()
         with torch.cuda.graph(cg):
-            for _ in range(2 * dc.layers):
-                dec._reduce(xr)
+            for k in range(2 * dc.layers):
+                if dec.peer is not None:  # the fused peer sum + residual + RMSNorm of the step
+                    dec.peer(xr, ln, dc.eps, yr, k & 1)
+                else:
+                    dec._reduce(xr)
         cg.replay()
         torch.cuda.synchronize()
         c0, c1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
@@ -882,7 +887,8 @@ def run_decoder(args, cfg):
             cg.replay()
         c1.record(stream)
         torch.cuda.synchronize()
-        comm["tp_allreduce_ms_per_step"] = round(c0.elapsed_time(c1) / reps, 4)
+        comm["tp_peer_sum_norm_ms_per_step" if dec.peer is not None else "tp_allreduce_ms_per_step"] = round(
+            c0.elapsed_time(c1) / reps, 4)
         del cg
 
     # e2e: a host-driven serving loop -- every step's input ids copied in from pinned host
@@ -909,6 +915,8 @@ def run_decoder(args, cfg):
         dist.all_reduce(tt, op=dist.ReduceOp.MAX)
         e_ms = float(tt.item())
     peak, peak_kind = load_peak()
+    tp_sum = ("one kernel: peer-memory sum over NVLink + residual add + RMSNorm" if dec.peer is not None else
+              "NCCL all-reduce")
     if rank == 0:
         res = {
             "metric": DECODER_METRIC, "value": round(value, 1), "unit": "tokens/s", "n_gpus": world,
@@ -922,10 +930,10 @@ def run_decoder(args, cfg):
                        "step": "one CUDA-graph replay: 36 x (RMSNorm, QKV, q/k norm, RoPE, fused append+decode "
                                "attention, o_proj, SwiGLU) + lm_head + argmax",
                        "parallelism": (f"seq{n_seq} x tp{n_tp} ({n_seq} token ranges of the context, each over "
-                                       f"{n_tp} kv-head tensor-parallel ranks: NCCL all-reduce after o_proj and the "
+                                       f"{n_tp} kv-head tensor-parallel ranks: {tp_sum} after o_proj and the "
                                        "down projection within a range, all-gather of partial attention + "
                                        "log-sum-exp merge per layer across ranges)") if tp and split else
-                                      (f"tp{world} (kv-head tensor parallel, NCCL all-reduce after o_proj and "
+                                      (f"tp{world} (kv-head tensor parallel, {tp_sum} after o_proj and "
                                        "the down projection)") if tp else
                                       (f"seq{world} (token ranges of one sequence per rank, NCCL all-gather of "
                                        "partial attention + log-sum-exp merge per layer)") if split else
@@ -1519,6 +1527,9 @@ def main():
     ap.add_argument("--page-tokens", type=int, default=None, help="cache page size (default: the cache's choice)")
     ap.add_argument("--cpu-rows", type=int, default=128, help="config 4 CPU sample: query rows per kv-head")
     ap.add_argument("--tp", action="store_true", help="config 5 under torchrun: kv-head tensor parallel")
+    ap.add_argument("--nccl-allreduce", action="store_true",
+                    help="config 5 tensor parallel: NCCL all-reduce + separate add and RMSNorm instead of the fused "
+                         "peer-memory sum")
     ap.add_argument("--tp-size", type=int, default=None,
                     help="config 5 with --tp and --seqsplit: tensor-parallel ranks per token range (the mesh is "
                          "(N / tp-size) token ranges x tp-size; default 2)")

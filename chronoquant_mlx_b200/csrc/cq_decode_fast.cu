@@ -1451,18 +1451,22 @@ extern "C" int cq_decode_chunk_tokens(int32_t stride_k, int32_t stride_v, int32_
 
 namespace cq {
 int read_append_error(int clear);
+namespace peer {
+int read_peer_error(int clear);
+}
 }
 
 extern "C" int cq_device_error(int *code, int clear) {
   if (!code) return cq::set_error(CQ_ERR_INVALID, "cq_device_error: code is null");
   const int a = cq::read_fast_error(clear), b = cq::read_append_error(clear), c = cq::read_prefill_error(clear);
+  const int p = cq::peer::read_peer_error(clear);
   int d = 0;  // bounds checks of a CQ_CHECKS build
   for (int (*rd)(int) : {cq::read_bounds_error_encode, cq::read_bounds_error_layout, cq::read_bounds_error_attention,
                          cq::read_bounds_error_prefill, cq::read_bounds_error_decode}) {
     const int v = rd(clear);
     if (!d) d = v;
   }
-  *code = a ? a : (b ? b : (c ? c : d));
+  *code = a ? a : (b ? b : (c ? c : (p ? p : d)));
   cudaError_t e = cudaGetLastError();
   if (e != cudaSuccess) return cq::set_error(CQ_ERR_CUDA, cudaGetErrorString(e));
   return CQ_OK;

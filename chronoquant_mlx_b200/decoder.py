@@ -103,7 +103,8 @@ class Qwen3StyleDecoder:
     greedy decode step for ``batch`` sequences of up to ``max_len`` tokens."""
 
     def __init__(self, cfg: DecoderConfig, batch: int, max_len: int, cache_kwargs: dict | None = None,
-                 device="cuda", dtype=torch.bfloat16, seed: int = 0, tp_group=None, seq_group=None):
+                 device="cuda", dtype=torch.bfloat16, seed: int = 0, tp_group=None, seq_group=None,
+                 peer_sum: bool = True):
         """``tp_group``: a torch.distributed (NCCL) group over which the layers
         are tensor-parallel by kv-head: this rank keeps kv_heads/N kv-heads
         with their query heads and ffn/N of each FFN; the o_proj and down
@@ -116,6 +117,11 @@ class Qwen3StyleDecoder:
         last rank owns the tail and encodes the new tokens.  Each layer's
         attention is a partial (output, log-sum-exp) per rank, all-gathered
         (NCCL) and merged by cq_lse_merge_packed, all inside the captured step.
+
+        ``peer_sum`` (tensor parallel): each row-parallel projection's sum
+        over the ranks, with the residual add and the next RMSNorm, is one
+        ``PeerSumNorm`` kernel reading the other ranks' parts over NVLink;
+        False uses an NCCL all-reduce followed by the separate add and norm.
 
         Both together (``mesh_groups``): the layers are tensor-parallel over
         ``tp_group`` and each rank's kv-heads hold its token range of the
@@ -176,6 +182,10 @@ class Qwen3StyleDecoder:
         self.pos = torch.zeros((), dtype=torch.long, device=self.device)   # their position
         self.out_ids = torch.zeros(batch, dtype=torch.long, device=self.device)
         self.graph = None
+        self.peer = None
+        if self.world > 1 and peer_sum:
+            from .peer import PeerSumNorm
+            self.peer = PeerSumNorm(tp_group, batch, c.hidden, dtype=dtype, device=self.device)
 
     # -- context ---------------------------------------------------------------
     def fill_context(self, T0: int, chunk: int = 4096, seed: int = 1) -> None:
@@ -279,14 +289,29 @@ class Qwen3StyleDecoder:
             dist.all_reduce(partial, group=self.group)
         return partial
 
+    def _project_sum_norm(self, x: torch.Tensor, a: torch.Tensor, wt: torch.Tensor, w_norm: torch.Tensor,
+                          parity: int) -> torch.Tensor:
+        """x <- x + (sum over the tensor-parallel ranks of a @ wt.T); returns
+        RMSNorm(x) * w_norm.  With peer sums: the GEMM writes this rank's part
+        into its peer region and one kernel does the sum, the add and the norm."""
+        if self.peer is not None:
+            torch.matmul(a, wt.t(), out=self.peer.part(parity))
+            y = torch.empty_like(x)
+            self.peer(x, w_norm, self.cfg.eps, y, parity)
+            return y
+        x += self._reduce(a @ wt.t())
+        return self._norm(x, w_norm)
+
     def _step_body(self, attention=None) -> torch.Tensor:
         c, B = self.cfg, self.B
         attention = attention or self._attention
         nq, nk = self.heads * c.head_dim, self.kv_heads * c.head_dim
         lib, st, dt = _lib.lib(), stream_ptr(self.device), cq_dtype(self.embed)
-        x = self.embed[self.ids]
-        for L in self.layers:
-            qkv = self._norm(x, L["ln1"]) @ L["wqkv"].t()
+        x = self.embed[self.ids]  # a fresh tensor: updated in place below
+        xn = self._norm(x, self.layers[0]["ln1"])
+        parity = 0  # peer part buffers alternate per call; a step makes an even number of calls
+        for i, L in enumerate(self.layers):
+            qkv = xn @ L["wqkv"].t()
             q = torch.empty((B, self.heads, c.head_dim), device=self.device, dtype=self.dtype)
             k = torch.empty((B, self.kv_heads, c.head_dim), device=self.device, dtype=self.dtype)
             v = torch.empty_like(k)
@@ -295,12 +320,15 @@ class Qwen3StyleDecoder:
                                            self.pos.data_ptr(), c.eps, q.data_ptr(), k.data_ptr(), v.data_ptr(), dt,
                                            st), "decoder")
             a = attention(L, q, k, v)
-            x = x + self._reduce(a.reshape(B, nq) @ L["wo"].t())
-            gu = self._norm(x, L["ln2"]) @ L["wgu"].t()
+            xn = self._project_sum_norm(x, a.reshape(B, nq), L["wo"], L["ln2"], parity)
+            parity ^= 1
+            gu = xn @ L["wgu"].t()
             h = torch.empty((B, self.ffn), device=self.device, dtype=self.dtype)
             _lib.check(lib.cq_silu_mul(gu.data_ptr(), h.data_ptr(), B, self.ffn, dt, st), "decoder")
-            x = x + self._reduce(h @ L["wdown"].t())
-        logits = self._norm(x, self.final_norm) @ self.lm_head.t()
+            w_next = self.layers[i + 1]["ln1"] if i + 1 < len(self.layers) else self.final_norm
+            xn = self._project_sum_norm(x, h, L["wdown"], w_next, parity)
+            parity ^= 1
+        logits = xn @ self.lm_head.t()
         self.out_ids.copy_(logits.argmax(-1))
         self.ids.copy_(self.out_ids)
         self.pos.add_(1)
@@ -322,7 +350,7 @@ class Qwen3StyleDecoder:
         for wt in (L0["wqkv"], L0["wgu"], self.lm_head):
             x @ wt.t()
         (torch.zeros((self.B, self.ffn), device=self.device, dtype=self.dtype) @ L0["wdown"].t())
-        if self.world > 1:  # the communicator exists before the capture
+        if self.world > 1 and self.peer is None:  # the communicator exists before the capture
             self._reduce(torch.zeros((self.B, c.hidden), device=self.device, dtype=self.dtype))
         if self.seq_group is not None:
             self.o_part.zero_()

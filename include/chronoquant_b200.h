@@ -139,8 +139,28 @@ int cq_decode_chunk_tokens(int32_t stride_k, int32_t stride_v, int32_t page_toke
  * wrote nothing), 6 = the tensor-core query-chunk kernel gave up on a bounded
  * wait (its output is incomplete), 7 = (debug build with -DCQ_CHECKS only) a
  * page index outside the block-table row or the page pool, replaced by page 0
- * (results invalid).  Synchronises the device; clear != 0 resets the word. */
+ * (results invalid), 9 = cq_peer_sum_norm gave up waiting for a peer rank
+ * (its rows unwritten).  Synchronises the device; clear != 0 resets the word. */
 int cq_device_error(int *code, int clear);
+
+/* Row-parallel sum over NVLink peer memory, fused with the residual add and
+ * RMSNorm that follow it in a tensor-parallel decode step (no reference
+ * counterpart: the reference runs on one device).  Every rank owns a region of
+ * cq_peer_region_bytes(part_bytes) zero-filled bytes that every rank has
+ * mapped (CUDA IPC): [64 u32 flags][part buffer 0][part buffer 1].  Before
+ * the call, this rank's part [rows][dim] (dtype) is in part buffer `parity`
+ * of its own region; calls alternate parity.  regions: host array of the
+ * world regions' device addresses in rank order.  The kernel signals the
+ * other ranks, waits (bounded; error 9 in cq_device_error when it gives up)
+ * for theirs, and computes x <- x + dtype(sum over ranks in rank order of the
+ * parts), y <- dtype(x * rsqrt(mean(x^2) + eps)) * w per row.  counter:
+ * device int64[2], zero at the first call, shared by the calls of one region
+ * set (a captured graph replays with fresh epochs).  Every rank makes the
+ * same calls in the same order. */
+int cq_peer_sum_norm(const uint64_t *regions, int32_t world, int32_t rank, int32_t parity, int64_t part_bytes,
+                     int64_t rows, int32_t dim, void *x, const void *w, float eps, void *y, int64_t *counter,
+                     int dtype, void *stream);
+int64_t cq_peer_region_bytes(int64_t part_bytes);
 
 /* Encode S new tokens at absolute positions t0..t0+S-1 for K and V in one
  * launch (cache.py:87-129, codec.py:23-65).  keys/values: [batch][kv_heads]

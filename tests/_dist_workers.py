@@ -5,6 +5,7 @@ partial attention with the oracle (float64 numpy: the test's checker), and
 exchanges partials with ``exchange_partials`` over a gloo process group.
 Results go back through a multiprocessing queue."""
 
+import ctypes
 import datetime
 import math
 import os
@@ -253,6 +254,117 @@ def mesh_groups_worker(rank, world, port, n_seq, queue):
         queue.put((rank, tp_ranks, seq_ranks, seq_sum, None))
     except Exception as e:
         queue.put((rank, None, None, None, repr(e)))
+
+
+def peer_sum_worker(rank, world, port, rows, dim, queue):
+    """PeerSumNorm on `world` GPUs against a torch restatement: every rank's
+    part all-gathered (NCCL), summed in fp32 in rank order and rounded, added
+    to x (one rounding); y = RMSNorm(x) * w as the torch expression.  Eager
+    calls alternating parity, then four calls captured in a CUDA graph and
+    replayed with new parts.  Returns (max ulps of x, max ulps of y)."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        from chronoquant_mlx_b200.peer import PeerSumNorm
+        from chronoquant_mlx_b200.decoder import _rmsnorm
+        ps = PeerSumNorm(dist.group.WORLD, rows, dim, dtype=torch.bfloat16, device=dev)
+        g = torch.Generator(device=dev).manual_seed(100 + rank)
+        w = (1.0 + 0.1 * torch.randn(dim, generator=g, device=dev)).to(torch.bfloat16)
+        dist.broadcast(w, 0)
+        eps = 1e-6
+
+        def expected(x, part):
+            parts = [torch.empty_like(part) for _ in range(world)]
+            dist.all_gather(parts, part)
+            acc = torch.zeros_like(part, dtype=torch.float32)
+            for p in parts:
+                acc += p.float()
+            xe = (x.float() + acc.to(torch.bfloat16).float()).to(torch.bfloat16)
+            return xe, _rmsnorm(xe, w, eps)
+
+        def ulps(a, b):
+            ia = a.view(torch.int16).int()
+            ib = b.view(torch.int16).int()
+            return int((ia - ib).abs().max())
+
+        worst = [0, 0]
+        x = torch.randn((rows, dim), generator=g, device=dev).to(torch.bfloat16)
+        y = torch.empty_like(x)
+        for k in range(6):  # eager calls, alternating parity
+            part = ps.part(k & 1)
+            part.copy_(torch.randn((rows, dim), generator=g, device=dev) * (k + 1))
+            xe, ye = expected(x, part)
+            ps(x, w, eps, y, k & 1)
+            torch.cuda.synchronize()
+            worst[0] = max(worst[0], ulps(x, xe))
+            worst[1] = max(worst[1], ulps(y, ye))
+        # four calls in a graph: each replay sums the parts written before it
+        xs = [x.clone() for _ in range(4)]
+        ys = [torch.empty_like(x) for _ in range(4)]
+        graph = torch.cuda.CUDAGraph()
+        torch.cuda.synchronize()
+        with torch.cuda.graph(graph):
+            for k in range(4):
+                ps(xs[k], w, eps, ys[k], k & 1)
+        for rep in range(3):
+            x0 = [t.clone() for t in xs]
+            # parts of calls 0, 1 are in buffers 0, 1; calls 2, 3 reuse them, so this rank writes
+            # equal parts for calls k and k + 2 and the expectation follows
+            p01 = [torch.randn((rows, dim), generator=g, device=dev).to(torch.bfloat16) for _ in range(2)]
+            for k in range(2):
+                ps.part(k).copy_(p01[k])
+            graph.replay()
+            torch.cuda.synchronize()
+            for k in range(4):
+                xe, ye = expected(x0[k], p01[k & 1])
+                worst[0] = max(worst[0], ulps(xs[k], xe))
+                worst[1] = max(worst[1], ulps(ys[k], ye))
+            dist.barrier()
+        c = ctypes.c_int(0)
+        from chronoquant_mlx_b200 import _lib
+        _lib.lib().cq_device_error(ctypes.byref(c), 1)
+        del graph
+        dist.barrier()
+        dist.destroy_process_group()
+        queue.put((rank, worst, c.value, None))
+    except Exception as e:
+        queue.put((rank, None, None, repr(e)))
+
+
+def peer_timeout_worker(rank, world, port, queue):
+    """Rank 1 never makes the call: rank 0's wait gives up (bounded) and
+    cq_device_error reports 9; rank 1 stays up (its region mapped) until
+    rank 0 has read the status."""
+    try:
+        os.environ["MASTER_ADDR"] = "127.0.0.1"
+        os.environ["MASTER_PORT"] = str(port)
+        os.environ.setdefault("NCCL_NVLS_ENABLE", "0")
+        torch.cuda.set_device(rank)
+        dev = torch.device("cuda", rank)
+        dist.init_process_group("nccl", rank=rank, world_size=world, timeout=datetime.timedelta(seconds=120),
+                                device_id=dev)
+        from chronoquant_mlx_b200 import _lib
+        from chronoquant_mlx_b200.peer import PeerSumNorm
+        ps = PeerSumNorm(dist.group.WORLD, 2, 256, dtype=torch.bfloat16, device=dev)
+        code = None
+        if rank == 0:
+            x = torch.zeros((2, 256), dtype=torch.bfloat16, device=dev)
+            w = torch.ones(256, dtype=torch.bfloat16, device=dev)
+            y = torch.full_like(x, 7.0)
+            ps(x, w, 1e-6, y, 0)
+            c = ctypes.c_int(0)
+            _lib.lib().cq_device_error(ctypes.byref(c), 1)  # synchronises: the kernel has given up
+            code = (c.value, bool(torch.all(y == 7.0)))
+        dist.barrier()
+        dist.destroy_process_group()
+        queue.put((rank, code, None))
+    except Exception as e:
+        queue.put((rank, None, repr(e)))
 
 
 class _ShardStub:
