@@ -870,13 +870,13 @@ def run_decoder(args, cfg):
         del cg
     if tp:
         xr = torch.zeros((B, dc.hidden), device=device, dtype=torch.bfloat16)
-        yr = torch.empty_like(xr)
+        yr, pr = torch.empty_like(xr), torch.zeros_like(xr)
         ln = dec.layers[0]["ln2"]
         cg = torch.cuda.CUDAGraph()
         with torch.cuda.graph(cg):
             for k in range(2 * dc.layers):
                 if dec.peer is not None:  # the fused peer sum + residual + RMSNorm of the step
-                    dec.peer(xr, ln, dc.eps, yr, k & 1)
+                    dec.peer(pr, xr, ln, dc.eps, yr, k & 1)
                 else:
                     dec._reduce(xr)
         cg.replay()
@@ -959,6 +959,7 @@ def run_decoder(args, cfg):
     if world > 1:
         dec.graph = None  # graphs holding NCCL work go before the process group
         torch.cuda.synchronize()
+        dec.close()
         dist.barrier()
         dist.destroy_process_group()
 

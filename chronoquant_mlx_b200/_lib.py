@@ -35,6 +35,7 @@ EXPORTED = [
     "cq_sdpa_reference_layout_workspace", "cq_attention_static_scratch", "cq_decode_chunk_tokens",
     "cq_append_at", "cq_attention_at", "cq_decode_step_at", "cq_prefill_prepare", "cq_prefill_attend",
     "cq_rmsnorm", "cq_qk_norm_rope", "cq_silu_mul", "cq_peer_sum_norm", "cq_peer_region_bytes",
+    "cq_peer_region_alloc", "cq_peer_region_open", "cq_peer_region_close", "cq_peer_region_free",
 ]
 
 
@@ -106,15 +107,19 @@ def _declare(lib):
         "cq_prefill_attend": [C, I64, I32, I32, I32, P, ctypes.c_int, P, P, SZ, P],
         "cq_attention_static_scratch": [C, I64, P, ctypes.c_int, I32, I32, I32, I64, I64, I64, F, P, ctypes.c_int,
                                         P, I32, P],
-        "cq_peer_sum_norm": [ctypes.POINTER(ctypes.c_uint64), I32, I32, I32, I64, I64, I32, P, P, F, P, P,
+        "cq_peer_sum_norm": [ctypes.POINTER(ctypes.c_uint64), I32, I32, I32, I64, I64, I32, P, P, P, F, P, P,
                              ctypes.c_int, P],
+        "cq_peer_region_alloc": [I64, ctypes.POINTER(P), P],
+        "cq_peer_region_open": [P, ctypes.POINTER(P)],
+        "cq_peer_region_close": [P],
+        "cq_peer_region_free": [P],
     }
     for name, args in sig.items():
         fn = getattr(lib, name)
         fn.restype = ctypes.c_int
         fn.argtypes = args
     lib.cq_peer_region_bytes.restype = I64
-    lib.cq_peer_region_bytes.argtypes = [I64]
+    lib.cq_peer_region_bytes.argtypes = [I64, I32, I32]
     return lib
 
 

@@ -2,29 +2,37 @@
 // over NVLink peer memory, fused with the two operations that follow it in a
 // decode step: the residual add and the next RMSNorm.
 //
-//   x <- x + bf16(sum_r part_r)         (every rank, the same rank order)
-//   y <- bf16(x * rsqrt(mean(x^2) + eps)) * w
+//   x <- x + dtype(sum_r part_r)         (every rank, the same rank order)
+//   y <- dtype(x * rsqrt(mean(x^2) + eps)) * w
 //
-// Every rank owns one region of device memory that the other ranks map (CUDA
-// IPC, opened by the host): [flags: 64 x u32][part buffer 0][part buffer 1].
-// A rank's projection GEMM writes its part into buffer (call parity) of its
-// own region; the kernel then signals "part of call e ready" by storing e
-// into flag slot `rank` of every peer's region (release, system scope), waits
-// until every peer's slot in its own region holds e or more (acquire), reads
-// the row from all regions over NVLink, and writes x and y locally.  Two part
-// buffers alternate by call: a rank overwrites buffer p only two calls later,
-// after every peer has signalled the call in between, which it does only once
-// its reads of buffer p are done (stream order).  e is a device counter that
-// the last block advances, so a captured graph replays with fresh epochs.
-// Waits are bounded: a wait that gives up records an error (cq_device_error)
-// and the block returns without writing.
+// Every rank owns one region of device memory (cq_peer_region_alloc) that
+// every other rank maps through CUDA IPC (cq_peer_region_open, in the mapping
+// process's own device context):
+//   [flags: u32 per (row, source rank), kMaxRows x kMaxRanks]
+//   [parts: parity (2) x source rank x rows x dim]
+// For call e, block b of rank s pushes row b of its part (the projection's
+// output, local memory) into slot s of every rank's region (NVLink stores),
+// then stores e into flag (b, s) of every region (release, system scope).
+// Block b of every rank waits until flags (b, 0..world-1) of its own region
+// hold e or more (acquire), sums the slots of row b in rank order from local
+// memory, and writes x and y.  Two part buffers alternate by call (parity): a
+// rank writes a peer's buffer p again only two calls later, after the peer
+// has flagged the call in between, which it does only after its reads of
+// buffer p have finished (stream order).  e is a device counter advanced by
+// the last block, so a captured graph replays with fresh epochs.  Waits are
+// bounded: a wait that gives up records an error (cq_device_error 9) and the
+// block writes nothing.
+#include <cstring>
+#include <string>
+
 #include "cq_common.cuh"
 
 namespace cq {
 namespace peer {
 
 constexpr int kMaxRanks = 8;
-constexpr int kFlagBytes = 256;
+constexpr int kMaxRows = 64;
+constexpr int kFlagBytes = kMaxRows * kMaxRanks * 4;
 constexpr int kThreads = 256;
 constexpr long long kSpinLimit = 1LL << 25;  // polls of 64 ns sleep: seconds, then give up
 constexpr int ERR_PEER_WAIT = 9;
@@ -76,9 +84,9 @@ __device__ __forceinline__ uint4 pack8(const float (&v)[8], int dt) {
 }
 
 // one block per row
-__global__ void __launch_bounds__(kThreads) sum_norm_kernel(Regions R, int world, int rank, int64_t part_off,
-                                                            int dim, void *x, const void *w, float eps, void *y,
-                                                            int64_t *ctr, int dt) {
+__global__ void __launch_bounds__(kThreads) sum_norm_kernel(Regions R, int world, int rank, int parity,
+                                                            int64_t part_bytes, int dim, const void *part, void *x,
+                                                            const void *w, float eps, void *y, int64_t *ctr, int dt) {
   __shared__ uint32_t s_e;
   __shared__ int s_ok;
   __shared__ float red[kThreads / 32];
@@ -86,15 +94,22 @@ __global__ void __launch_bounds__(kThreads) sum_norm_kernel(Regions R, int world
     s_e = (uint32_t)(*(volatile int64_t *)ctr + 1);
     s_ok = 1;
   }
+  const int64_t row = blockIdx.x;
+  const int n8 = dim / 8;
+  // push this rank's row into slot `rank` of every region (parity buffer)
+  const int64_t slot_off = kFlagBytes + ((int64_t)parity * world + rank) * part_bytes;
+  const uint4 *src = reinterpret_cast<const uint4 *>(part) + row * n8;
+  for (int c = threadIdx.x; c < n8; c += kThreads) {
+    const uint4 v = src[c];
+    for (int r = 0; r < world; ++r) reinterpret_cast<uint4 *>(R.r[r] + slot_off)[row * n8 + c] = v;
+  }
   __syncthreads();
   const uint32_t e = s_e;
-  if (blockIdx.x == 0 && threadIdx.x < world) {
-    // this rank's part of call e is complete (written before this kernel began): tell every rank
+  if (threadIdx.x < world) {  // row `row` of this rank's part is in every region: flag it there
     asm volatile("fence.acq_rel.sys;" ::: "memory");
-    st_release_sys(reinterpret_cast<uint32_t *>(R.r[threadIdx.x]) + rank, e);
-  }
-  if (threadIdx.x < world && threadIdx.x != rank) {
-    const uint32_t *f = reinterpret_cast<const uint32_t *>(R.r[rank]) + threadIdx.x;
+    st_release_sys(reinterpret_cast<uint32_t *>(R.r[threadIdx.x]) + row * kMaxRanks + rank, e);
+    // wait for the row from source rank threadIdx.x in this rank's region
+    const uint32_t *f = reinterpret_cast<const uint32_t *>(R.r[rank]) + row * kMaxRanks + threadIdx.x;
     long long it = 0;
     while ((int32_t)(ld_acquire_sys(f) - e) < 0) {
       if (++it > kSpinLimit) {
@@ -106,17 +121,15 @@ __global__ void __launch_bounds__(kThreads) sum_norm_kernel(Regions R, int world
     }
   }
   __syncthreads();
-  const int64_t row = blockIdx.x;
-  const int n8 = dim / 8;
   if (s_ok) {
     float ss = 0.f;
     uint4 *xv = reinterpret_cast<uint4 *>(x) + row * n8;
+    const char *mine = R.r[rank] + kFlagBytes + (int64_t)parity * world * part_bytes;
     for (int c = threadIdx.x; c < n8; c += kThreads) {
       float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
       for (int r = 0; r < world; ++r) {  // rank order: the same sum on every rank
-        const uint4 *src = reinterpret_cast<const uint4 *>(R.r[r] + part_off) + row * n8 + c;
         float v[8];
-        unpack8(__ldcv(src), dt, v);
+        unpack8(__ldcg(reinterpret_cast<const uint4 *>(mine + r * part_bytes) + row * n8 + c), dt, v);
 #pragma unroll
         for (int k = 0; k < 8; ++k) acc[k] += v[k];
       }
@@ -124,8 +137,8 @@ __global__ void __launch_bounds__(kThreads) sum_norm_kernel(Regions R, int world
       unpack8(xv[c], dt, xo);
 #pragma unroll
       for (int k = 0; k < 8; ++k) {
-        const float s = round_dt(acc[k], dt);  // the all-reduced part, in the dtype
-        xo[k] = round_dt(xo[k] + s, dt);       // x + part (one rounding)
+        const float sm = round_dt(acc[k], dt);  // the summed part, in the dtype
+        xo[k] = round_dt(xo[k] + sm, dt);       // x + part (one rounding)
         ss = fmaf(xo[k], xo[k], ss);
       }
       xv[c] = pack8(xo, dt);
@@ -178,31 +191,67 @@ int read_peer_error(int clear) {
 
 using namespace cq;
 
-extern "C" int cq_peer_sum_norm(const uint64_t *regions, int32_t world, int32_t rank, int32_t parity,
-                                int64_t part_bytes, int64_t rows, int32_t dim, void *x, const void *w, float eps,
-                                void *y, int64_t *counter, int dtype, void *stream) {
-  CQ_REQUIRE(regions && x && w && y && counter, CQ_ERR_INVALID, "cq_peer_sum_norm: null pointer");
+static int64_t part_bytes_of(int64_t rows, int32_t dim) { return (rows * dim * 2 + 15) / 16 * 16; }
+
+extern "C" int64_t cq_peer_region_bytes(int64_t max_rows, int32_t dim, int32_t world) {
+  if (max_rows < 1 || max_rows > peer::kMaxRows || dim < 8 || world < 1 || world > peer::kMaxRanks) return 0;
+  return peer::kFlagBytes + 2LL * world * part_bytes_of(max_rows, dim);
+}
+
+extern "C" int cq_peer_region_alloc(int64_t bytes, void **ptr, void *ipc_handle) {
+  CQ_REQUIRE(ptr && ipc_handle && bytes > 0, CQ_ERR_INVALID, "cq_peer_region_alloc: bad arguments");
+  *ptr = nullptr;
+  void *p = nullptr;
+  if (cudaMalloc(&p, (size_t)bytes) != cudaSuccess) return set_error(CQ_ERR_CUDA, "cq_peer_region_alloc: cudaMalloc");
+  cudaIpcMemHandle_t h;
+  if (cudaMemset(p, 0, (size_t)bytes) != cudaSuccess || cudaDeviceSynchronize() != cudaSuccess ||
+      cudaIpcGetMemHandle(&h, p) != cudaSuccess) {
+    cudaFree(p);
+    return set_error(CQ_ERR_CUDA, "cq_peer_region_alloc: zero fill or IPC handle");
+  }
+  std::memcpy(ipc_handle, &h, sizeof(h));
+  *ptr = p;
+  return CQ_OK;
+}
+
+extern "C" int cq_peer_region_open(const void *ipc_handle, void **ptr) {
+  CQ_REQUIRE(ptr && ipc_handle, CQ_ERR_INVALID, "cq_peer_region_open: bad arguments");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, ipc_handle, sizeof(h));
+  // mapped into the calling thread's current device context, with peer access to the owner
+  const cudaError_t e = cudaIpcOpenMemHandle(ptr, h, cudaIpcMemLazyEnablePeerAccess);
+  if (e != cudaSuccess) return set_error(CQ_ERR_CUDA, std::string("cq_peer_region_open: ") + cudaGetErrorString(e));
+  return CQ_OK;
+}
+
+extern "C" int cq_peer_region_close(void *ptr) {
+  if (ptr && cudaIpcCloseMemHandle(ptr) != cudaSuccess) return set_error(CQ_ERR_CUDA, "cq_peer_region_close");
+  return CQ_OK;
+}
+
+extern "C" int cq_peer_region_free(void *ptr) {
+  if (ptr && cudaFree(ptr) != cudaSuccess) return set_error(CQ_ERR_CUDA, "cq_peer_region_free");
+  return CQ_OK;
+}
+
+extern "C" int cq_peer_sum_norm(const uint64_t *regions, int32_t world, int32_t rank, int32_t parity, int64_t max_rows,
+                                int64_t rows, int32_t dim, const void *part, void *x, const void *w, float eps, void *y,
+                                int64_t *counter, int dtype, void *stream) {
+  CQ_REQUIRE(regions && part && x && w && y && counter, CQ_ERR_INVALID, "cq_peer_sum_norm: null pointer");
   CQ_REQUIRE(world >= 1 && world <= peer::kMaxRanks && rank >= 0 && rank < world, CQ_ERR_INVALID,
              "cq_peer_sum_norm: need 1 <= world <= 8 and 0 <= rank < world");
   CQ_REQUIRE(parity == 0 || parity == 1, CQ_ERR_INVALID, "cq_peer_sum_norm: parity must be 0 or 1");
   CQ_REQUIRE(dtype == CQ_BF16 || dtype == CQ_F16, CQ_ERR_UNSUPPORTED, "cq_peer_sum_norm: dtype must be bf16 or f16");
-  CQ_REQUIRE(dim > 0 && dim % 8 == 0 && rows > 0 && rows < (1LL << 31), CQ_ERR_INVALID,
-             "cq_peer_sum_norm: dim must be a positive multiple of 8, rows in [1, 2^31)");
-  CQ_REQUIRE(rows * dim * 2 <= part_bytes && part_bytes % 16 == 0, CQ_ERR_INVALID,
-             "cq_peer_sum_norm: a part (rows x dim) exceeds the region's part buffer");
+  CQ_REQUIRE(dim >= 8 && dim % 8 == 0 && rows >= 1 && rows <= max_rows && max_rows <= peer::kMaxRows, CQ_ERR_INVALID,
+             "cq_peer_sum_norm: dim must be a positive multiple of 8 and 1 <= rows <= max_rows <= 64");
   peer::Regions R{};
   for (int i = 0; i < world; ++i) {
     R.r[i] = reinterpret_cast<char *>(regions[i]);
     CQ_REQUIRE(R.r[i] && (regions[i] & 15) == 0, CQ_ERR_INVALID, "cq_peer_sum_norm: regions must be 16-byte aligned");
   }
-  CQ_REQUIRE((((uintptr_t)x | (uintptr_t)w | (uintptr_t)y) & 15) == 0, CQ_ERR_INVALID,
-             "cq_peer_sum_norm: x, w and y must be 16-byte aligned");
-  const int64_t off = peer::kFlagBytes + (int64_t)parity * part_bytes;
-  peer::sum_norm_kernel<<<(unsigned)rows, peer::kThreads, 0, (cudaStream_t)stream>>>(R, world, rank, off, dim, x, w,
-                                                                                     eps, y, counter, dtype);
+  CQ_REQUIRE((((uintptr_t)part | (uintptr_t)x | (uintptr_t)w | (uintptr_t)y) & 15) == 0, CQ_ERR_INVALID,
+             "cq_peer_sum_norm: part, x, w and y must be 16-byte aligned");
+  peer::sum_norm_kernel<<<(unsigned)rows, peer::kThreads, 0, (cudaStream_t)stream>>>(
+      R, world, rank, parity, part_bytes_of(max_rows, dim), dim, part, x, w, eps, y, counter, dtype);
   return check_launch("cq_peer_sum_norm");
-}
-
-extern "C" int64_t cq_peer_region_bytes(int64_t part_bytes) {
-  return part_bytes <= 0 ? 0 : peer::kFlagBytes + 2 * ((part_bytes + 15) / 16 * 16);
 }

@@ -185,7 +185,7 @@ class Qwen3StyleDecoder:
         self.peer = None
         if self.world > 1 and peer_sum:
             from .peer import PeerSumNorm
-            self.peer = PeerSumNorm(tp_group, batch, c.hidden, dtype=dtype, device=self.device)
+            self.peer = PeerSumNorm(tp_group, batch, c.hidden, device=self.device)
 
     # -- context ---------------------------------------------------------------
     def fill_context(self, T0: int, chunk: int = 4096, seed: int = 1) -> None:
@@ -292,12 +292,11 @@ class Qwen3StyleDecoder:
     def _project_sum_norm(self, x: torch.Tensor, a: torch.Tensor, wt: torch.Tensor, w_norm: torch.Tensor,
                           parity: int) -> torch.Tensor:
         """x <- x + (sum over the tensor-parallel ranks of a @ wt.T); returns
-        RMSNorm(x) * w_norm.  With peer sums: the GEMM writes this rank's part
-        into its peer region and one kernel does the sum, the add and the norm."""
+        RMSNorm(x) * w_norm.  With peer sums one kernel pushes this rank's part
+        to every rank and does the sum, the add and the norm."""
         if self.peer is not None:
-            torch.matmul(a, wt.t(), out=self.peer.part(parity))
             y = torch.empty_like(x)
-            self.peer(x, w_norm, self.cfg.eps, y, parity)
+            self.peer(a @ wt.t(), x, w_norm, self.cfg.eps, y, parity)
             return y
         x += self._reduce(a @ wt.t())
         return self._norm(x, w_norm)
@@ -381,6 +380,13 @@ class Qwen3StyleDecoder:
             for L in self.layers:
                 L["cache"].offset += steps
         return self.logits
+
+    def close(self) -> None:
+        """Release the peer-memory regions (collective over the tensor-parallel
+        group; after the graphs are gone, before the process group)."""
+        if self.peer is not None:
+            self.peer.close()
+            self.peer = None
 
     def bytes_per_step(self) -> int:
         """Algorithmic HBM bytes of one step: every weight once, every layer's

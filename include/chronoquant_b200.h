@@ -145,22 +145,28 @@ int cq_device_error(int *code, int clear);
 
 /* Row-parallel sum over NVLink peer memory, fused with the residual add and
  * RMSNorm that follow it in a tensor-parallel decode step (no reference
- * counterpart: the reference runs on one device).  Every rank owns a region of
- * cq_peer_region_bytes(part_bytes) zero-filled bytes that every rank has
- * mapped (CUDA IPC): [64 u32 flags][part buffer 0][part buffer 1].  Before
- * the call, this rank's part [rows][dim] (dtype) is in part buffer `parity`
- * of its own region; calls alternate parity.  regions: host array of the
- * world regions' device addresses in rank order.  The kernel signals the
- * other ranks, waits (bounded; error 9 in cq_device_error when it gives up)
- * for theirs, and computes x <- x + dtype(sum over ranks in rank order of the
- * parts), y <- dtype(x * rsqrt(mean(x^2) + eps)) * w per row.  counter:
- * device int64[2], zero at the first call, shared by the calls of one region
- * set (a captured graph replays with fresh epochs).  Every rank makes the
- * same calls in the same order. */
-int cq_peer_sum_norm(const uint64_t *regions, int32_t world, int32_t rank, int32_t parity, int64_t part_bytes,
-                     int64_t rows, int32_t dim, void *x, const void *w, float eps, void *y, int64_t *counter,
-                     int dtype, void *stream);
-int64_t cq_peer_region_bytes(int64_t part_bytes);
+ * counterpart: the reference runs on one device).  Every rank allocates a
+ * region of cq_peer_region_bytes(max_rows, dim, world) bytes with
+ * cq_peer_region_alloc (zero-filled; its CUDA IPC handle, 64 bytes, goes to
+ * the other ranks), and maps every other rank's region with
+ * cq_peer_region_open, called with its own device current.  regions: host
+ * array of the world regions' addresses as this rank sees them, in rank
+ * order.  cq_peer_sum_norm pushes this rank's part [rows][dim] (local device
+ * memory, dtype bf16 or f16) into every region, flags it, waits (bounded;
+ * error 9 in cq_device_error when it gives up, rows unwritten) for every
+ * rank's part, and computes per row x <- x + dtype(sum of the parts in rank
+ * order), y <- dtype(x * rsqrt(mean(x^2) + eps)) * w.  parity alternates
+ * between consecutive calls; counter: device int64[2], zero before the first
+ * call of a region set.  Every rank makes the same calls in the same order;
+ * rows <= max_rows <= 64, dim a multiple of 8, all pointers 16-byte aligned. */
+int64_t cq_peer_region_bytes(int64_t max_rows, int32_t dim, int32_t world);
+int cq_peer_region_alloc(int64_t bytes, void **ptr, void *ipc_handle);
+int cq_peer_region_open(const void *ipc_handle, void **ptr);
+int cq_peer_region_close(void *ptr);
+int cq_peer_region_free(void *ptr);
+int cq_peer_sum_norm(const uint64_t *regions, int32_t world, int32_t rank, int32_t parity, int64_t max_rows,
+                     int64_t rows, int32_t dim, const void *part, void *x, const void *w, float eps, void *y,
+                     int64_t *counter, int dtype, void *stream);
 
 /* Encode S new tokens at absolute positions t0..t0+S-1 for K and V in one
  * launch (cache.py:87-129, codec.py:23-65).  keys/values: [batch][kv_heads]

@@ -135,6 +135,7 @@ def tp_decoder_worker(rank, world, port, steps, queue):
                 rels.append(float((lt - lo).norm() / lo.norm()))
         torch.cuda.synchronize()
         del tp.graph  # graphs holding NCCL work go before the process group
+        tp.close()
         if one is not None:
             del one.graph
         dist.barrier()
@@ -179,6 +180,7 @@ def seq_decoder_worker(rank, world, port, steps, queue):
         torch.cuda.synchronize()
         lens = [int(L["len"][0]) for L in sp.layers]
         del sp.graph  # graphs holding NCCL work go before the process group
+        sp.close()
         if one is not None:
             del one.graph
         dist.barrier()
@@ -225,6 +227,7 @@ def mesh_decoder_worker(rank, world, port, n_seq, steps, queue):
         torch.cuda.synchronize()
         lens = [int(L["len"][0]) for L in m.layers]
         del m.graph  # graphs holding NCCL work go before the process group
+        m.close()
         if one is not None:
             del one.graph
         dist.barrier()
@@ -272,7 +275,7 @@ def peer_sum_worker(rank, world, port, rows, dim, queue):
                                 device_id=dev)
         from chronoquant_mlx_b200.peer import PeerSumNorm
         from chronoquant_mlx_b200.decoder import _rmsnorm
-        ps = PeerSumNorm(dist.group.WORLD, rows, dim, dtype=torch.bfloat16, device=dev)
+        ps = PeerSumNorm(dist.group.WORLD, rows, dim, device=dev)
         g = torch.Generator(device=dev).manual_seed(100 + rank)
         w = (1.0 + 0.1 * torch.randn(dim, generator=g, device=dev)).to(torch.bfloat16)
         dist.broadcast(w, 0)
@@ -288,47 +291,47 @@ def peer_sum_worker(rank, world, port, rows, dim, queue):
             return xe, _rmsnorm(xe, w, eps)
 
         def ulps(a, b):
-            ia = a.view(torch.int16).int()
-            ib = b.view(torch.int16).int()
-            return int((ia - ib).abs().max())
+            return int((a.view(torch.int16).int() - b.view(torch.int16).int()).abs().max())
+
+        def rand_part(k):
+            return (torch.randn((rows, dim), generator=g, device=dev) * (k + 1)).to(torch.bfloat16)
 
         worst = [0, 0]
         x = torch.randn((rows, dim), generator=g, device=dev).to(torch.bfloat16)
         y = torch.empty_like(x)
         for k in range(6):  # eager calls, alternating parity
-            part = ps.part(k & 1)
-            part.copy_(torch.randn((rows, dim), generator=g, device=dev) * (k + 1))
+            part = rand_part(k)
             xe, ye = expected(x, part)
-            ps(x, w, eps, y, k & 1)
+            ps(part, x, w, eps, y, k & 1)
             torch.cuda.synchronize()
             worst[0] = max(worst[0], ulps(x, xe))
             worst[1] = max(worst[1], ulps(y, ye))
         # four calls in a graph: each replay sums the parts written before it
+        parts = [rand_part(k) for k in range(4)]
         xs = [x.clone() for _ in range(4)]
         ys = [torch.empty_like(x) for _ in range(4)]
-        graph = torch.cuda.CUDAGraph()
         torch.cuda.synchronize()
+        graph = torch.cuda.CUDAGraph()
         with torch.cuda.graph(graph):
             for k in range(4):
-                ps(xs[k], w, eps, ys[k], k & 1)
+                ps(parts[k], xs[k], w, eps, ys[k], k & 1)
         for rep in range(3):
+            dist.barrier()
             x0 = [t.clone() for t in xs]
-            # parts of calls 0, 1 are in buffers 0, 1; calls 2, 3 reuse them, so this rank writes
-            # equal parts for calls k and k + 2 and the expectation follows
-            p01 = [torch.randn((rows, dim), generator=g, device=dev).to(torch.bfloat16) for _ in range(2)]
-            for k in range(2):
-                ps.part(k).copy_(p01[k])
+            for k in range(4):
+                parts[k].copy_(rand_part(k))
+            torch.cuda.synchronize()
             graph.replay()
             torch.cuda.synchronize()
             for k in range(4):
-                xe, ye = expected(x0[k], p01[k & 1])
+                xe, ye = expected(x0[k], parts[k])
                 worst[0] = max(worst[0], ulps(xs[k], xe))
                 worst[1] = max(worst[1], ulps(ys[k], ye))
-            dist.barrier()
         c = ctypes.c_int(0)
         from chronoquant_mlx_b200 import _lib
         _lib.lib().cq_device_error(ctypes.byref(c), 1)
         del graph
+        ps.close()
         dist.barrier()
         dist.destroy_process_group()
         queue.put((rank, worst, c.value, None))
@@ -350,17 +353,17 @@ def peer_timeout_worker(rank, world, port, queue):
                                 device_id=dev)
         from chronoquant_mlx_b200 import _lib
         from chronoquant_mlx_b200.peer import PeerSumNorm
-        ps = PeerSumNorm(dist.group.WORLD, 2, 256, dtype=torch.bfloat16, device=dev)
+        ps = PeerSumNorm(dist.group.WORLD, 2, 256, device=dev)
         code = None
         if rank == 0:
             x = torch.zeros((2, 256), dtype=torch.bfloat16, device=dev)
             w = torch.ones(256, dtype=torch.bfloat16, device=dev)
             y = torch.full_like(x, 7.0)
-            ps(x, w, 1e-6, y, 0)
+            ps(torch.ones_like(x), x, w, 1e-6, y, 0)
             c = ctypes.c_int(0)
             _lib.lib().cq_device_error(ctypes.byref(c), 1)  # synchronises: the kernel has given up
             code = (c.value, bool(torch.all(y == 7.0)))
-        dist.barrier()
+        dist.barrier()  # rank 1 keeps its region mapped until rank 0's kernel has given up
         dist.destroy_process_group()
         queue.put((rank, code, None))
     except Exception as e:
