@@ -34,7 +34,8 @@ constexpr int kMaxRanks = 8;
 constexpr int kMaxRows = 64;
 constexpr int kFlagBytes = kMaxRows * kMaxRanks * 4;
 constexpr int kThreads = 256;
-constexpr long long kSpinLimit = 1LL << 25;  // polls of 64 ns sleep: seconds, then give up
+constexpr long long kSpinLimit = 1LL << 25;  // polls before giving up (seconds: the later ones sleep)
+constexpr long long kBusyPolls = 1LL << 14;  // polls without sleeping: a peer a few ms late costs no sleep overshoot
 constexpr int ERR_PEER_WAIT = 9;
 
 __device__ int g_peer_error;
@@ -117,7 +118,7 @@ __global__ void __launch_bounds__(kThreads) sum_norm_kernel(Regions R, int world
         s_ok = 0;
         break;
       }
-      __nanosleep(64);
+      if (it > kBusyPolls) __nanosleep(128);
     }
   }
   __syncthreads();

@@ -3,8 +3,9 @@ peer memory fused with the residual add and RMSNorm (csrc/cq_peer.cu).
 
 On two GPUs: x must equal, bit for bit, the torch restatement (every rank's
 part gathered, summed in fp32 in rank order, rounded to bf16, added to x with
-one rounding); y within one bf16 ulp of the torch RMSNorm expression (the
-fp32 sum of squares is reduced in another order).  Eager calls alternate the
+one rounding); y within two bf16 ulps of the torch RMSNorm expression (the
+fp32 sum of squares is reduced in another order, which can move the rounded
+x * rsqrt(...) by one ulp, and the product with w rounds once more).  Eager calls alternate the
 part buffers; a captured graph of four calls replays with new parts.  A
 second case leaves one rank out: the other's bounded wait gives up and
 cq_device_error reports 9 without the output being written."""
@@ -48,7 +49,7 @@ def test_peer_sum_norm_matches_torch(rows, dim):
     for rank, worst, code, err in res:
         assert err is None, err
         assert worst[0] == 0, worst  # x: bit-exact
-        assert worst[1] <= 1, worst  # y: within one ulp
+        assert worst[1] <= 2, worst  # y: within two ulps
         assert code == 0
 
 
