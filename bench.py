@@ -1075,19 +1075,19 @@ def run_codec(args, cfg):
     stream = torch.cuda.current_stream()
     flush = torch.empty(256 << 20, dtype=torch.uint8, device=device)
 
-    def timed_steps(n, before=None, after=None):
+    def timed_steps(n, inputs_in=None, output_out=None):
+        """n steps, each after an L2 flush and timed alone; inputs_in /
+        output_out (host copies) run inside each step's events."""
         ms = []
         for _ in range(n):
             flush.fill_(1)
-            if before:
-                before()
             e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             e0.record(stream)
-            if before is not None:
-                before(True)
+            if inputs_in is not None:
+                inputs_in()
             graph.replay()
-            if after is not None:
-                after()
+            if output_out is not None:
+                output_out()
             e1.record(stream)
             ms.append((e0, e1))
         torch.cuda.synchronize()
@@ -1132,16 +1132,15 @@ def run_codec(args, cfg):
     hq = torch.from_numpy(q_host).pin_memory()
     hout = torch.empty(out.shape, dtype=out.dtype).pin_memory()
 
-    def h2d(_inside=False):
-        if _inside:
-            k_dev.copy_(hk, non_blocking=True)
-            v_dev.copy_(hv, non_blocking=True)
-            q_dev.copy_(hq, non_blocking=True)
+    def h2d():
+        k_dev.copy_(hk, non_blocking=True)
+        v_dev.copy_(hv, non_blocking=True)
+        q_dev.copy_(hq, non_blocking=True)
 
     def d2h():
         hout.copy_(out, non_blocking=True)
 
-    e_ms = timed_steps(args.steps, before=h2d, after=d2h)
+    e_ms = timed_steps(args.steps, inputs_in=h2d, output_out=d2h)
     e_tot = sum(e_ms)
     if world > 1:
         tt = torch.tensor([e_tot], device=device)
