@@ -1378,8 +1378,10 @@ int run_fast_decode(const cq_paged_cache &c, const CacheView &cv, int64_t T, con
   p.lse_out = lse_out;
 
   static std::mutex mu;
-  static bool attr_set[64][16] = {};
+  constexpr int kGeoSlots = 32;  // >= the entries of find_geo's table
+  static bool attr_set[64][kGeoSlots] = {};
   const int v = L.gi;
+  CQ_REQUIRE(v >= 0 && v < kGeoSlots, CQ_ERR_INVALID, "decode_kernel: geometry index out of range");
   {
     int dev = 0;
     cudaGetDevice(&dev);
